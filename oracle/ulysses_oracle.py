@@ -1,0 +1,189 @@
+"""CPU restatement of cozy-runtime's Ulysses context-parallel attention (TEST INFRASTRUCTURE ONLY).
+
+Only `tests/`, `__graft_entry__.smoke()` and `bench.py`'s CPU legs use this module, and only as
+the checker. Each function cites the reference lines it restates; paths are relative to the
+cozy-runtime project root. All arithmetic is torch on CPU in fp32 or fp64.
+"""
+
+from __future__ import annotations
+
+import math
+from collections.abc import Callable, Sequence
+
+import torch
+from torch import Tensor
+
+E4M3_MAX = 448.0
+#: attention_fp8.py:33-38: the value a head's amax maps onto, and the descale floor
+E4M3_TARGET = 440.0
+SCALE_FLOOR = 1e-12
+
+
+def sequence_rows(total: int, world: int) -> list[int]:
+    """Rows each rank holds: `torch.tensor_split` along the sequence, the first `total % world`
+    ranks one row longer (src/cozy_runtime/internal/parallel/cp.py:166-174, Diffusers'
+    `ulysses_anything=True`)."""
+    base, extra = divmod(total, world)
+    return [base + (1 if rank < extra else 0) for rank in range(world)]
+
+
+def heads_padded(heads: int, world: int) -> int:
+    """Heads rounded up to a multiple of the degree with zero heads
+    (src/cozy_runtime/internal/parallel/ulysses.py:647)."""
+    return heads + (-heads % world)
+
+
+def owned_heads(heads: int, world: int, rank: int) -> range:
+    """The query heads rank `rank` attends over: block `rank` of `padded/world` heads
+    (ulysses.py:325-362 `_pack`, peer p takes heads `start + p*local ...`), less the padding."""
+    local = heads_padded(heads, world) // world
+    return range(min(rank * local, heads), min((rank + 1) * local, heads))
+
+
+def attention_fp32(
+    q: Tensor,
+    k: Tensor,
+    v: Tensor,
+    *,
+    causal: bool = False,
+    scale: float | None = None,
+    dtype: torch.dtype = torch.float32,
+) -> Tensor:
+    """softmax(Q Kᵀ·scale) V over [batch, seq, heads, dim], computed in `dtype` per head.
+
+    Restates src/cozy_runtime/internal/attention_upstream.py:109-147 (`sdpa`): torch SDPA on the
+    transposed operands, causal aligned bottom-right when the query and key lengths differ
+    (:106-107, :136-139). Grouped-query attention maps query head h to key head
+    h // (Hq / Hkv), torch's `enable_gqa` rule. Returns `dtype`.
+    """
+    batch, sq, hq, dim = q.shape
+    sk, hkv = k.shape[1], k.shape[2]
+    if hq % hkv:
+        raise ValueError("query heads must be a multiple of key heads")
+    group = hq // hkv
+    scale = 1.0 / math.sqrt(dim) if scale is None else scale
+    out = torch.empty(batch, sq, hq, dim, dtype=dtype)
+    mask = None
+    if causal:
+        rows = torch.arange(sq)[:, None] + (sk - sq)
+        mask = torch.arange(sk)[None, :] > rows
+    for b in range(batch):
+        for h in range(hq):
+            qh = q[b, :, h].to(dtype)
+            kh = k[b, :, h // group].to(dtype)
+            vh = v[b, :, h // group].to(dtype)
+            s = (qh @ kh.T) * scale
+            if mask is not None:
+                s = s.masked_fill(mask, float("-inf"))
+            p = torch.softmax(s, dim=-1)
+            out[b, :, h] = p @ vh
+    return out
+
+
+def exchange(
+    queries: Sequence[Tensor],
+    keys: Sequence[Tensor],
+    values: Sequence[Tensor],
+    compute: Callable[[Tensor, Tensor, Tensor], Tensor],
+) -> list[Tensor]:
+    """The whole Ulysses exchange of W ranks, simulated in one process.
+
+    `queries[r]` is rank r's [B, S_r, Hq, D] rows (likewise keys/values with Hkv heads). Restates
+    src/cozy_runtime/internal/parallel/ulysses.py:633-766 (`_exchange`): heads padded to a
+    multiple of W (:647) with zero heads (`_pack`, :335-340), rank p attending over heads
+    `[p·local, (p+1)·local)` of the whole sequence (rows stacked in rank order, `_unpack`
+    :420-432), `compute` on [B, S, local, D], the attended rows returned to their owners
+    (`_land`, :435-457) and the padding cropped (:766). Grouped K/V heads (Hkv < Hq) cross as
+    the query heads they serve, which is the reference's exchange after K/V replication.
+    Returns each rank's [B, S_r, Hq, D] output.
+    """
+    world = len(queries)
+    rows = [int(t.shape[1]) for t in queries]
+    heads = int(queries[0].shape[2])
+    hkv = int(keys[0].shape[2])
+    group = heads // hkv
+    q = torch.cat(list(queries), dim=1)
+    k = torch.cat(list(keys), dim=1).repeat_interleave(group, dim=2)
+    v = torch.cat(list(values), dim=1).repeat_interleave(group, dim=2)
+    padded = heads_padded(heads, world)
+    if padded != heads:
+        pad = (0, 0, 0, padded - heads)
+        q, k, v = (torch.nn.functional.pad(t, pad) for t in (q, k, v))
+    local = padded // world
+    attended = []
+    for rank in range(world):
+        part = slice(rank * local, (rank + 1) * local)
+        attended.append(compute(q[:, :, part], k[:, :, part], v[:, :, part]))
+    whole = torch.cat(attended, dim=2)[:, :, :heads]
+    starts = [sum(rows[:r]) for r in range(world)]
+    return [whole[:, s : s + n] for s, n in zip(starts, rows, strict=True)]
+
+
+def head_norm_rope(
+    x: Tensor,
+    cos: Tensor,
+    sin: Tensor,
+    *,
+    rotary: int,
+    interleaved: bool,
+    normalize: bool = True,
+    weight: Tensor | None = None,
+    offset: float = 0.0,
+    eps: float = 1e-6,
+    stride_channel: int = 1,
+) -> Tensor:
+    """Per-head RMSNorm (optional weight + offset), then RoPE on the first `rotary` channels.
+
+    x: [B, S, H, D]; cos/sin: per token, `[S, C]` fp32 with column `col` of channel j read at
+    `col * stride_channel` (the reference's `rope_tables` layout,
+    src/cozy_runtime/accel/fusion/_kernels.py:497-517). Interleaved pairs channel 2i with 2i+1
+    (table column i); split-half pairs j with j ± rotary/2 (column j). The law is the reference's
+    own checker, src/cozy_runtime/internal/bench/kernels.py:819-850, of the fused kernel
+    `head_norm_rope_kernel` (_kernels.py:177-240). Computed in fp64, returned fp64.
+    """
+    y = x.double()
+    if normalize:
+        y = y * torch.rsqrt(y.pow(2).mean(-1, keepdim=True) + eps)
+        if weight is not None:
+            y = y * (weight.double() + offset)
+    out = y.clone()
+    c, s = cos.double(), sin.double()
+    for j in range(rotary):
+        if interleaved:
+            low, partner, col = j % 2 == 0, j ^ 1, j // 2
+        else:
+            half = rotary // 2
+            low, partner, col = j < half, (j + half if j < half else j - half), j
+        paired = -y[..., partner] if low else y[..., partner]
+        cc = c[:, col * stride_channel][None, :, None]
+        ss = s[:, col * stride_channel][None, :, None]
+        out[..., j] = y[..., j] * cc + paired * ss
+    return out
+
+
+def quantise_e4m3_per_head(x: Tensor) -> tuple[Tensor, Tensor]:
+    """Per-(batch, head) e4m3: descale = max(amax/440, 1e-12), x/descale clamped to ±448, cast
+    round-to-nearest-even. Restates src/cozy_runtime/internal/attention_fp8.py:162-169
+    (`quantise_eager`). x: [B, S, H, D]; returns (e4m3 codes, [B, H] fp32 descale)."""
+    amax = x.abs().amax(dim=(1, 3)).float()
+    descale = (amax / E4M3_TARGET).clamp_(min=SCALE_FLOOR)
+    scaled = (x.float() / descale[:, None, :, None]).clamp_(-E4M3_MAX, E4M3_MAX)
+    return scaled.to(torch.float8_e4m3fn), descale.contiguous()
+
+
+def quantise_fp8_blocks(x: Tensor, block: int = 64) -> tuple[Tensor, Tensor]:
+    """e4m3 with one fp32 descale per `block` tokens × head: descale = max(amax/448, 1e-12) of the
+    block, codes = RTNE(x/descale) clamped to ±448. This is the block form of the per-head law
+    above (attention_fp8.py:162-169) at the granularity the FP8 video configuration names; a
+    block covering the whole sequence with target 440 is that law exactly. x: [B, S, H, D];
+    returns (codes [B, S, H, D], descale [B, ceil(S/block), H])."""
+    batch, seq, heads, dim = x.shape
+    blocks = -(-seq // block)
+    pad = blocks * block - seq
+    xf = torch.nn.functional.pad(x.float(), (0, 0, 0, 0, 0, pad))
+    tiles = xf.view(batch, blocks, block, heads, dim)
+    amax = tiles.abs().amax(dim=(2, 4))
+    descale = (amax / E4M3_MAX).clamp_(min=SCALE_FLOOR)
+    scaled = (tiles / descale[:, :, None, :, None]).clamp_(-E4M3_MAX, E4M3_MAX)
+    codes = scaled.to(torch.float8_e4m3fn).view(batch, blocks * block, heads, dim)[:, :seq]
+    return codes, descale

@@ -1,0 +1,221 @@
+"""Generate the golden vectors under tests/golden/ by running the REFERENCE's own code.
+
+Test infrastructure only: this script imports cozy-runtime from a local checkout of the
+reference (default `/root/reference/src`, or `$COZY_REFERENCE_SRC`) and is run by hand in a
+container that has it. Nothing else in this repository imports it; the GPU box never runs it.
+
+What it records, each as an `.npz` in this directory:
+
+* ``ulysses_*.npz``: the reference's Ulysses exchange
+  (`src/cozy_runtime/internal/parallel/ulysses.py:607` `exchange`) run over a gloo process group
+  of W CPU processes, with `compute` = the reference's local kernel
+  (`src/cozy_runtime/internal/attention_upstream.py:109` `sdpa`). Inputs are split along the
+  sequence with `torch.tensor_split` (Diffusers' `ulysses_anything` split,
+  `src/cozy_runtime/internal/parallel/cp.py:166-174`), the rank outputs are concatenated back in
+  rank order. The causal-GQA case replicates K/V heads to the query heads first and passes
+  `is_causal=True` to `sdpa`, as the exchange itself is mask-agnostic.
+* ``rope_*.npz``: the reference's own eager RMSNorm+RoPE law, the checker inside
+  `src/cozy_runtime/internal/bench/kernels.py:819` `_fused_rope`, executed with the Triton
+  launch replaced by a recorder, so the recorded `want` is the reference code's output.
+* ``fp8_quantise.npz``: `src/cozy_runtime/internal/attention_fp8.py:162` `quantise_eager`.
+
+Run:  python tests/golden/make_golden.py
+Third-party pins the reference declares but this container lacks (`tensorfs` 0.27.0,
+`diffusers` 0.40.0) are replaced by import stubs: neither is on the computed path.
+"""
+
+from __future__ import annotations
+
+import importlib.abc
+import importlib.machinery
+import os
+import sys
+import tempfile
+from pathlib import Path
+from unittest.mock import MagicMock
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+REFERENCE_SRC = os.environ.get("COZY_REFERENCE_SRC", "/root/reference/src")
+
+
+class _Stub(importlib.abc.MetaPathFinder, importlib.abc.Loader):
+    """Stub packages the reference imports but never computes with on this path."""
+
+    roots = ("tensorfs", "diffusers")
+
+    def find_spec(self, name, path, target=None):  # noqa: D102
+        if name.split(".")[0] in self.roots:
+            return importlib.machinery.ModuleSpec(name, self, is_package=True)
+        return None
+
+    def create_module(self, spec):  # noqa: D102
+        module = MagicMock(name=spec.name)
+        module.__path__ = []
+        module.__spec__ = spec
+        return module
+
+    def exec_module(self, module):  # noqa: D102
+        pass
+
+
+def import_reference() -> None:
+    if any(isinstance(f, _Stub) for f in sys.meta_path):
+        return
+    sys.meta_path.insert(0, _Stub())
+    meta = tempfile.mkdtemp(prefix="cozy-dist-")
+    info = Path(meta, "cozy_runtime-0.0.0.dist-info")
+    info.mkdir()
+    (info / "METADATA").write_text("Metadata-Version: 2.1\nName: cozy-runtime\nVersion: 0.0.0\n")
+    sys.path[:0] = [meta, REFERENCE_SRC]
+
+
+def to_np(t: torch.Tensor) -> np.ndarray:
+    if t.dtype == torch.bfloat16:
+        return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+    return t.contiguous().numpy()
+
+
+# (name, world, batch, seq, heads_q, heads_kv, dim, dtype, causal)
+ULYSSES_CASES = [
+    ("w1_fp32", 1, 1, 64, 4, 4, 64, torch.float32, False),
+    ("w2_fp32_batch2", 2, 2, 45, 4, 4, 32, torch.float32, False),
+    ("w3_fp32_padheads", 3, 1, 40, 5, 5, 32, torch.float32, False),
+    ("w4_bf16_padheads", 4, 1, 50, 6, 6, 64, torch.bfloat16, False),
+    ("w7_fp32_uneven", 7, 1, 50, 7, 7, 32, torch.float32, False),
+    ("w2_fp32_causal_gqa", 2, 1, 33, 4, 2, 32, torch.float32, True),
+    ("w8_bf16", 8, 1, 37, 8, 8, 32, torch.bfloat16, False),
+]
+SEED = 20261017  # the reference's attention self-check seed (internal/attention.py cases)
+
+
+def _inputs(batch, seq, hq, hkv, dim, dtype, seed):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(batch, seq, hq, dim, generator=g).to(dtype)
+    k = torch.randn(batch, seq, hkv, dim, generator=g).to(dtype)
+    v = torch.randn(batch, seq, hkv, dim, generator=g).to(dtype)
+    return q, k, v
+
+
+def _rank(rank, world, port, case, outdir):
+    import torch.distributed as dist
+
+    import_reference()
+    from cozy_runtime.internal import attention_upstream
+    from cozy_runtime.internal.parallel import ulysses
+
+    name, _, batch, seq, hq, hkv, dim, dtype, causal = case
+    dist.init_process_group(
+        "gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world
+    )
+    torch.set_num_threads(1)
+    q, k, v = _inputs(batch, seq, hq, hkv, dim, dtype, SEED)
+    if hkv != hq:  # the exchange serves equal heads: K/V replicated to the query heads
+        k = k.repeat_interleave(hq // hkv, dim=2)
+        v = v.repeat_interleave(hq // hkv, dim=2)
+    parts = [torch.tensor_split(t, world, dim=1)[rank].contiguous() for t in (q, k, v)]
+    out = ulysses.exchange(
+        *parts,
+        dist.group.WORLD,
+        lambda a, b, c: attention_upstream.sdpa(a, b, c, is_causal=causal),
+        site="golden",
+    )
+    torch.save(out, os.path.join(outdir, f"{name}.{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def ulysses_goldens() -> None:
+    import torch.multiprocessing as mp
+
+    for index, case in enumerate(ULYSSES_CASES):
+        name, world, batch, seq, hq, hkv, dim, dtype, causal = case
+        with tempfile.TemporaryDirectory() as tmp:
+            mp.spawn(_rank, args=(world, 29600 + index, case, tmp), nprocs=world, join=True)
+            outs = [torch.load(os.path.join(tmp, f"{name}.{r}.pt")) for r in range(world)]
+        out = torch.cat(outs, dim=1)
+        q, k, v = _inputs(batch, seq, hq, hkv, dim, dtype, SEED)
+        rows = [int(o.shape[1]) for o in outs]
+        np.savez_compressed(
+            HERE / f"ulysses_{name}.npz",
+            q=to_np(q), k=to_np(k), v=to_np(v), out=to_np(out),
+            world=world, causal=int(causal), rows=np.array(rows),
+            dtype=str(dtype).replace("torch.", ""),
+        )
+        print(f"ulysses_{name}: rows {rows} out {tuple(out.shape)} {out.dtype}")
+
+
+# (name, HEADS, HEAD_DIM, ROTARY, INTERLEAVED, WEIGHT, OFFSET, ROUND, X32)
+ROPE_CASES = [
+    ("interleaved_full", 2, 64, 64, 1, 0, 0.0, 0, 1),
+    ("split_half_full", 2, 64, 64, 0, 0, 0.0, 0, 1),
+    ("interleaved_partial_weight", 2, 128, 96, 1, 1, 0.0, 0, 1),
+    ("split_half_partial_weight_offset", 2, 128, 64, 0, 1, 1.0, 0, 1),
+]
+
+
+def rope_goldens() -> None:
+    import_reference()
+    from cozy_runtime.internal.bench import kernels as bench_kernels
+
+    for name, heads, dim, rotary, inter, weight, offset, rnd, x32 in ROPE_CASES:
+        entry = MagicMock()
+        entry.key = name
+        entry.constexprs = {
+            "HEADS": heads, "HEAD_DIM": dim, "ROTARY": rotary, "INTERLEAVED": inter,
+            "WEIGHT": weight, "OFFSET": offset, "ROUND": rnd, "X32": x32,
+        }
+        seen: dict[str, object] = {}
+
+        def recorder(launch, entry_, x, w, eps, tables, out_type):
+            seen.update(x=x.clone(), weight=w, eps=eps, tables=tables)
+            return torch.zeros(x.shape, dtype=out_type)
+
+        def error(torch_, got, want):
+            seen["want"] = want.clone()
+            return 0.0
+
+        fused, verify = bench_kernels.fused, bench_kernels.verify
+        saved = fused.head_norm_rope, verify.error
+        fused.head_norm_rope, verify.error = recorder, error
+        try:
+            g = torch.Generator().manual_seed(8)
+            bench_kernels._fused_rope(None, entry, torch.device("cpu"), g, {})
+        finally:
+            fused.head_norm_rope, verify.error = saved
+        cos, sin, stride_token, stride_channel = seen["tables"]
+        w = seen["weight"]
+        np.savez_compressed(
+            HERE / f"rope_{name}.npz",
+            x=to_np(seen["x"]),
+            weight=to_np(w.float()) if w is not None else np.zeros(0, np.float32),
+            cos=cos.contiguous().numpy(), sin=sin.contiguous().numpy(),
+            stride_token=stride_token, stride_channel=stride_channel,
+            eps=seen["eps"], want=seen["want"].numpy(),
+            rotary=rotary, interleaved=inter, has_weight=weight, offset=offset,
+        )
+        print(f"rope_{name}: x {tuple(seen['x'].shape)} strides ({stride_token},{stride_channel})")
+
+
+def fp8_golden() -> None:
+    import_reference()
+    from cozy_runtime.internal import attention_fp8
+
+    g = torch.Generator().manual_seed(SEED)
+    x = torch.randn(2, 70, 3, 64, generator=g).to(torch.bfloat16)
+    x[1, :, 2] = 0  # an all-zero head takes the scale floor
+    x[0, 5, 1, 7] = 40.0
+    codes, descale = attention_fp8.quantise_eager(x)
+    np.savez_compressed(
+        HERE / "fp8_quantise.npz",
+        x=to_np(x), codes=codes.view(torch.uint8).numpy(), descale=descale.numpy(),
+    )
+    print("fp8_quantise:", tuple(codes.shape), tuple(descale.shape))
+
+
+if __name__ == "__main__":
+    ulysses_goldens()
+    rope_goldens()
+    fp8_golden()
