@@ -1,0 +1,396 @@
+#!/usr/bin/env python
+"""Benchmark of the Ulysses context-parallel attention layer (BASELINE.json's metric).
+
+A step is one layer: the fused first stage (RoPE/RMSNorm + transposition into per-peer blocks),
+the seq->head crossing of Q/K/V (NCCL all-to-all; none at degree 1), the sm_100a attention
+kernel, the head->seq crossing of O and the landing. Inputs are synthetic, seeded, resident in
+HBM before the timed region and larger than L2 (126 MB), so no flush is needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c3|c5] [--impl reference]
+
+Under torchrun (N > 1) every rank holds its `torch.tensor_split` rows; the step time is the max
+over ranks of CUDA-event time. Rank 0 prints one JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+METRIC = "CP attention layer ms and TFLOP/s at 1/2/4/8 B200 (device-timed, max over ranks)"
+FALLBACK_BF16_TFLOPS = 1590.0
+
+CONFIGS = {
+    "c2": {
+        "workload": "C2 video-DiT joint self-attention: B=1 H=24 D=128 S=21x30x52+512=33272, "
+        "non-causal, 3D axial RoPE (44/42/42) on the video tokens, inputs N(0,1)*0.5",
+        "batch": 1, "heads": 24, "heads_kv": 24, "dim": 128, "seq": 33272, "causal": False,
+        "rope": ("axial", (21, 30, 52), (44, 42, 42), 10000.0, 0, 512), "norm": False, "amp": 0.5,
+    },
+    "c3": {
+        "workload": "C3 Flux-style joint attention: B=2 H=24 D=128 S=512+64x64=4608, non-causal, "
+        "per-head RMSNorm on Q,K then 2D axial RoPE (16/56/56, theta 10000)",
+        "batch": 2, "heads": 24, "heads_kv": 24, "dim": 128, "seq": 4608, "causal": False,
+        "rope": ("axial", (1, 64, 64), (16, 56, 56), 10000.0, 512, 0), "norm": True, "amp": 1.0,
+    },
+    "c5": {
+        "workload": "C5 causal GQA prefill: B=1 Hq=32 Hkv=8 D=128 S=131071, causal, "
+        "1D RoPE theta 500000",
+        "batch": 1, "heads": 32, "heads_kv": 8, "dim": 128, "seq": 131071, "causal": True,
+        "rope": ("llama", 500000.0), "norm": False, "amp": 1.0,
+    },
+}
+
+
+def layer_flops(cfg: dict, heads: int | None = None) -> float:
+    """Algorithmic FLOPs (padding excluded): 4·B·H·S²·D, causal 4·B·H·D·S(S+1)/2."""
+    b, s, d = cfg["batch"], cfg["seq"], cfg["dim"]
+    h = cfg["heads"] if heads is None else heads
+    if cfg["causal"]:
+        return 4.0 * b * h * d * s * (s + 1) / 2
+    return 4.0 * b * h * s * s * d
+
+
+def make_rope(cfg: dict):
+    from cozy_runtime_b200 import rope
+
+    kind = cfg["rope"][0]
+    if kind == "axial":
+        _, grid, dims, theta, before, after = cfg["rope"]
+        return rope.axial(grid, dims, theta, before=before, after=after)
+    return rope.llama(cfg["seq"], cfg["dim"], cfg["rope"][1])
+
+
+def peaks() -> tuple[float, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return float(data["bf16_tflops"]), "measured (MEASURED_PEAKS.json bf16_tflops, burst)"
+    return FALLBACK_BF16_TFLOPS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi samples of the SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int) -> None:
+        self.gpu, self.proc = gpu, None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+            )
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            out, _ = self.proc.communicate(timeout=10)
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self) -> dict | None:
+        rows = []
+        for ln in getattr(self, "lines", []):
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, flags in rows for i, f in enumerate(flags)
+                          if f.lower().startswith("active")})
+        return {
+            "sm_mhz": statistics.median(r[0] for r in rows),
+            "sm_max_mhz": max(r[1] for r in rows),
+            "reasons": reasons,
+            "samples": len(rows),
+        }
+
+
+def local_gpu_index(local_rank: int) -> int:
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    if visible:
+        ids = [v.strip() for v in visible.split(",") if v.strip()]
+        if local_rank < len(ids) and ids[local_rank].isdigit():
+            return int(ids[local_rank])
+    return local_rank
+
+
+def cpu_baseline(cfg: dict, budget_s: float = 12.0) -> dict:
+    """The reference's CPU computation (torch SDPA math, restated by the oracle) on host cores,
+    over a bounded sample of the workload: query-row blocks of one head against the whole
+    sequence's keys, repeated until `budget_s`; reported as TFLOP/s of that sample."""
+    import torch
+
+    import oracle
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    s, d = cfg["seq"], cfg["dim"]
+    rows = 512
+    g = torch.Generator().manual_seed(1)
+    q = torch.randn(1, rows, 1, d, generator=g).to(torch.bfloat16)
+    k = torch.randn(1, s, 1, d, generator=g).to(torch.bfloat16)
+    v = torch.randn(1, s, 1, d, generator=g).to(torch.bfloat16)
+    flops_call = 4.0 * rows * s * d
+    if cfg["causal"]:  # a causal block at the sequence's end sees every key: same cost
+        pass
+    calls, start = 0, time.perf_counter()
+    while True:
+        oracle.attention_fp32(q, k, v)
+        calls += 1
+        if time.perf_counter() - start >= budget_s:
+            break
+    elapsed = time.perf_counter() - start
+    return {
+        "value": round(flops_call * calls / elapsed / 1e12, 5),
+        "unit": "TFLOP/s",
+        "cores": threads,
+        "kind": "port",
+        "sample": f"{calls} calls of 1 head x {rows} query rows x {s} keys x D={d} "
+        f"(fp32 math on bf16 inputs, oracle restatement of torch SDPA), {elapsed:.1f} s",
+    }
+
+
+def run_reference(args, cfg) -> None:
+    """`--impl reference`: the reference's CPU path for this layer (no GPU), rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    samples = []
+    for i in range(args.warmup + args.steps):
+        base = cpu_baseline(cfg, budget_s=max(1.0, 60.0 / (args.steps + args.warmup)))
+        if i >= args.warmup:
+            samples.append(base)
+    value = statistics.median(s["value"] for s in samples)
+    flops = layer_flops(cfg)
+    base = samples[-1]
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": "TFLOP/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(flops / (value * 1e12) * 1e3, 3) if value else None,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "fp32",
+        "data": "synthetic",
+        "config": {"workload": cfg["workload"], "parallelism": "cpu", "sampled": True},
+        "cpu_baseline": {**base, "value": value},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=40)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    parser.add_argument("--impl", default="cozy", choices=["cozy", "reference"])
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    args = parser.parse_args()
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        run_reference(args, cfg)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    from cozy_runtime_b200 import _lib, attention, ulysses
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    group = None
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=300))
+        group = dist.group.WORLD
+    _lib.load()
+
+    batch, heads, hkv, dim, seq = (cfg[k] for k in ("batch", "heads", "heads_kv", "dim", "seq"))
+    rows = ulysses.tensor_split_rows(seq, world)
+    mine = rows[rank]
+    gen = torch.Generator(device=device).manual_seed(1234 + rank)
+    amp = cfg["amp"]
+
+    def randn(h):
+        return (torch.randn(batch, mine, h, dim, generator=gen, device=device) * amp).to(
+            torch.bfloat16)
+
+    q, k, v = randn(heads), randn(hkv), randn(hkv)
+    spec = make_rope(cfg).to(device)
+    norm = ulysses.Norm() if cfg["norm"] else None
+
+    def step(qq, kk, vv):
+        return ulysses.exchange(qq, kk, vv, group, None, rows=rows, causal=cfg["causal"],
+                                rope=spec, norm_q=norm, norm_k=norm)
+
+    for _ in range(args.warmup):
+        step(q, k, v)
+    torch.cuda.synchronize()
+    attention.check_status(device)
+    ulysses.taken()
+    if group is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local_gpu_index(local))
+    with sampler:
+        e0.record()
+        for _ in range(args.steps):
+            step(q, k, v)
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    clock = ulysses.taken()
+    attention.check_status(device)
+    attn_ms = clock["attention_ms"] / max(1, clock["calls"])
+    layout = ulysses.plan(rows, heads, hkv)
+    my_flops = layer_flops(cfg, heads=layout.q_n[rank])
+    stats = torch.tensor([ms, attn_ms, clock["exposed_ms"] / max(1, clock["calls"])],
+                         dtype=torch.float64, device=device)
+    achieved = torch.tensor([my_flops / (attn_ms * 1e-3) / 1e12 if attn_ms else 0.0],
+                            dtype=torch.float64, device=device)
+    if group is not None:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+        dist.all_reduce(achieved, op=dist.ReduceOp.MIN)
+    ms_max, attn_max, exposed_max = stats.tolist()
+
+    # ---- end to end through the public call, host buffers in and out every step
+    hq = [t.cpu().pin_memory() for t in (q, k, v)]
+    dq = [torch.empty_like(t) for t in (q, k, v)]
+    host_out = torch.empty((batch, mine, heads, dim), dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        for src, dst in zip(hq, dq, strict=True):
+            dst.copy_(src, non_blocking=True)
+        out = step(*dq)
+        host_out.copy_(out, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if group is not None:
+        dist.barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    e2e_steps = max(3, args.steps // 2)
+    for _ in range(e2e_steps):
+        e2e_step()
+    f1.record()
+    torch.cuda.synchronize()
+    e2e_ms = torch.tensor([f0.elapsed_time(f1) / e2e_steps], dtype=torch.float64, device=device)
+    if group is not None:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    h2d = sum(t.numel() * t.element_size() for t in hq)
+    d2h = host_out.numel() * host_out.element_size()
+
+    flops = layer_flops(cfg)
+    if rank == 0:
+        peak, peak_src = peaks()
+        ach = achieved.item()
+        per_step = 2 + (1 if world > 1 else 0)  # pack + attention (+ land)
+        profile = ROOT / "profiles" / f"attention_fwd_{args.config}_traffic.json"
+        traffic = None
+        if profile.exists():
+            traffic = json.loads(profile.read_text()).get("dram_bytes_per_launch")
+        line = {
+            "metric": METRIC,
+            "value": round(flops / (ms_max * 1e-3) / 1e12, 2),
+            "unit": "TFLOP/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_max, 4),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic",
+            "config": {
+                "workload": cfg["workload"],
+                "name": args.config,
+                "batch": batch,
+                "seq_len": seq,
+                "heads": heads,
+                "heads_kv": hkv,
+                "head_dim": dim,
+                "causal": cfg["causal"],
+                "parallelism": f"ulysses{world}",
+                "rows_per_rank": rows,
+                "l2": "inputs larger than L2 (no flush)",
+            },
+            "layer": {
+                "attention_ms": round(attn_max, 4),
+                "exposed_ms": round(exposed_max, 4),
+                "exposed_frac": round(exposed_max / ms_max, 4) if ms_max else None,
+            },
+            "clocks": sampler.summary(),
+            "e2e": {
+                "value": round(flops / (e2e_ms.item() * 1e-3) / 1e12, 2),
+                "unit": "TFLOP/s",
+                "ms_per_step": round(e2e_ms.item(), 4),
+                "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h,
+                "call": "cozy_runtime_b200.ulysses.exchange(q, k, v, group, None, rope=...)",
+            },
+            "gpu_launches": per_step * args.steps,
+            "roofline": {
+                "bound": "tensor",
+                "kernel": "attention_fwd_kernel<128>",
+                "achieved": round(ach, 2),
+                "peak": peak,
+                "unit": "TFLOP/s",
+                "frac": round(ach / peak, 4),
+                "peak_source": peak_src,
+                "traffic": traffic,
+            },
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(cfg)
+        print(json.dumps(line), flush=True)
+    if group is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,130 @@
+"""ctypes binding of libcozy_ulysses.so (the C ABI declared in include/cozy_ulysses.h).
+
+The library is built in-tree (`cozy_runtime_b200.build`). There is no fallback: if the library
+is missing or fails to load, every entry point raises, so a GPU run can never silently take a
+CPU or eager path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from ctypes import POINTER, Structure, c_char_p, c_float, c_int, c_longlong, c_uint64, c_void_p
+from pathlib import Path
+
+MAX_PEERS = 16
+LIBRARY = Path(__file__).resolve().parent / "libcozy_ulysses.so"
+
+#: cudaError_t values the library returns itself
+SUCCESS = 0
+INVALID_VALUE = 1
+NOT_SUPPORTED = 801
+
+#: device status words (include/cozy_ulysses.h)
+STATUS_NAMES = {0: "ok", 1: "on-chip wait timed out", 2: "wait on a peer timed out"}
+
+
+class PackTensor(Structure):
+    """`CozyPackTensor`."""
+
+    _fields_ = [
+        ("src", c_void_p),
+        ("src_strides", c_longlong * 3),
+        ("heads", c_int),
+        ("normalize", c_int),
+        ("norm_weight", c_void_p),
+        ("norm_offset", c_float),
+        ("norm_eps", c_float),
+        ("rotate", c_int),
+        ("dst", c_void_p * MAX_PEERS),
+        ("head_lo", c_int * MAX_PEERS),
+        ("head_n", c_int * MAX_PEERS),
+    ]
+
+
+class Rope(Structure):
+    """`CozyRope`."""
+
+    _fields_ = [
+        ("cos", c_void_p),
+        ("sin", c_void_p),
+        ("stride_token", c_longlong),
+        ("stride_channel", c_int),
+        ("token0", c_longlong),
+        ("rotary", c_int),
+        ("interleaved", c_int),
+    ]
+
+
+class HeadMap(Structure):
+    """`CozyHeadMap`."""
+
+    _fields_ = [("group", c_int), ("q_base", c_int), ("kv_base", c_int)]
+
+
+class CudaCallError(RuntimeError):
+    """A library entry point returned a non-zero cudaError_t."""
+
+    def __init__(self, entry: str, code: int, name: str) -> None:
+        super().__init__(f"{entry} returned {code} ({name})")
+        self.code = code
+
+
+_LIB: ctypes.CDLL | None = None
+_LOAD_ERROR: str = ""
+
+#: entry point -> (argtypes, restype); the exported symbols `include/cozy_ulysses.h` declares
+SIGNATURES = {
+    "cozy_attention_fwd": (
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int,
+         POINTER(c_longlong), POINTER(c_longlong), POINTER(c_longlong), POINTER(c_longlong),
+         POINTER(HeadMap), c_int, c_float, c_void_p, c_uint64],
+        c_int,
+    ),
+    "cozy_ulysses_pack": (
+        [POINTER(PackTensor), c_int, c_int, c_int, c_int, c_int, POINTER(Rope), c_uint64],
+        c_int,
+    ),
+    "cozy_ulysses_land": (
+        [c_void_p, c_int, c_int, c_int, c_int, POINTER(c_int), POINTER(c_int), c_void_p,
+         POINTER(c_longlong), c_uint64],
+        c_int,
+    ),
+    "cozy_error_name": ([c_int], c_char_p),
+    "cozy_abi_version": ([], c_int),
+}
+
+
+def load() -> ctypes.CDLL:
+    """The loaded library; raises RuntimeError when it is missing or does not load."""
+    global _LIB, _LOAD_ERROR
+    if _LIB is not None:
+        return _LIB
+    if not LIBRARY.exists():
+        raise RuntimeError(
+            f"{LIBRARY.name} is not built: run `python -m cozy_runtime_b200.build` "
+            "(the CUDA path has no fallback)"
+        )
+    try:
+        lib = ctypes.CDLL(str(LIBRARY))
+    except OSError as exc:
+        _LOAD_ERROR = str(exc)
+        raise RuntimeError(f"{LIBRARY.name} failed to load: {exc}") from exc
+    for name, (args, res) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = res
+    _LIB = lib
+    return lib
+
+
+def error_name(code: int) -> str:
+    return load().cozy_error_name(code).decode()
+
+
+def check(entry: str, code: int) -> None:
+    if code != SUCCESS:
+        raise CudaCallError(entry, code, error_name(code))
+
+
+def strides3(values) -> ctypes.Array:
+    return (c_longlong * 3)(*(int(v) for v in values))

@@ -1,0 +1,118 @@
+"""The B200 local attention kernel as a `Local`-style forward over [batch, seq, heads, dim].
+
+`forward` is what the reference's exchange calls as `compute` on each rank (the reference's B200
+row is `src/cozy_runtime/internal/attention_upstream.py:191-215` `cudnn`; its option checks are
+:71-95 `_options`, `_heads`, `_output`). It runs `cozy_attention_fwd` from libcozy_ulysses.so;
+there is no other implementation behind it.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+from torch import Tensor
+
+from cozy_runtime_b200 import _lib
+
+_STATUS: dict[int, Tensor] = {}
+
+
+def status_word(device: torch.device) -> Tensor:
+    """This device's status word the kernels report timeouts through (int32, 0 = fine)."""
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    found = _STATUS.get(index)
+    if found is None:
+        found = _STATUS[index] = torch.zeros(1, dtype=torch.int32, device=device)
+    return found
+
+
+def check_status(device: torch.device) -> None:
+    """Raise if a kernel on `device` reported a timed-out wait (synchronizes the device)."""
+    word = int(status_word(device).item())
+    if word:
+        status_word(device).zero_()
+        raise RuntimeError(f"attention kernel reported: {_lib.STATUS_NAMES.get(word, word)}")
+
+
+def _strides(t: Tensor) -> ctypes.Array:
+    """Element strides {seq, head, batch} of a [batch, seq, heads, dim] view."""
+    if t.stride(3) != 1:
+        raise ValueError("the head dimension must be contiguous")
+    return _lib.strides3((t.stride(1), t.stride(2), t.stride(0)))
+
+
+def refusal(query: Tensor, key: Tensor, options: dict) -> str:
+    """Why this kernel does not serve a call, or "" (the reference's `Local.refusal`)."""
+    if options.get("attn_mask") is not None:
+        return "masks are not served"
+    if options.get("dropout_p", 0.0) != 0.0:
+        return "dropout is not served"
+    if query.dtype != torch.bfloat16:
+        return f"{query.dtype} is not served (bf16 only)"
+    if query.shape[-1] not in (64, 128):
+        return f"head dim {query.shape[-1]} is not served (64 or 128)"
+    if not query.is_cuda:
+        return "operands are not on a CUDA device"
+    return ""
+
+
+def attention_into(
+    out: Tensor,
+    query: Tensor,
+    key: Tensor,
+    value: Tensor,
+    *,
+    causal: bool = False,
+    scale: float | None = None,
+    head_map: tuple[int, int, int] | None = None,
+) -> None:
+    """softmax(QKᵀ·scale)V of [B, Sq, Hq, D] queries over [B, Sk, Hkv, D] keys/values, into
+    `out` ([B, Sq, Hq, D], any strides with D contiguous), on the current stream.
+    `head_map` = (group, q_base, kv_base): query head h reads key head (h+q_base)//group-kv_base."""
+    batch, sq, hq, dim = query.shape
+    sk, hkv = key.shape[1], key.shape[2]
+    scale = 1.0 / math.sqrt(dim) if scale is None else float(scale)
+    mapping = None if head_map is None else ctypes.byref(_lib.HeadMap(*head_map))
+    code = _lib.load().cozy_attention_fwd(
+        query.data_ptr(), key.data_ptr(), value.data_ptr(), out.data_ptr(),
+        batch, sq, sk, hq, hkv, dim,
+        _strides(query), _strides(key), _strides(value), _strides(out),
+        mapping, int(causal), scale, status_word(query.device).data_ptr(),
+        torch.cuda.current_stream(query.device).cuda_stream,
+    )
+    _lib.check("cozy_attention_fwd", code)
+
+
+def forward(
+    query: Tensor,
+    key: Tensor,
+    value: Tensor,
+    *,
+    attn_mask: Tensor | None = None,
+    dropout_p: float = 0.0,
+    is_causal: bool = False,
+    scale: float | None = None,
+    enable_gqa: bool = False,
+) -> Tensor:
+    """Attention over [batch, seq, heads, dim] with the reference's local-kernel options
+    (`attention_ulysses.Options`), causal aligned bottom-right; returns the query's shape and
+    dtype on its device."""
+    if dropout_p != 0.0:
+        raise ValueError("cozy-b200 is an inference kernel and does not support dropout")
+    if scale is not None and not math.isfinite(scale):
+        raise ValueError("attention scale must be finite")
+    if query.shape[2] != key.shape[2] and not enable_gqa:
+        raise ValueError("unequal Q/KV head counts require enable_gqa=True")
+    why = refusal(query, key, {"attn_mask": attn_mask, "dropout_p": dropout_p})
+    if why:
+        raise ValueError(f"cozy-b200 attention: {why}")
+    out = torch.empty(query.shape, dtype=query.dtype, device=query.device)
+    attention_into(out, query, key, value, causal=is_causal, scale=scale)
+    return out
+
+
+def implementation(query: Tensor, key: Tensor, value: Tensor, options: dict) -> str:
+    """The reference's `Local.impl`: the concrete implementation serving these operands."""
+    return "cozy-b200-tcgen05"

@@ -1,0 +1,509 @@
+// Flash-attention forward for sm_100a: softmax(Q Kᵀ · scale) V per head, bf16 in and out, fp32
+// softmax statistics and accumulation, on the 5th-generation tensor cores.
+//
+// One CTA owns 256 query rows of one (batch, head): two 128-row query tiles that take turns on
+// the tensor core, so one tile's softmax runs while the other's matrix products do.
+//
+//   warps 0-3   softmax for query tile 0 (thread = one query row = one TMEM lane)
+//   warps 4-7   softmax for query tile 1
+//   warp  8     TMA producer: Q once, then K_j, V_j into a ring of shared-memory slots
+//   warp  9     MMA issuer (one thread): S = Q·Kᵀ into TMEM, O += P·V with P read from TMEM
+//
+// Tensor memory (512 columns × 128 lanes of 32 bits):
+//   [0,128)   S/P of tile 0   (S fp32; P bf16 pairs overwrite its first HD/2... columns)
+//   [128,256) S/P of tile 1
+//   [256, 256+HD) O of tile 0, then O of tile 1
+//
+// The running max is rescaled lazily: a warp rescales its rows of O only when some row's max
+// grew by more than 2^8 since the max its probabilities were taken against; otherwise P is
+// formed against the stale max (values ≤ 256, exact in fp32 and safe in bf16).
+//
+// Memory layout of Q, K, V and O: any strides over (sequence, head, batch) with the head
+// dimension contiguous, described to TMA by 4-D tensor maps (dims: head_dim, seq, head, batch).
+// This reads both a rank's own [B, S, H, D] rows and the [S, B, h, D] receive buffers of the
+// Ulysses exchange without a transpose.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#include "../../include/cozy_ulysses.h"
+#include "sm100.cuh"
+
+namespace cozy {
+
+constexpr int kBlockM = 128;   // query rows per tile (TMEM lanes)
+constexpr int kBlockN = 128;   // key rows per tile
+constexpr int kQTiles = 2;     // query tiles per CTA
+constexpr int kStages = 4;     // K/V ring slots
+constexpr int kThreads = 320;  // 8 softmax warps + producer + MMA
+constexpr float kRescaleLog2 = 8.0f;
+
+struct AttentionParams {
+  int batch, seq_q, seq_k, heads_q, heads_kv;
+  int group, q_base, kv_base;  // query head h reads key/value head (h + q_base) / group - kv_base
+  int causal;
+  int causal_offset;  // seq_k - seq_q: causal aligned bottom-right
+  int q_blocks;       // ceil(seq_q / 256)
+  float scale_log2;   // softmax scale × log2(e)
+  __nv_bfloat16* out;
+  long long out_s, out_h, out_b;  // element strides of O
+  int* status;
+};
+
+template <int HD>
+struct AttentionSmem {
+  static constexpr int kBoxes = HD / 64;              // 128-byte swizzle atoms per row
+  static constexpr int kBoxBytes = 128 * 128;         // one box: 128 rows × 128 bytes
+  static constexpr int kTileBytes = kBoxes * kBoxBytes;
+  static constexpr int kQOffset = 0;
+  static constexpr int kKVOffset = kQTiles * kTileBytes;
+  static constexpr int kBarOffset = kKVOffset + kStages * kTileBytes;
+  // barriers: q_full, kv_full[S], kv_empty[S], s_full[2], p_ready[2], o_final[2], drain
+  static constexpr int kBars = 1 + 2 * kStages + 6 + 1;
+  static constexpr int kMiscOffset = kBarOffset + kBars * 8;
+  static constexpr int kBytes = kMiscOffset + 16;
+  static constexpr int kAlloc = kBytes + 1024;  // slack to align the base to 1024 bytes
+};
+
+// Empty asm that ties 32 registers to a point in the program, so no use of a TMEM load's
+// outputs moves above the tcgen05.wait::ld that makes them valid.
+__device__ __forceinline__ void reg_fence(uint32_t (&r)[32]) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                 "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                 "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]),
+                 "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+                 "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]),
+                 "+r"(r[30]), "+r"(r[31]));
+}
+
+// A wait that ignores the CTA's abort flag but still ends at the time limit: used to drain the
+// asynchronous copies and MMAs a CTA issued before it unwinds.
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity, int* status) {
+  (void)status;  // a drain never gives up early on another CTA's report
+  int never = 0;
+  mbar_wait(bar, parity, reinterpret_cast<volatile int*>(&never), nullptr);
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kThreads, 1)
+    attention_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
+                         const __grid_constant__ CUtensorMap tm_k,
+                         const __grid_constant__ CUtensorMap tm_v, const AttentionParams p) {
+  using L = AttentionSmem<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sQ = smem + L::kQOffset;
+  uint8_t* sKV = smem + L::kKVOffset;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = bars + 1 + kStages;
+  uint64_t* s_full = bars + 1 + 2 * kStages;
+  uint64_t* p_ready = s_full + 2;
+  uint64_t* o_final = s_full + 4;
+  uint64_t* drain = s_full + 6;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMiscOffset);
+  volatile int* abort = reinterpret_cast<volatile int*>(smem + L::kMiscOffset + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // Heaviest causal blocks first: block x takes query block (q_blocks - 1 - x).
+  const int qb = p.q_blocks - 1 - static_cast<int>(blockIdx.x);
+  const int head = blockIdx.y;
+  const int b = blockIdx.z;
+  const int kv_head = (head + p.q_base) / p.group - p.kv_base;
+  const int q0 = qb * (kQTiles * kBlockM);
+  int kv_end = p.seq_k;
+  if (p.causal) kv_end = min(p.seq_k, max(0, q0 + kQTiles * kBlockM + p.causal_offset));
+  const int n_kv = (kv_end + kBlockN - 1) / kBlockN;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&s_full[s], 1);
+      mbar_init(&p_ready[s], kBlockM);
+      mbar_init(&o_final[s], 1);
+    }
+    mbar_init(drain, 1);
+    *abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 8) {
+    tmem_alloc(tmem_slot, 512);
+    tc_fence_before();
+  }
+  if (warp == 9 && lane == 0) {
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp < 8) {
+    // ------------------------------------------------------------------ softmax warpgroups
+    const int s = warp >> 2;
+    const int quarter = warp & 3;
+    const int q_row = q0 + s * kBlockM + quarter * 32 + lane;
+    const uint32_t lane_bits = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t tS = tmem + lane_bits + static_cast<uint32_t>(s * kBlockN);
+    const uint32_t tO = tmem + lane_bits + 256u + static_cast<uint32_t>(s * HD);
+    const int visible = q_row + p.causal_offset;  // last key column this row sees (causal)
+    const float scale = p.scale_log2;
+    float m = -INFINITY;  // running max, log2 domain, of the probabilities' reference point
+    float l = 0.f;        // running row sum against m
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      if (!mbar_wait(&s_full[s], j & 1, abort, p.status)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t r0[32], r1[32], r2[32], r3[32];
+      tmem_ld32(tS + 0, r0);
+      tmem_ld32(tS + 32, r1);
+      tmem_ld32(tS + 64, r2);
+      tmem_ld32(tS + 96, r3);
+      tmem_wait_ld();
+      reg_fence(r0);
+      reg_fence(r1);
+      reg_fence(r2);
+      reg_fence(r3);
+      float x[128];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        x[i] = __uint_as_float(r0[i]);
+        x[32 + i] = __uint_as_float(r1[i]);
+        x[64 + i] = __uint_as_float(r2[i]);
+        x[96 + i] = __uint_as_float(r3[i]);
+      }
+      const int kv0 = j * kBlockN;
+      const bool ragged = kv0 + kBlockN > p.seq_k;
+      const bool diagonal = p.causal && kv0 + kBlockN - 1 > visible;
+      if (ragged || diagonal) {
+        const int limit = min(p.seq_k - 1, p.causal ? visible : p.seq_k - 1) - kv0;
+#pragma unroll
+        for (int i = 0; i < 128; ++i)
+          if (i > limit) x[i] = -INFINITY;
+      }
+      float mt = x[0];
+#pragma unroll
+      for (int i = 1; i < 128; ++i) mt = fmaxf(mt, x[i]);
+      const float m_new = fmaxf(m, mt * scale);
+      if (j == 0) {
+        m = m_new;
+      } else if (__any_sync(0xffffffffu, m_new > m + kRescaleLog2)) {
+        // O row rescale: this warp's rows, once PV of the previous tile completed (the commit
+        // behind s_full covers every earlier MMA of the issuing thread).
+        const float factor = (m == -INFINITY) ? 0.f : ex2_approx(m - m_new);
+        l *= factor;
+#pragma unroll
+        for (int c = 0; c < HD / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + c * 32, o);
+          tmem_wait_ld();
+          reg_fence(o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
+          tmem_st32(tO + c * 32, o);
+        }
+        m = m_new;
+      }
+      const float mu = (m == -INFINITY) ? 0.f : m;
+      float sum = 0.f;
+      uint32_t pk0[32], pk1[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float a = ex2_approx(fmaf(x[2 * i], scale, -mu));
+        const float c = ex2_approx(fmaf(x[2 * i + 1], scale, -mu));
+        sum += a + c;
+        pk0[i] = pack_bf16x2(a, c);
+      }
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float a = ex2_approx(fmaf(x[64 + 2 * i], scale, -mu));
+        const float c = ex2_approx(fmaf(x[64 + 2 * i + 1], scale, -mu));
+        sum += a + c;
+        pk1[i] = pack_bf16x2(a, c);
+      }
+      l += sum;
+      tmem_st32(tS + 0, pk0);
+      tmem_st32(tS + 32, pk1);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&p_ready[s]);
+    }
+    // ------------------------------------------------------------------------- epilogue
+    if (ok && n_kv > 0) {
+      ok = mbar_wait(&o_final[s], 0, abort, p.status);
+      tc_fence_after();
+    }
+    if (ok) {
+      const float inv = (l > 0.f) ? 1.f / l : 0.f;
+      const bool valid = q_row < p.seq_q;
+      __nv_bfloat16* dst = p.out + static_cast<long long>(b) * p.out_b +
+                           static_cast<long long>(q_row) * p.out_s +
+                           static_cast<long long>(head) * p.out_h;
+#pragma unroll
+      for (int c = 0; c < HD / 32; ++c) {
+        uint32_t o[32];
+        if (n_kv > 0) {
+          tmem_ld32(tO + c * 32, o);
+          tmem_wait_ld();
+          reg_fence(o);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = 0u;
+        }
+        uint32_t packed[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          packed[i] = pack_bf16x2(__uint_as_float(o[2 * i]) * inv,
+                                  __uint_as_float(o[2 * i + 1]) * inv);
+        if (valid) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            d4[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2],
+                               packed[4 * i + 3]);
+        }
+      }
+    }
+  } else if (warp == 8) {
+    // ------------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      mbar_expect_tx(q_full, kQTiles * L::kTileBytes);
+      for (int s = 0; s < kQTiles; ++s)
+        for (int box = 0; box < L::kBoxes; ++box)
+          tma_load_4d(sQ + s * L::kTileBytes + box * L::kBoxBytes, &tm_q, q_full, box * 64,
+                      q0 + s * kBlockM, head, b);
+      int issued = 0;
+      for (int i = 0; i < 2 * n_kv; ++i) {
+        const int stage = i % kStages;
+        if (i >= kStages && !mbar_wait(&kv_empty[stage], ((i / kStages) - 1) & 1, abort,
+                                       p.status))
+          break;
+        const int j = i >> 1;
+        const CUtensorMap* map = (i & 1) ? &tm_v : &tm_k;
+        mbar_expect_tx(&kv_full[stage], L::kTileBytes);
+        for (int box = 0; box < L::kBoxes; ++box)
+          tma_load_4d(sKV + stage * L::kTileBytes + box * L::kBoxBytes, map, &kv_full[stage],
+                      box * 64, j * kBlockN, kv_head, b);
+        issued = i + 1;
+      }
+      // Every copy this CTA issued lands before the CTA unwinds (already true on the normal
+      // path, where the MMA thread waited for each one).
+      drain_wait(q_full, 0, p.status);
+      for (int i = max(0, issued - kStages); i < issued; ++i)
+        drain_wait(&kv_full[i % kStages], (i / kStages) & 1, p.status);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------------- MMA issuer
+    if (lane == 0 && n_kv > 0) {
+      constexpr uint32_t kIdescQK = idesc_bf16_f32(kBlockM, kBlockN, false);
+      constexpr uint32_t kIdescPV = idesc_bf16_f32(kBlockM, HD, true);
+      const uint32_t q_base = smem_u32(sQ);
+      const uint32_t kv_base = smem_u32(sKV);
+      auto issue_qk = [&](int s, int stage) {
+        const uint32_t qa = q_base + s * L::kTileBytes;
+        const uint32_t ka = kv_base + stage * L::kTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          // K-major 128-byte swizzle: 16-element steps move 32 bytes inside a row's atom;
+          // every 4 steps move to the next 64-column box.
+          const uint32_t off = (kk >> 2) * L::kBoxBytes + (kk & 3) * 32;
+          mma_ss(tmem + s * kBlockN, smem_desc_sw128(qa + off, 16, 1024),
+                 smem_desc_sw128(ka + off, 16, 1024), kIdescQK, kk > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_pv = [&](int s, int stage, bool accumulate) {
+        const uint32_t va = kv_base + stage * L::kTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < kBlockN / 16; ++kk) {
+          // V is MN-major for this product: 16 key rows per step (2048 bytes); the two
+          // 64-column halves of the head dimension are one box (16 KB) apart.
+          mma_ts(tmem + 256u + s * HD, tmem + s * kBlockN + kk * 8,
+                 smem_desc_sw128(va + kk * 2048, L::kBoxBytes, 1024), kIdescPV,
+                 (accumulate || kk > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait(q_full, 0, abort, p.status);
+      if (ok) ok = mbar_wait(&kv_full[0], 0, abort, p.status);
+      if (ok) {
+        tc_fence_after();
+        issue_qk(0, 0);
+        mma_commit(&s_full[0]);
+        issue_qk(1, 0);
+        mma_commit(&s_full[1]);
+        mma_commit(&kv_empty[0]);
+      }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int iv = 2 * j + 1, ik = 2 * j + 2;
+        const int sv = iv % kStages, sk = ik % kStages;
+        const bool more = j + 1 < n_kv;
+        if (!(ok = mbar_wait(&kv_full[sv], (iv / kStages) & 1, abort, p.status))) break;
+        if (!(ok = mbar_wait(&p_ready[0], j & 1, abort, p.status))) break;
+        tc_fence_after();
+        issue_pv(0, sv, j > 0);
+        if (!more) mma_commit(&o_final[0]);
+        if (more) {
+          if (!(ok = mbar_wait(&kv_full[sk], (ik / kStages) & 1, abort, p.status))) break;
+          tc_fence_after();
+          issue_qk(0, sk);
+          mma_commit(&s_full[0]);
+        }
+        if (!(ok = mbar_wait(&p_ready[1], j & 1, abort, p.status))) break;
+        tc_fence_after();
+        issue_pv(1, sv, j > 0);
+        mma_commit(&kv_empty[sv]);
+        if (!more) mma_commit(&o_final[1]);
+        if (more) {
+          issue_qk(1, sk);
+          mma_commit(&s_full[1]);
+          mma_commit(&kv_empty[sk]);
+        }
+      }
+      // Every MMA this thread issued completes before TMEM is released.
+      mma_commit(drain);
+      drain_wait(drain, 0, p.status);
+    }
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 8) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------------------- host side
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                 const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                 const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                 CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiled encode_tiled() {
+  static EncodeTiled fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiled>(ptr);
+  }
+  return fn;
+}
+
+// A 4-D bf16 tensor map over (head_dim, seq, heads, batch) with element strides
+// (1, s_stride, h_stride, b_stride) and a 64 × 128 box in 128-byte swizzle.
+static int make_map(CUtensorMap* map, const void* base, int head_dim, int seq, int heads,
+                    int batch, long long s_stride, long long h_stride, long long b_stride) {
+  EncodeTiled fn = encode_tiled();
+  if (fn == nullptr) return cudaErrorNotSupported;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(head_dim), static_cast<cuuint64_t>(seq),
+                        static_cast<cuuint64_t>(heads), static_cast<cuuint64_t>(batch)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(s_stride) * 2,
+                           static_cast<cuuint64_t>(h_stride) * 2,
+                           static_cast<cuuint64_t>(b_stride) * 2};
+  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t elem[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims,
+                  strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : cudaErrorInvalidValue;
+}
+
+template <int HD>
+static int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                  const AttentionParams& p, cudaStream_t stream) {
+  using L = AttentionSmem<HD>;
+  static bool configured[64] = {};
+  int device = 0;
+  cudaGetDevice(&device);
+  if (device < 64 && !configured[device]) {
+    cudaError_t e = cudaFuncSetAttribute(attention_fwd_kernel<HD>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+    if (e != cudaSuccess) return e;
+    configured[device] = true;
+  }
+  dim3 grid(p.q_blocks, p.heads_q, p.batch);
+  attention_fwd_kernel<HD><<<grid, kThreads, L::kAlloc, stream>>>(mq, mk, mv, p);
+  return cudaGetLastError();
+}
+
+int attention_forward(const void* q, const void* k, const void* v, void* out, int batch,
+                      int seq_q, int seq_k, int heads_q, int heads_kv, int head_dim,
+                      const long long* q_strides, const long long* k_strides,
+                      const long long* v_strides, const long long* o_strides,
+                      const CozyHeadMap* head_map, int causal, float scale, int* status,
+                      cudaStream_t stream) {
+  if (head_dim != 64 && head_dim != 128) return cudaErrorNotSupported;
+  if (batch <= 0 || seq_q <= 0 || seq_k <= 0 || heads_q <= 0 || heads_kv <= 0)
+    return cudaErrorInvalidValue;
+  CozyHeadMap map = {heads_q / heads_kv, 0, 0};
+  if (head_map != nullptr) {
+    map = *head_map;
+  } else if (heads_q % heads_kv != 0) {
+    return cudaErrorInvalidValue;
+  }
+  if (map.group <= 0) return cudaErrorInvalidValue;
+  // every query head's key/value head must exist
+  const int kv_first = (0 + map.q_base) / map.group - map.kv_base;
+  const int kv_last = (heads_q - 1 + map.q_base) / map.group - map.kv_base;
+  if (kv_first < 0 || kv_last >= heads_kv) return cudaErrorInvalidValue;
+  if (batch > 65535 || heads_q > 65535) return cudaErrorInvalidValue;
+  const void* ptrs[4] = {q, k, v, out};
+  for (const void* ptr : ptrs)
+    if (ptr == nullptr || reinterpret_cast<uintptr_t>(ptr) % 16 != 0) return cudaErrorInvalidValue;
+  const long long* all[4] = {q_strides, k_strides, v_strides, o_strides};
+  for (const long long* st : all)
+    for (int i = 0; i < 3; ++i)
+      if (st[i] <= 0 || st[i] % 8 != 0) return cudaErrorInvalidValue;
+  CUtensorMap mq, mk, mv;
+  int e;
+  if ((e = make_map(&mq, q, head_dim, seq_q, heads_q, batch, q_strides[0], q_strides[1],
+                    q_strides[2])))
+    return e;
+  if ((e = make_map(&mk, k, head_dim, seq_k, heads_kv, batch, k_strides[0], k_strides[1],
+                    k_strides[2])))
+    return e;
+  if ((e = make_map(&mv, v, head_dim, seq_k, heads_kv, batch, v_strides[0], v_strides[1],
+                    v_strides[2])))
+    return e;
+  AttentionParams p;
+  p.batch = batch;
+  p.seq_q = seq_q;
+  p.seq_k = seq_k;
+  p.heads_q = heads_q;
+  p.heads_kv = heads_kv;
+  p.group = map.group;
+  p.q_base = map.q_base;
+  p.kv_base = map.kv_base;
+  p.causal = causal ? 1 : 0;
+  p.causal_offset = seq_k - seq_q;
+  p.q_blocks = (seq_q + kQTiles * kBlockM - 1) / (kQTiles * kBlockM);
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_s = o_strides[0];
+  p.out_h = o_strides[1];
+  p.out_b = o_strides[2];
+  p.status = status;
+  if (head_dim == 128) return launch<128>(mq, mk, mv, p, stream);
+  return launch<64>(mq, mk, mv, p, stream);
+}
+
+}  // namespace cozy

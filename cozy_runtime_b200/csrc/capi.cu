@@ -1,0 +1,60 @@
+// The library's C ABI (include/cozy_ulysses.h): thin extern "C" wrappers that turn the
+// stream handle into a cudaStream_t and forward to the kernels' launchers. Nothing here throws;
+// every entry point returns a cudaError_t value as an int.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/cozy_ulysses.h"
+
+namespace cozy {
+int attention_forward(const void* q, const void* k, const void* v, void* out, int batch,
+                      int seq_q, int seq_k, int heads_q, int heads_kv, int head_dim,
+                      const long long* q_strides, const long long* k_strides,
+                      const long long* v_strides, const long long* o_strides,
+                      const CozyHeadMap* head_map, int causal, float scale, int* status,
+                      cudaStream_t stream);
+int ulysses_pack(const CozyPackTensor* tensors, int count, int world, int rows, int batch,
+                 int head_dim, const CozyRope* rope, cudaStream_t stream);
+int ulysses_land(const void* returned, int world, int rows, int batch, int head_dim,
+                 const int* head_lo, const int* head_n, void* out, const long long* out_strides,
+                 cudaStream_t stream);
+}  // namespace cozy
+
+static inline cudaStream_t as_stream(uintptr_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+extern "C" {
+
+int cozy_attention_fwd(const void* q, const void* k, const void* v, void* out, int batch,
+                       int seq_q, int seq_k, int heads_q, int heads_kv, int head_dim,
+                       const long long* q_strides, const long long* k_strides,
+                       const long long* v_strides, const long long* o_strides,
+                       const CozyHeadMap* head_map, int causal, float scale, int* status,
+                       uintptr_t stream) {
+  if (!q_strides || !k_strides || !v_strides || !o_strides) return cudaErrorInvalidValue;
+  return cozy::attention_forward(q, k, v, out, batch, seq_q, seq_k, heads_q, heads_kv, head_dim,
+                                 q_strides, k_strides, v_strides, o_strides, head_map, causal, scale,
+                                 status, as_stream(stream));
+}
+
+int cozy_ulysses_pack(const CozyPackTensor* tensors, int count, int world, int rows, int batch,
+                      int head_dim, const CozyRope* rope, uintptr_t stream) {
+  if (!tensors) return cudaErrorInvalidValue;
+  return cozy::ulysses_pack(tensors, count, world, rows, batch, head_dim, rope,
+                            as_stream(stream));
+}
+
+int cozy_ulysses_land(const void* returned, int world, int rows, int batch, int head_dim,
+                      const int* head_lo, const int* head_n, void* out,
+                      const long long* out_strides, uintptr_t stream) {
+  if (!head_lo || !head_n || !out_strides) return cudaErrorInvalidValue;
+  return cozy::ulysses_land(returned, world, rows, batch, head_dim, head_lo, head_n, out,
+                            out_strides, as_stream(stream));
+}
+
+const char* cozy_error_name(int code) {
+  return cudaGetErrorName(static_cast<cudaError_t>(code));
+}
+
+int cozy_abi_version(void) { return 100; }
+
+}  // extern "C"

@@ -1,0 +1,241 @@
+// The memory-bound stages around the attention: the fused first stage of the seq->head exchange
+// (per-head RMSNorm + RoPE + transpose into per-peer blocks, one pass over Q/K/V) and the landing
+// of returned output rows into [batch, rows, heads, head_dim].
+//
+// Both move 16-byte vectors: a row of head_dim bf16 is head_dim/8 consecutive threads, so a
+// warp reads and writes whole 128-byte lines. These kernels are bounded by HBM (or, when the
+// destination is a peer's buffer, by NVLink); see the roofline notes in DESIGN.md.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/cozy_ulysses.h"
+
+namespace cozy {
+
+struct PackArgs {
+  CozyPackTensor t[3];
+  CozyRope rope;
+  int count, world, rows, batch;
+  int max_rows_per_peer;  // rows × batch × max(head_n): the grid's x extent
+};
+
+__device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 x = __bfloat1622float2(h[i]);
+    f[2 * i] = x.x;
+    f[2 * i + 1] = x.y;
+  }
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  uint4 v;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+  return v;
+}
+
+// grid: x covers rows × batch × head_n[p] destination rows (CHUNKS threads each), y = peer,
+// z = tensor. One thread = 8 channels of one destination row.
+template <int HD>
+__global__ void __launch_bounds__(256) pack_kernel(const PackArgs a) {
+  constexpr int CHUNKS = HD / 8;
+  constexpr int ROWS_PER_BLOCK = 256 / CHUNKS;
+  const CozyPackTensor& t = a.t[blockIdx.z];
+  const int peer = blockIdx.y;
+  const int n = t.head_n[peer];
+  const int chunk = threadIdx.x % CHUNKS;
+  const long long row = static_cast<long long>(blockIdx.x) * ROWS_PER_BLOCK + threadIdx.x / CHUNKS;
+  const long long total = static_cast<long long>(a.rows) * a.batch * n;
+  // Whole row groups leave together: every lane of a row's group shares `row`.
+  if (n == 0 || row >= total) return;
+  // destination order [rows][batch][n]
+  const int hh = static_cast<int>(row % n);
+  const long long sb = row / n;
+  const int b = static_cast<int>(sb % a.batch);
+  const int s = static_cast<int>(sb / a.batch);
+  const int head = t.head_lo[peer] + hh;
+  const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(t.src) + s * t.src_strides[0] +
+                             head * t.src_strides[1] + b * t.src_strides[2];
+  const int d0 = chunk * 8;
+  float x[8];
+  unpack8(*reinterpret_cast<const uint4*>(src + d0), x);
+
+  // A row's CHUNKS threads are consecutive lanes of one warp (CHUNKS divides 32).
+  const unsigned group_mask =
+      (CHUNKS == 32) ? 0xffffffffu
+                     : (((1u << CHUNKS) - 1u) << ((threadIdx.x & 31) / CHUNKS * CHUNKS));
+  if (t.normalize) {
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss = fmaf(x[i], x[i], ss);
+#pragma unroll
+    for (int o = CHUNKS / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(group_mask, ss, o);
+    const float inv = rsqrtf(ss / HD + t.norm_eps);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float w = t.norm_weight ? t.norm_weight[d0 + i] + t.norm_offset : 1.f;
+      x[i] = t.norm_weight ? x[i] * inv * w : x[i] * inv;
+    }
+  }
+  const CozyRope& r = a.rope;
+  if (t.rotate && r.rotary > 0) {
+    const long long token = r.token0 + s;
+    const float* cs = r.cos + token * r.stride_token;
+    const float* sn = r.sin + token * r.stride_token;
+    if (r.interleaved) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int d = d0 + 2 * i;
+        if (d < r.rotary) {
+          const int col = (d >> 1) * r.stride_channel;
+          const float c = cs[col], sv = sn[col];
+          const float lo = x[2 * i], hi = x[2 * i + 1];
+          x[2 * i] = lo * c - hi * sv;
+          x[2 * i + 1] = hi * c + lo * sv;
+        }
+      }
+    } else {
+      // split-half: channel j pairs with j ± rotary/2, a whole chunk (rotary/16) lanes away
+      const int half_chunks = r.rotary / 16;
+      const int lane = threadIdx.x & 31;
+      const int base = lane - chunk;
+      int partner = chunk;
+      if (chunk < half_chunks) partner = chunk + half_chunks;
+      else if (chunk < 2 * half_chunks) partner = chunk - half_chunks;
+      float y[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) y[i] = __shfl_sync(group_mask, x[i], base + partner);
+      if (chunk < 2 * half_chunks) {
+        const bool low = chunk < half_chunks;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int col = (d0 + i) * r.stride_channel;
+          const float c = cs[col], sv = sn[col];
+          x[i] = low ? x[i] * c - y[i] * sv : x[i] * c + y[i] * sv;
+        }
+      }
+    }
+  }
+  __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(t.dst[peer]) + row * HD + d0;
+  *reinterpret_cast<uint4*>(dst) = pack8(x);
+}
+
+int ulysses_pack(const CozyPackTensor* tensors, int count, int world, int rows, int batch,
+                 int head_dim, const CozyRope* rope, cudaStream_t stream) {
+  if (count < 1 || count > 3 || world < 1 || world > COZY_MAX_PEERS || rows < 0 || batch < 1)
+    return cudaErrorInvalidValue;
+  if (head_dim != 64 && head_dim != 128) return cudaErrorNotSupported;
+  PackArgs a = {};
+  int max_n = 0;
+  bool any_rotate = false;
+  for (int i = 0; i < count; ++i) {
+    a.t[i] = tensors[i];
+    const CozyPackTensor& t = tensors[i];
+    if (t.src == nullptr || reinterpret_cast<uintptr_t>(t.src) % 16) return cudaErrorInvalidValue;
+    for (int k = 0; k < 3; ++k)
+      if (t.src_strides[k] % 8) return cudaErrorInvalidValue;
+    for (int p = 0; p < world; ++p) {
+      if (t.head_n[p] < 0 || t.head_lo[p] < 0 || t.head_lo[p] + t.head_n[p] > t.heads)
+        return cudaErrorInvalidValue;
+      if (t.head_n[p] > 0 && (t.dst[p] == nullptr || reinterpret_cast<uintptr_t>(t.dst[p]) % 16))
+        return cudaErrorInvalidValue;
+      max_n = t.head_n[p] > max_n ? t.head_n[p] : max_n;
+    }
+    any_rotate = any_rotate || t.rotate;
+  }
+  if (any_rotate) {
+    if (rope == nullptr || rope->cos == nullptr || rope->sin == nullptr) return cudaErrorInvalidValue;
+    if (rope->rotary < 0 || rope->rotary > head_dim || rope->rotary % 2) return cudaErrorInvalidValue;
+    if (!rope->interleaved && rope->rotary % 16) return cudaErrorNotSupported;
+    a.rope = *rope;
+  }
+  a.count = count;
+  a.world = world;
+  a.rows = rows;
+  a.batch = batch;
+  const long long dest_rows = static_cast<long long>(rows) * batch * max_n;
+  if (dest_rows == 0) return cudaSuccess;
+  const int rows_per_block = 256 / (head_dim / 8);
+  const long long blocks = (dest_rows + rows_per_block - 1) / rows_per_block;
+  if (blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
+  dim3 grid(static_cast<unsigned>(blocks), world, count);
+  if (head_dim == 128)
+    pack_kernel<128><<<grid, 256, 0, stream>>>(a);
+  else
+    pack_kernel<64><<<grid, 256, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------- landing
+struct LandArgs {
+  const __nv_bfloat16* returned;
+  __nv_bfloat16* out;
+  long long out_s, out_h, out_b;
+  long long offset[COZY_MAX_PEERS];  // element offset of source p's block in `returned`
+  int head_lo[COZY_MAX_PEERS], head_n[COZY_MAX_PEERS];
+  int rows, batch;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(256) land_kernel(const LandArgs a) {
+  constexpr int CHUNKS = HD / 8;
+  constexpr int ROWS_PER_BLOCK = 256 / CHUNKS;
+  const int p = blockIdx.y;
+  const int n = a.head_n[p];
+  const long long row = static_cast<long long>(blockIdx.x) * ROWS_PER_BLOCK + threadIdx.x / CHUNKS;
+  if (n == 0 || row >= static_cast<long long>(a.rows) * a.batch * n) return;
+  const int chunk = threadIdx.x % CHUNKS;
+  const int hh = static_cast<int>(row % n);
+  const long long sb = row / n;
+  const int b = static_cast<int>(sb % a.batch);
+  const int s = static_cast<int>(sb / a.batch);
+  const uint4 v = *reinterpret_cast<const uint4*>(a.returned + a.offset[p] + row * HD + chunk * 8);
+  __nv_bfloat16* dst =
+      a.out + s * a.out_s + (a.head_lo[p] + hh) * a.out_h + b * a.out_b + chunk * 8;
+  *reinterpret_cast<uint4*>(dst) = v;
+}
+
+int ulysses_land(const void* returned, int world, int rows, int batch, int head_dim,
+                 const int* head_lo, const int* head_n, void* out, const long long* out_strides,
+                 cudaStream_t stream) {
+  if (world < 1 || world > COZY_MAX_PEERS || rows < 0 || batch < 1) return cudaErrorInvalidValue;
+  if (head_dim != 64 && head_dim != 128) return cudaErrorNotSupported;
+  if (returned == nullptr || out == nullptr || reinterpret_cast<uintptr_t>(returned) % 16 ||
+      reinterpret_cast<uintptr_t>(out) % 16)
+    return cudaErrorInvalidValue;
+  for (int k = 0; k < 3; ++k)
+    if (out_strides[k] % 8) return cudaErrorInvalidValue;
+  LandArgs a = {};
+  a.returned = static_cast<const __nv_bfloat16*>(returned);
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.out_s = out_strides[0];
+  a.out_h = out_strides[1];
+  a.out_b = out_strides[2];
+  a.rows = rows;
+  a.batch = batch;
+  long long offset = 0;
+  int max_n = 0;
+  for (int p = 0; p < world; ++p) {
+    if (head_n[p] < 0 || head_lo[p] < 0) return cudaErrorInvalidValue;
+    a.offset[p] = offset;
+    a.head_lo[p] = head_lo[p];
+    a.head_n[p] = head_n[p];
+    offset += static_cast<long long>(rows) * batch * head_n[p] * head_dim;
+    max_n = head_n[p] > max_n ? head_n[p] : max_n;
+  }
+  const long long dest_rows = static_cast<long long>(rows) * batch * max_n;
+  if (dest_rows == 0) return cudaSuccess;
+  const int rows_per_block = 256 / (head_dim / 8);
+  dim3 grid(static_cast<unsigned>((dest_rows + rows_per_block - 1) / rows_per_block), world, 1);
+  if (head_dim == 128)
+    land_kernel<128><<<grid, 256, 0, stream>>>(a);
+  else
+    land_kernel<64><<<grid, 256, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace cozy

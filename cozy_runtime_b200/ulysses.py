@@ -1,0 +1,523 @@
+"""The Ulysses exchange around head-local attention, B200-native.
+
+`exchange(query, key, value, handle, compute, site, narrow)` has the signature and the result of
+the reference's `src/cozy_runtime/internal/parallel/ulysses.py:607` (`exchange`, installed behind
+`attention_ulysses.exchange`): every rank passes its sequence rows [B, S_r, H, D] and gets back
+its rows of the attention over the whole sequence, for every head. Differences of mechanism:
+
+* The first stage is one fused kernel (`cozy_ulysses_pack`): RoPE and per-head RMSNorm (when
+  asked), the transpose into per-peer head blocks, for Q, K and V in one launch.
+* Q, K and V cross with NCCL all-to-all (the reference's default wire, ulysses.py:207-246).
+* With `compute=None` the native sm_100a attention reads the receive buffers in place
+  ([S, B, h, D], no unpack) and writes its output straight into the return send buffer; a
+  callable `compute` gets [B, S, h, D] views and is served the reference's way.
+* Heads are owned per rank as the reference pads them (ulysses.py:647): rank p attends over
+  heads [p·⌈H/W⌉, (p+1)·⌈H/W⌉) ∩ [0, H); padded heads are never computed or sent. Grouped-query
+  K/V heads cross only to the ranks whose query heads read them.
+* The landing of the returned rows is one kernel (`cozy_ulysses_land`).
+
+Row ownership follows `torch.tensor_split` (the reference's Diffusers split with
+`ulysses_anything=True`, src/cozy_runtime/internal/parallel/cp.py:166-174). Every rank's row count
+comes from a store meeting per call, as the reference's (ulysses.py:89-133), unless the caller
+passes `rows`.
+"""
+
+from __future__ import annotations
+
+import json
+import threading
+import weakref
+from collections.abc import Callable, Sequence
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+from torch import Tensor
+
+from cozy_runtime_b200 import _lib, attention
+from cozy_runtime_b200.rope import RopeSpec
+
+Compute = Callable[[Tensor, Tensor, Tensor], Tensor]
+
+
+@dataclass(frozen=True)
+class Norm:
+    """Per-head RMSNorm applied in the first stage: `x·rsqrt(mean(x²)+eps)·(weight+offset)`
+    (weight None: unit), the law of src/cozy_runtime/accel/fusion/_kernels.py:78-86."""
+
+    weight: Tensor | None = None
+    offset: float = 0.0
+    eps: float = 1e-6
+
+
+@dataclass(frozen=True)
+class Plan:
+    """Who holds what in one exchange of `world` ranks."""
+
+    rows: tuple[int, ...]
+    heads: int
+    heads_kv: int
+    q_lo: tuple[int, ...]
+    q_n: tuple[int, ...]
+    kv_lo: tuple[int, ...]
+    kv_n: tuple[int, ...]
+
+    @property
+    def world(self) -> int:
+        return len(self.rows)
+
+    @property
+    def total(self) -> int:
+        return sum(self.rows)
+
+    @property
+    def group(self) -> int:
+        return self.heads // self.heads_kv
+
+    def start(self, rank: int) -> int:
+        return sum(self.rows[:rank])
+
+
+def plan(rows: Sequence[int], heads: int, heads_kv: int) -> Plan:
+    """Head ownership for rows `rows` (one entry per rank): query heads as the reference's padded
+    blocks (ulysses.py:647, :325-362), key/value heads as the query heads read them."""
+    world = len(rows)
+    if heads % heads_kv:
+        raise ValueError("query heads must be a multiple of key/value heads")
+    group = heads // heads_kv
+    local = (heads + (-heads % world)) // world
+    q_lo, q_n, kv_lo, kv_n = [], [], [], []
+    for rank in range(world):
+        lo = min(rank * local, heads)
+        hi = min((rank + 1) * local, heads)
+        q_lo.append(lo)
+        q_n.append(hi - lo)
+        if hi > lo:
+            kv_lo.append(lo // group)
+            kv_n.append((hi - 1) // group - lo // group + 1)
+        else:
+            kv_lo.append(0)
+            kv_n.append(0)
+    return Plan(tuple(rows), heads, heads_kv, tuple(q_lo), tuple(q_n), tuple(kv_lo), tuple(kv_n))
+
+
+def tensor_split_rows(total: int, world: int) -> list[int]:
+    """`torch.tensor_split` row counts (cp.py:166-174)."""
+    base, extra = divmod(total, world)
+    return [base + (1 if r < extra else 0) for r in range(world)]
+
+
+# --------------------------------------------------------------------------- store meeting
+class _Meeting:
+    """One metadata round per call over the group's store: every rank's rows and site. Ranks
+    whose sites differ made different calls; each raises (ulysses.py:103-133)."""
+
+    def __init__(self, handle) -> None:
+        from torch.distributed.distributed_c10d import _get_process_group_store
+
+        base = _get_process_group_store(handle)
+        name = getattr(handle, "group_name", "") or "world"
+        self.store = dist.PrefixStore(f"cozy-b200.ulysses/{name}/", base)
+        self.rank = dist.get_rank(handle)
+        self.world = dist.get_world_size(handle)
+        self.sequence = 0
+        self.lock = threading.Lock()
+
+    def gather(self, value: dict) -> list[dict]:
+        self.sequence += 1
+        keys = [f"{self.sequence}/{rank}" for rank in range(self.world)]
+        self.store.set(keys[self.rank], json.dumps(value))
+        self.store.wait(keys)
+        rows = [json.loads(self.store.get(key)) for key in keys]
+        if self.sequence > 1:
+            self.store.delete_key(f"{self.sequence - 1}/{self.rank}")
+        sites = [row["site"] for row in rows]
+        if len(set(sites)) > 1:
+            raise RuntimeError(
+                f"Ulysses call {self.sequence} is not one call: "
+                + ", ".join(f"GPU {rank} at {site}" for rank, site in enumerate(sites))
+            )
+        return rows
+
+
+_MEETINGS: weakref.WeakKeyDictionary = weakref.WeakKeyDictionary()
+_MEETINGS_LOCK = threading.Lock()
+
+
+def _meeting(handle) -> _Meeting:
+    with _MEETINGS_LOCK:
+        found = _MEETINGS.get(handle)
+        if found is None:
+            found = _MEETINGS[handle] = _Meeting(handle)
+        return found
+
+
+# ------------------------------------------------------------------------------- clock
+class _Clock:
+    """Device-event spans of this process's exchanges (the reference's `_Clock`,
+    ulysses.py:507-577): the whole exchange, the attention inside it; exposed = the rest."""
+
+    def __init__(self) -> None:
+        self.pending: list[tuple] = []
+        self.totals = {"calls": 0, "exchange": 0.0, "attention": 0.0, "crossed": 0}
+        self.lock = threading.Lock()
+
+    @staticmethod
+    def mark(on: Tensor):
+        if not on.is_cuda or torch.cuda.is_current_stream_capturing():
+            return None
+        event = torch.cuda.Event(enable_timing=True)
+        event.record()
+        return event
+
+    def add(self, marks: tuple, crossed: int) -> None:
+        if any(m is None for m in marks):
+            return
+        with self.lock:
+            self.pending.append((marks, crossed))
+            if len(self.pending) > 256:
+                self._fold(wait=False)
+
+    def _fold(self, *, wait: bool) -> None:
+        while self.pending:
+            (began, first, last, ended), crossed = self.pending[0]
+            if wait:
+                ended.synchronize()
+            elif not ended.query():
+                return
+            self.pending.pop(0)
+            self.totals["calls"] += 1
+            self.totals["exchange"] += began.elapsed_time(ended)
+            self.totals["attention"] += first.elapsed_time(last)
+            self.totals["crossed"] += crossed
+
+    def take(self) -> dict:
+        with self.lock:
+            self._fold(wait=True)
+            t, self.totals = self.totals, {"calls": 0, "exchange": 0.0, "attention": 0.0, "crossed": 0}
+        return {
+            "calls": t["calls"],
+            "crossed_gb": round(t["crossed"] / 1e9, 3),
+            "exchange_ms": round(t["exchange"], 3),
+            "attention_ms": round(t["attention"], 3),
+            "exposed_ms": round(t["exchange"] - t["attention"], 3),
+        }
+
+
+_CLOCK = _Clock()
+
+
+def taken() -> dict:
+    """What this process's exchanges moved and took since the last take (ulysses.py:580)."""
+    return _CLOCK.take()
+
+
+# ------------------------------------------------------------------------------ exchange
+def _pack_tensor(
+    src: Tensor,
+    sends: list[int],
+    lo: Sequence[int],
+    n: Sequence[int],
+    *,
+    rotate: bool,
+    norm: Norm | None,
+) -> _lib.PackTensor:
+    t = _lib.PackTensor()
+    t.src = src.data_ptr()
+    t.src_strides[:] = [src.stride(1), src.stride(2), src.stride(0)]
+    t.heads = src.shape[2]
+    t.rotate = int(rotate)
+    t.normalize = int(norm is not None)
+    if norm is not None:
+        t.norm_weight = norm.weight.data_ptr() if norm.weight is not None else None
+        t.norm_offset = float(norm.offset)
+        t.norm_eps = float(norm.eps)
+    for p, ptr in enumerate(sends):
+        t.dst[p] = ptr
+        t.head_lo[p] = lo[p]
+        t.head_n[p] = n[p]
+    return t
+
+
+def _rope_struct(rope: RopeSpec, token0: int) -> _lib.Rope:
+    r = _lib.Rope()
+    r.cos = rope.cos.data_ptr()
+    r.sin = rope.sin.data_ptr()
+    r.stride_token = rope.stride_token
+    r.stride_channel = rope.stride_channel
+    r.token0 = token0
+    r.rotary = rope.rotary
+    r.interleaved = int(rope.interleaved)
+    return r
+
+
+def pack(
+    tensors: Sequence[tuple[Tensor, Sequence[int], Sequence[int], Sequence[int], bool, Norm | None]],
+    rows: int,
+    rope: RopeSpec | None,
+    token0: int,
+) -> None:
+    """One `cozy_ulysses_pack` launch: each entry (src, dst pointers per peer, head_lo, head_n,
+    rotate, norm)."""
+    src0 = tensors[0][0]
+    arr = (_lib.PackTensor * len(tensors))(
+        *(_pack_tensor(s, d, lo, n, rotate=r, norm=nm) for s, d, lo, n, r, nm in tensors)
+    )
+    rope_arg = None
+    if rope is not None:
+        rope_arg = _rope_struct(rope, token0)
+    code = _lib.load().cozy_ulysses_pack(
+        arr, len(tensors), len(tensors[0][1]), rows, src0.shape[0], src0.shape[3],
+        None if rope_arg is None else rope_arg, torch.cuda.current_stream(src0.device).cuda_stream,
+    )
+    _lib.check("cozy_ulysses_pack", code)
+
+
+def land(
+    returned: Tensor, out: Tensor, lo: Sequence[int], n: Sequence[int]
+) -> None:
+    """One `cozy_ulysses_land` launch: `returned` stacked by source rank into `out`'s heads."""
+    world = len(lo)
+    code = _lib.load().cozy_ulysses_land(
+        returned.data_ptr(), world, out.shape[1], out.shape[0], out.shape[3],
+        (_lib.c_int * world)(*lo), (_lib.c_int * world)(*n), out.data_ptr(),
+        _lib.strides3((out.stride(1), out.stride(2), out.stride(0))),
+        torch.cuda.current_stream(out.device).cuda_stream,
+    )
+    _lib.check("cozy_ulysses_land", code)
+
+
+def _offsets(sizes: Sequence[int]) -> list[int]:
+    out, acc = [], 0
+    for s in sizes:
+        out.append(acc)
+        acc += s
+    return out
+
+
+class RankStep:
+    """One rank's part of one exchange, phase by phase, so a crossing can be NCCL's
+    (`exchange`) or any other transport that moves the same blocks: `send` buffers hold this
+    rank's block for peer p at `send_offsets[p]`; `receive` buffers take source p's block at
+    `receive_offsets[p]`."""
+
+    def __init__(
+        self,
+        query: Tensor,
+        key: Tensor,
+        value: Tensor,
+        layout: Plan,
+        rank: int,
+        *,
+        rope: RopeSpec | None = None,
+        norm_q: Norm | None = None,
+        norm_k: Norm | None = None,
+    ) -> None:
+        self.query, self.key, self.value = query, key, value
+        self.layout, self.rank = layout, rank
+        self.rope, self.norm_q, self.norm_k = rope, norm_q, norm_k
+        batch, mine, heads, dim = (int(n) for n in query.shape)
+        self.batch, self.mine, self.heads, self.dim = batch, mine, heads, dim
+        world, rows = layout.world, layout.rows
+        self.qn, self.kvn = layout.q_n[rank], layout.kv_n[rank]
+        self.q_sizes = [mine * batch * layout.q_n[p] * dim for p in range(world)]
+        self.kv_sizes = [mine * batch * layout.kv_n[p] * dim for p in range(world)]
+        self.q_in = [r * batch * self.qn * dim for r in rows]
+        self.kv_in = [r * batch * self.kvn * dim for r in rows]
+        self.back_sizes = list(self.q_sizes)  # O returns as Q left: my rows, peer p's heads
+        self.back_in = list(self.q_in)
+        dev, dt = query.device, query.dtype
+        self.q_send = torch.empty(sum(self.q_sizes), dtype=dt, device=dev)
+        self.k_send = torch.empty(sum(self.kv_sizes), dtype=dt, device=dev)
+        self.v_send = torch.empty(sum(self.kv_sizes), dtype=dt, device=dev)
+
+    def receive_buffers(self) -> tuple[Tensor, Tensor, Tensor]:
+        total, dev, dt = self.layout.total, self.query.device, self.query.dtype
+        return (
+            torch.empty(total * self.batch * self.qn * self.dim, dtype=dt, device=dev),
+            torch.empty(total * self.batch * self.kvn * self.dim, dtype=dt, device=dev),
+            torch.empty(total * self.batch * self.kvn * self.dim, dtype=dt, device=dev),
+        )
+
+    def pack(self) -> None:
+        """Stage 1: norm/RoPE/transposition of Q, K, V into the send blocks (one launch)."""
+        el = self.query.element_size()
+
+        def ptrs(buf: Tensor, sizes: Sequence[int]) -> list[int]:
+            return [buf.data_ptr() + off * el for off in _offsets(sizes)]
+
+        lay, rotate = self.layout, self.rope is not None
+        pack(
+            [
+                (self.query, ptrs(self.q_send, self.q_sizes), lay.q_lo, lay.q_n, rotate, self.norm_q),
+                (self.key, ptrs(self.k_send, self.kv_sizes), lay.kv_lo, lay.kv_n, rotate, self.norm_k),
+                (self.value, ptrs(self.v_send, self.kv_sizes), lay.kv_lo, lay.kv_n, False, None),
+            ],
+            self.mine,
+            self.rope,
+            lay.start(self.rank),
+        )
+
+    def attend(
+        self,
+        q_recv: Tensor,
+        k_recv: Tensor,
+        v_recv: Tensor,
+        compute: Compute | None,
+        causal: bool,
+        scale: float | None,
+        into: Tensor | None = None,
+    ) -> Tensor:
+        """Attention over this rank's heads of the whole sequence, read in place from the
+        receive buffers ([total][B][n][D]); returns the O send buffer in the same layout, or
+        writes `into` ([B, total, n, D], any strides; degree 1: the output itself)."""
+        lay, total, batch, dim = self.layout, self.layout.total, self.batch, self.dim
+        qn, kvn = self.qn, self.kvn
+        if into is None:
+            o_send = torch.empty(
+                total * batch * qn * dim, dtype=self.query.dtype, device=self.query.device
+            )
+            ov = o_send.view(total, batch, qn, dim).permute(1, 0, 2, 3) if qn else None
+        else:
+            o_send, ov = into, into
+        if not qn:
+            return o_send
+        qv = q_recv.view(total, batch, qn, dim).permute(1, 0, 2, 3)
+        kv = k_recv.view(total, batch, kvn, dim).permute(1, 0, 2, 3)
+        vv = v_recv.view(total, batch, kvn, dim).permute(1, 0, 2, 3)
+        if compute is None:
+            head_map = (lay.group, lay.q_lo[self.rank], lay.kv_lo[self.rank])
+            attention.attention_into(ov, qv, kv, vv, causal=causal, scale=scale, head_map=head_map)
+            return o_send
+        if kvn != qn or lay.group != 1:
+            idx = torch.tensor(
+                [(lay.q_lo[self.rank] + i) // lay.group - lay.kv_lo[self.rank] for i in range(qn)],
+                device=self.query.device,
+            )
+            kv, vv = kv.index_select(2, idx), vv.index_select(2, idx)
+        attended = compute(qv, kv, vv)
+        if attended.shape != (batch, total, qn, dim) or attended.dtype != self.query.dtype:
+            raise ValueError("Ulysses attention returned incompatible output")
+        ov.copy_(attended)
+        return o_send
+
+    def land(self, returned: Tensor) -> Tensor:
+        """Stage 3: the returned rows of every source rank into [B, S_r, H, D]."""
+        out = torch.empty(
+            (self.batch, self.mine, self.heads, self.dim), dtype=self.query.dtype,
+            device=self.query.device,
+        )
+        land(returned, out, self.layout.q_lo, self.layout.q_n)
+        return out
+
+    def moved(self) -> int:
+        """Bytes this rank sent to other ranks (Q, K, V in; O back)."""
+        r = self.rank
+        el = self.query.element_size()
+        return el * (
+            sum(self.q_sizes) - self.q_sizes[r] + 2 * (sum(self.kv_sizes) - self.kv_sizes[r])
+            + sum(self.back_in) - self.back_in[r]
+        )
+
+
+def exchange(
+    query: Tensor,
+    key: Tensor,
+    value: Tensor,
+    handle,
+    compute: Compute | None = None,
+    site: str = "",
+    narrow: bool | Callable[[int], bool] = False,
+    *,
+    rows: Sequence[int] | None = None,
+    causal: bool = False,
+    scale: float | None = None,
+    rope: RopeSpec | None = None,
+    norm_q: Norm | None = None,
+    norm_k: Norm | None = None,
+) -> Tensor:
+    """Sequence shards -> whole sequences per head subset -> attention -> back.
+
+    The first seven arguments are the reference's (`attention_ulysses.Exchange`); `compute=None`
+    takes the native attention with `causal`/`scale`. `rows`: every rank's row count, when the
+    caller knows them (skips the store meeting). `rope`: tables over the whole sequence, applied
+    to Q and K by global position in the first stage; `norm_q`/`norm_k`: per-head RMSNorm before
+    it. Returns [B, S_r, H, D] in the query's dtype.
+    """
+    wide = narrow(0) if callable(narrow) else narrow
+    if wide:
+        raise NotImplementedError("the int8 narrow wire is not built on this path")
+    if not query.is_cuda:
+        raise ValueError("cozy-b200 exchange serves CUDA tensors only")
+    if query.dtype != torch.bfloat16:
+        raise ValueError(f"cozy-b200 exchange serves bf16, not {query.dtype}")
+    world = dist.get_world_size(handle) if handle is not None else 1
+    rank = dist.get_rank(handle) if handle is not None else 0
+    batch, mine, heads, dim = (int(n) for n in query.shape)
+    heads_kv = int(key.shape[2])
+    if key.shape != value.shape or key.shape[:2] != query.shape[:2] or key.shape[3] != dim:
+        raise ValueError("Q, K and V must share batch, rows and head dim; K and V one shape")
+    if rows is None:
+        if world == 1:
+            rows = [mine]
+        else:
+            meet = _meeting(handle)
+            with meet.lock:
+                proposals = meet.gather(
+                    {"rows": mine, "site": f"{site or 'attention'} [{batch} x {heads} x {dim}]"}
+                )
+            rows = [int(p["rows"]) for p in proposals]
+    rows = [int(r) for r in rows]
+    if len(rows) != world or rows[rank] != mine:
+        raise ValueError(f"rows {rows} do not match rank {rank}'s {mine} rows of {world}")
+    layout = plan(rows, heads, heads_kv)
+    began = _Clock.mark(query)
+
+    if world == 1 and rope is None and norm_q is None and norm_k is None and compute is None:
+        out = torch.empty((batch, mine, heads, dim), dtype=query.dtype, device=query.device)
+        first = _Clock.mark(query)
+        attention.attention_into(out, query, key, value, causal=causal, scale=scale)
+        _CLOCK.add((began, first, _Clock.mark(query), _Clock.mark(query)), 0)
+        return out
+
+    step = RankStep(query, key, value, layout, rank, rope=rope, norm_q=norm_q, norm_k=norm_k)
+    step.pack()
+    crossed = False
+    try:
+        if world == 1:
+            q_recv, k_recv, v_recv = step.q_send, step.k_send, step.v_send
+        else:
+            q_recv, k_recv, v_recv = step.receive_buffers()
+            crossed = True
+            dist.all_to_all_single(q_recv, step.q_send, step.q_in, step.q_sizes, group=handle)
+            dist.all_to_all_single(k_recv, step.k_send, step.kv_in, step.kv_sizes, group=handle)
+            dist.all_to_all_single(v_recv, step.v_send, step.kv_in, step.kv_sizes, group=handle)
+        if world == 1:  # degree 1: attention writes the output itself, nothing lands
+            out = torch.empty((batch, mine, heads, dim), dtype=query.dtype, device=query.device)
+            first = _Clock.mark(query)
+            step.attend(q_recv, k_recv, v_recv, compute, causal, scale, into=out)
+            last = _Clock.mark(query)
+        else:
+            first = _Clock.mark(query)
+            o_send = step.attend(q_recv, k_recv, v_recv, compute, causal, scale)
+            last = _Clock.mark(query)
+            returned = torch.empty(sum(step.back_sizes), dtype=query.dtype, device=query.device)
+            dist.all_to_all_single(returned, o_send, step.back_sizes, step.back_in, group=handle)
+            out = step.land(returned)
+    except BaseException:
+        if crossed:
+            _abort(handle)
+        raise
+    _CLOCK.add((began, first, last, _Clock.mark(query)), step.moved())
+    return out
+
+
+def _abort(handle) -> None:
+    """After crossing began, a failing rank ends its group so peers blocked in collectives raise
+    (the reference's `abort_process_group`, ulysses.py:754-758)."""
+    abort = getattr(handle, "abort", None)
+    if callable(abort):
+        try:
+            abort()
+        except Exception:  # noqa: BLE001 - the original error is what the caller sees
+            pass

@@ -1,0 +1,115 @@
+/* C ABI of the B200-native Ulysses context-parallel attention path (libcozy_ulysses.so).
+ *
+ * Conventions (those of the reference's native modules, kernels/csrc/gemm.cpp:1-7 and
+ * kernels/csrc/fa3.cpp:1-9 in cozy-runtime): arguments are raw device pointers, sizes, element
+ * strides and a cudaStream_t passed as uintptr_t; the caller allocates every buffer; each call
+ * returns a cudaError_t value as an int (0 = queued on the stream; cudaErrorNotSupported = 801
+ * when no kernel serves the shape; cudaErrorInvalidValue = 1 for bad arguments) and never
+ * throws. `cozy_error_name` names a code. Kernels that wait report through a caller-owned
+ * device status word (0 = fine, 1 = an on-chip wait timed out, 2 = a wait on a peer timed out).
+ *
+ * Every tensor is bf16 with its last (head) dimension contiguous unless stated otherwise.
+ */
+#ifndef COZY_ULYSSES_H
+#define COZY_ULYSSES_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define COZY_MAX_PEERS 16
+
+#if defined(__GNUC__)
+#define COZY_API __attribute__((visibility("default")))
+#else
+#define COZY_API
+#endif
+
+/* How query heads map to key/value heads: query head h reads key/value head
+ * (h + q_base) / group - kv_base. NULL selects group = heads_q / heads_kv, q_base = kv_base = 0
+ * (torch's enable_gqa rule). A Ulysses rank that owns query heads [q_lo, q_lo + n) of a
+ * grouped-query layer, and received key/value heads from kv_lo, passes {group, q_lo, kv_lo}. */
+typedef struct CozyHeadMap {
+  int group;
+  int q_base;
+  int kv_base;
+} CozyHeadMap;
+
+/* Local attention over whole sequences: softmax(Q Kᵀ·scale) V for every (batch, query head),
+ * query head h reading the key/value head `head_map` names. Causal masks align bottom-right
+ * (key j visible to query i when j <= i + seq_k - seq_q).
+ * Replaces the local kernel the reference's exchange calls as `compute` on a B200:
+ * src/cozy_runtime/internal/attention_upstream.py:191-215 (`cudnn`, torch SDPA on cuDNN) and
+ * :109-147 (`sdpa`), on [batch, seq, heads, dim] operands.
+ * Strides are in elements, ordered {seq, head, batch}; each a multiple of 8; pointers 16-byte
+ * aligned. head_dim 64 or 128. */
+COZY_API int cozy_attention_fwd(const void* q, const void* k, const void* v, void* out, int batch,
+                       int seq_q, int seq_k, int heads_q, int heads_kv, int head_dim,
+                       const long long* q_strides, const long long* k_strides,
+                       const long long* v_strides, const long long* o_strides,
+                       const CozyHeadMap* head_map, int causal, float scale, int* status,
+                       uintptr_t stream);
+
+/* One tensor of the seq->head exchange's first stage (Q, K or V): this rank's rows
+ * [batch, rows, heads, head_dim] (`src`, element strides {seq, head, batch}), optionally
+ * RMS-normalised per head and rotated, written as the block each peer receives:
+ * peer p gets heads [head_lo[p], head_lo[p] + head_n[p]) at dst[p] laid out
+ * [rows][batch][head_n[p]][head_dim]. dst[p] may be a local send buffer (NCCL crossing) or
+ * this rank's row offset inside peer p's receive buffer (peer stores over NVLink). */
+typedef struct CozyPackTensor {
+  const void* src;
+  long long src_strides[3];
+  int heads;
+  int normalize;            /* per-head RMSNorm before RoPE */
+  const float* norm_weight; /* [head_dim] fp32, or NULL for unit weight */
+  float norm_offset;        /* weight + offset multiplies the normalised row */
+  float norm_eps;
+  int rotate;               /* apply RoPE (CozyRope) */
+  void* dst[COZY_MAX_PEERS];
+  int head_lo[COZY_MAX_PEERS];
+  int head_n[COZY_MAX_PEERS];
+} CozyPackTensor;
+
+/* RoPE tables as the reference's `rope_tables` returns them
+ * (src/cozy_runtime/accel/fusion/_kernels.py:497-517): fp32 cos and sin read at
+ * token * stride_token + column * stride_channel. `token0` is the table row of this rank's
+ * first row. The first `rotary` channels rotate: interleaved pairs (2i, 2i+1) read column i;
+ * split-half pairs (j, j ± rotary/2) read column j. */
+typedef struct CozyRope {
+  const float* cos;
+  const float* sin;
+  long long stride_token;
+  int stride_channel;
+  long long token0;
+  int rotary;
+  int interleaved;
+} CozyRope;
+
+/* The fused first stage of the exchange for up to three tensors in one launch: per-head
+ * RMSNorm + RoPE (the law of src/cozy_runtime/accel/fusion/_kernels.py:177-240
+ * `head_norm_rope_kernel`, fp32 arithmetic rounded once) fused with the pack into per-peer
+ * blocks that src/cozy_runtime/internal/parallel/ulysses.py:325-362 (`_pack`) performs. */
+COZY_API int cozy_ulysses_pack(const CozyPackTensor* tensors, int count, int world, int rows, int batch,
+                      int head_dim, const CozyRope* rope, uintptr_t stream);
+
+/* The last stage of the exchange: the attended rows returned by every rank, stacked by source
+ * rank in `returned` ([world][rows][batch][head_n[p]][head_dim]), landed in this rank's output
+ * `out` [batch, rows, heads, head_dim] (element strides {seq, head, batch}) at heads
+ * head_lo[p] + j. Replaces src/cozy_runtime/internal/parallel/ulysses.py:435-457 (`_land`). */
+COZY_API int cozy_ulysses_land(const void* returned, int world, int rows, int batch, int head_dim,
+                      const int* head_lo, const int* head_n, void* out,
+                      const long long* out_strides, uintptr_t stream);
+
+/* Name of a code returned above (a cudaError_t, or one of this library's). */
+COZY_API const char* cozy_error_name(int code);
+
+/* Library ABI version (major * 100 + minor). */
+COZY_API int cozy_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* COZY_ULYSSES_H */

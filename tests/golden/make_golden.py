@@ -78,24 +78,27 @@ def to_np(t: torch.Tensor) -> np.ndarray:
     return t.contiguous().numpy()
 
 
-# (name, world, batch, seq, heads_q, heads_kv, dim, dtype, causal)
+# (name, world, batch, seq, heads_q, heads_kv, dim, compute dtype, causal). Inputs are drawn
+# as bf16 values (the GPU path's input type) and the reference computes in `dtype` on them.
 ULYSSES_CASES = [
-    ("w1_fp32", 1, 1, 64, 4, 4, 64, torch.float32, False),
-    ("w2_fp32_batch2", 2, 2, 45, 4, 4, 32, torch.float32, False),
-    ("w3_fp32_padheads", 3, 1, 40, 5, 5, 32, torch.float32, False),
-    ("w4_bf16_padheads", 4, 1, 50, 6, 6, 64, torch.bfloat16, False),
-    ("w7_fp32_uneven", 7, 1, 50, 7, 7, 32, torch.float32, False),
-    ("w2_fp32_causal_gqa", 2, 1, 33, 4, 2, 32, torch.float32, True),
-    ("w8_bf16", 8, 1, 37, 8, 8, 32, torch.bfloat16, False),
+    ("w1", 1, 1, 64, 4, 4, 64, torch.float32, False),
+    ("w2_batch2", 2, 2, 45, 4, 4, 64, torch.float32, False),
+    ("w3_padheads", 3, 1, 40, 5, 5, 128, torch.float32, False),
+    ("w4_padheads", 4, 1, 50, 6, 6, 64, torch.float32, False),
+    ("w4_bf16_compute", 4, 1, 50, 6, 6, 64, torch.bfloat16, False),
+    ("w7_uneven", 7, 1, 50, 7, 7, 64, torch.float32, False),
+    ("w2_causal_gqa", 2, 1, 33, 4, 2, 128, torch.float32, True),
+    ("w7_causal_gqa_idle_ranks", 7, 1, 60, 8, 2, 64, torch.float32, True),
+    ("w8", 8, 1, 37, 8, 8, 64, torch.float32, False),
 ]
 SEED = 20261017  # the reference's attention self-check seed (internal/attention.py cases)
 
 
 def _inputs(batch, seq, hq, hkv, dim, dtype, seed):
     g = torch.Generator().manual_seed(seed)
-    q = torch.randn(batch, seq, hq, dim, generator=g).to(dtype)
-    k = torch.randn(batch, seq, hkv, dim, generator=g).to(dtype)
-    v = torch.randn(batch, seq, hkv, dim, generator=g).to(dtype)
+    q = torch.randn(batch, seq, hq, dim, generator=g).to(torch.bfloat16).to(dtype)
+    k = torch.randn(batch, seq, hkv, dim, generator=g).to(torch.bfloat16).to(dtype)
+    v = torch.randn(batch, seq, hkv, dim, generator=g).to(torch.bfloat16).to(dtype)
     return q, k, v
 
 
@@ -138,9 +141,10 @@ def ulysses_goldens() -> None:
         out = torch.cat(outs, dim=1)
         q, k, v = _inputs(batch, seq, hq, hkv, dim, dtype, SEED)
         rows = [int(o.shape[1]) for o in outs]
+        q, k, v = (t.to(torch.bfloat16) for t in (q, k, v))  # exact: drawn as bf16
         np.savez_compressed(
             HERE / f"ulysses_{name}.npz",
-            q=to_np(q), k=to_np(k), v=to_np(v), out=to_np(out),
+            q=to_np(q), k=to_np(k), v=to_np(v), out=to_np(out.float()), heads_kv=hkv,
             world=world, causal=int(causal), rows=np.array(rows),
             dtype=str(dtype).replace("torch.", ""),
         )
@@ -149,10 +153,11 @@ def ulysses_goldens() -> None:
 
 # (name, HEADS, HEAD_DIM, ROTARY, INTERLEAVED, WEIGHT, OFFSET, ROUND, X32)
 ROPE_CASES = [
-    ("interleaved_full", 2, 64, 64, 1, 0, 0.0, 0, 1),
-    ("split_half_full", 2, 64, 64, 0, 0, 0.0, 0, 1),
-    ("interleaved_partial_weight", 2, 128, 96, 1, 1, 0.0, 0, 1),
-    ("split_half_partial_weight_offset", 2, 128, 64, 0, 1, 1.0, 0, 1),
+    ("interleaved_full", 2, 64, 64, 1, 0, 0.0, 1, 0),
+    ("split_half_full", 2, 64, 64, 0, 0, 0.0, 1, 0),
+    ("interleaved_partial_weight", 2, 128, 96, 1, 1, 0.0, 1, 0),
+    ("split_half_partial_weight_offset", 2, 128, 64, 0, 1, 1.0, 1, 0),
+    ("interleaved_full_d128", 2, 128, 128, 1, 0, 0.0, 1, 0),
 ]
 
 

@@ -1,0 +1,138 @@
+"""Host logic without a GPU: head ownership, row splits, the store meeting over gloo ranks, and the
+C ABI library's exports (no compute calls)."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+import oracle
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def test_plan_matches_oracle_head_ownership():
+    from cozy_runtime_b200 import ulysses
+
+    for heads in (5, 7, 8, 24, 32, 40):
+        for world in (1, 2, 3, 4, 7, 8):
+            layout = ulysses.plan([10] * world, heads, heads)
+            for r in range(world):
+                owned = oracle.owned_heads(heads, world, r)
+                assert layout.q_lo[r] == (owned.start if len(owned) else layout.q_lo[r])
+                assert layout.q_n[r] == len(owned)
+
+
+def test_plan_gqa_kv_heads_cover_query_heads():
+    from cozy_runtime_b200 import ulysses
+
+    for hq, hkv in ((32, 8), (8, 2), (24, 24), (40, 8)):
+        for world in (1, 2, 4, 7, 8):
+            lay = ulysses.plan([3] * world, hq, hkv)
+            for r in range(world):
+                for h in range(lay.q_lo[r], lay.q_lo[r] + lay.q_n[r]):
+                    kvh = h // lay.group
+                    assert lay.kv_lo[r] <= kvh < lay.kv_lo[r] + lay.kv_n[r]
+
+
+def test_c5_degree7_ownership():
+    """Causal GQA prefill at degree 7: 32 query heads pad to 35, ranks own 5,5,5,5,5,5,2."""
+    from cozy_runtime_b200 import ulysses
+
+    rows = ulysses.tensor_split_rows(131071, 7)
+    assert rows == [18725, 18725, 18725, 18724, 18724, 18724, 18724]
+    lay = ulysses.plan(rows, 32, 8)
+    assert lay.q_n == (5, 5, 5, 5, 5, 5, 2)
+    assert lay.kv_n == (2, 2, 2, 2, 2, 2, 1)
+
+
+def test_tensor_split_rows():
+    from cozy_runtime_b200 import ulysses
+
+    for total in (7, 4608, 33272, 131071):
+        for world in (1, 2, 4, 7, 8):
+            want = [t.shape[0] for t in torch.tensor_split(torch.empty(total), world)]
+            assert ulysses.tensor_split_rows(total, world) == want
+
+
+def _meeting_rank(rank, world, port, results):
+    import torch.distributed as dist
+
+    from cozy_runtime_b200 import ulysses
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world)
+    meet = ulysses._meeting(dist.group.WORLD)
+    first = meet.gather({"rows": 10 + rank, "site": "a"})
+    second = meet.gather({"rows": 20 + rank, "site": "a"})
+    diverged = ""
+    try:
+        meet.gather({"rows": 1, "site": f"site{rank}"})
+    except RuntimeError as exc:
+        diverged = str(exc)
+    results[rank] = ([r["rows"] for r in first], [r["rows"] for r in second], diverged)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_store_meeting_gloo_world2():
+    """Two gloo ranks agree on each other's rows per call and both see a divergence."""
+    import torch.multiprocessing as mp
+
+    manager = mp.Manager()
+    results = manager.dict()
+    mp.spawn(_meeting_rank, args=(2, 29731, results), nprocs=2, join=True)
+    for rank in range(2):
+        first, second, diverged = results[rank]
+        assert first == [10, 11] and second == [20, 21]
+        assert "is not one call" in diverged
+
+
+def _header_symbols() -> set[str]:
+    text = (ROOT / "include" / "cozy_ulysses.h").read_text()
+    return set(re.findall(r"COZY_API\s+[\w\s\*]+?\b(cozy_\w+)\s*\(", text))
+
+
+def test_library_exports_header_symbols():
+    from cozy_runtime_b200 import _lib
+
+    lib = ctypes.CDLL(str(_lib.LIBRARY))
+    declared = _header_symbols()
+    assert declared == set(_lib.SIGNATURES), "the ctypes binding covers the header"
+    for name in declared:
+        assert hasattr(lib, name), name
+    assert lib.cozy_abi_version() == 100
+
+
+def test_error_name_without_gpu():
+    from cozy_runtime_b200 import _lib
+
+    assert _lib.error_name(801) == "cudaErrorNotSupported"
+    assert _lib.error_name(0) == "cudaSuccess"
+
+
+def test_product_path_fails_loudly_without_library(monkeypatch, tmp_path):
+    from cozy_runtime_b200 import _lib
+
+    monkeypatch.setattr(_lib, "_LIB", None)
+    monkeypatch.setattr(_lib, "LIBRARY", tmp_path / "missing.so")
+    with pytest.raises(RuntimeError, match="not built"):
+        _lib.load()
+
+
+def test_product_does_not_import_oracle():
+    for path in (ROOT / "cozy_runtime_b200").rglob("*.py"):
+        text = path.read_text()
+        assert "import oracle" not in text and "from oracle" not in text, path
+
+
+def test_exchange_refuses_cpu_and_narrow():
+    from cozy_runtime_b200 import ulysses
+
+    x = torch.zeros(1, 4, 2, 64, dtype=torch.bfloat16)
+    with pytest.raises(NotImplementedError):
+        ulysses.exchange(x, x, x, None, None, narrow=True)
+    with pytest.raises(ValueError):
+        ulysses.exchange(x, x, x, None, None)

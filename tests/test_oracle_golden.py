@@ -21,7 +21,7 @@ def test_exchange_matches_reference(name):
     )
     got = torch.cat(outs, dim=1)
     want = tensor(case["out"]).float()
-    if q.dtype == torch.bfloat16:  # the reference computed in bf16: its own rounding
+    if str(case["dtype"]) == "bfloat16":  # the reference computed in bf16: its own rounding
         assert (got - want).abs().max() < 2e-2
     else:
         assert (got - want).abs().max() < 2e-5
