@@ -38,7 +38,7 @@ CASES = [
     (1, 1024, 1024, 2, 2, 64, True, 1.0),
     (1, 2048, 2048, 1, 1, 128, True, 1.0),
     (1, 384, 384, 2, 2, 128, False, 4.0),  # large logits: exercises the O rescale
-    (1, 300, 257, 2, 2, 128, True, 1.0),  # cross lengths, causal bottom-right
+    (1, 257, 300, 2, 2, 128, True, 1.0),  # cross lengths, causal bottom-right
     (1, 1, 130, 1, 1, 128, False, 1.0),  # one query row
 ]
 
@@ -58,6 +58,21 @@ def test_attention_matches_oracle(batch, sq, sk, hq, hkv, dim, causal, amp):
     attention.check_status(got.device)
     want = oracle.attention_fp32(q, k, v, causal=causal)
     _check(got, want)
+
+
+def test_attention_rows_without_keys_are_zero():
+    """Bottom-right causal with more queries than keys: the first Sq - Sk rows see no key. The
+    kernel writes zeros there (torch's SDPA gives NaN); every other row matches the oracle."""
+    from cozy_runtime_b200 import attention
+
+    g = torch.Generator().manual_seed(3)
+    q = _randn((1, 300, 2, 128), g)
+    k = _randn((1, 257, 2, 128), g)
+    v = _randn((1, 257, 2, 128), g)
+    got = attention.forward(q.cuda(), k.cuda(), v.cuda(), is_causal=True).float().cpu()
+    assert torch.equal(got[:, :43], torch.zeros_like(got[:, :43]))
+    want = oracle.attention_fp32(q, k, v, causal=True)
+    _check(got[:, 43:], want[:, 43:])
 
 
 def test_attention_strided_layouts():
