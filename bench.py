@@ -220,8 +220,15 @@ def main() -> None:
     parser.add_argument("--config", default="c2", choices=sorted(CONFIGS))
     parser.add_argument("--impl", default="cozy", choices=["cozy", "reference"])
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
+    parser.add_argument("--heads", type=int, default=0,
+                        help="profiling only: fewer heads (same sequence and layout)")
     args = parser.parse_args()
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.heads:
+        group = cfg["heads"] // cfg["heads_kv"]
+        cfg["heads"], cfg["heads_kv"] = args.heads, max(1, args.heads // group)
+        cfg["workload"] += f" [profiling subset: {cfg['heads']} heads]"
     if args.impl == "reference":
         run_reference(args, cfg)
         return
@@ -295,6 +302,10 @@ def main() -> None:
     ms_max, attn_max, exposed_max = stats.tolist()
 
     # ---- end to end through the public call, host buffers in and out every step
+    if args.no_e2e:
+        if group is not None:
+            dist.destroy_process_group()
+        return
     hq = [t.cpu().pin_memory() for t in (q, k, v)]
     dq = [torch.empty_like(t) for t in (q, k, v)]
     host_out = torch.empty((batch, mine, heads, dim), dtype=torch.bfloat16).pin_memory()

@@ -8,6 +8,7 @@
 //   warps 4-7   softmax for query tile 1
 //   warp  8     TMA producer: Q once, then K_j, V_j into a ring of shared-memory slots
 //   warp  9     MMA issuer (one thread): S = Q·Kᵀ into TMEM, O += P·V with P read from TMEM
+//   warps 10-11 idle (they complete the third warpgroup the register split needs)
 //
 // Tensor memory (512 columns × 128 lanes of 32 bits):
 //   [0,128)   S/P of tile 0   (S fp32; P bf16 pairs overwrite its first HD/2... columns)
@@ -37,7 +38,13 @@ constexpr int kBlockM = 128;   // query rows per tile (TMEM lanes)
 constexpr int kBlockN = 128;   // key rows per tile
 constexpr int kQTiles = 2;     // query tiles per CTA
 constexpr int kStages = 4;     // K/V ring slots
-constexpr int kThreads = 320;  // 8 softmax warps + producer + MMA
+constexpr int kThreads = 384;  // 8 softmax warps + producer + MMA + 2 idle (a full warpgroup)
+// Register split (setmaxnreg): the launch gives every thread 168 (384 × 168 = 64512 of 65536);
+// the producer warpgroup drops to 80 so the two softmax warpgroups can hold 208 each:
+// 256 × 208 + 128 × 80 = 63488 ≤ 64512, and per SM sub-partition 208 + 208 + 80 = 496 ≤ 512
+// per lane.
+constexpr int kSoftmaxRegs = 208;
+constexpr int kProducerRegs = 80;
 constexpr float kRescaleLog2 = 8.0f;
 
 struct AttentionParams {
@@ -60,8 +67,9 @@ struct AttentionSmem {
   static constexpr int kQOffset = 0;
   static constexpr int kKVOffset = kQTiles * kTileBytes;
   static constexpr int kBarOffset = kKVOffset + kStages * kTileBytes;
-  // barriers: q_full, kv_full[S], kv_empty[S], s_full[2], p_ready[2], o_final[2], drain
-  static constexpr int kBars = 1 + 2 * kStages + 6 + 1;
+  // barriers: q_full, kv_full[S], kv_empty[S], s_full[2], p_ready[2][2 halves], o_final[2],
+  // drain
+  static constexpr int kBars = 1 + 2 * kStages + 2 + 4 + 2 + 1;
   static constexpr int kMiscOffset = kBarOffset + kBars * 8;
   static constexpr int kBytes = kMiscOffset + 16;
   static constexpr int kAlloc = kBytes + 1024;  // slack to align the base to 1024 bytes
@@ -87,6 +95,83 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity, int* 
   mbar_wait(bar, parity, reinterpret_cast<volatile int*>(&never), nullptr);
 }
 
+// -------------------------------------------------------------------------- softmax helpers
+// 2^f on [0, 1) by a degree-3 polynomial, coefficients fitted for this kernel (relative-error
+// weighted least squares on 20001 points, Lawson reweighting toward minimax): max relative
+// error 7.6e-5, far below the bf16 rounding P is stored with.
+constexpr float kExp2C0 = 0.99992478f;
+constexpr float kExp2C1 = 0.69583595f;
+constexpr float kExp2C2 = 0.22606595f;
+constexpr float kExp2C3 = 0.07802287f;
+// Pairs of every 8 whose exponentials run on the FMA pipe instead of the MUFU unit. Measured on
+// B200 at the C2 shape (24 heads × 33272 tokens): 0/8 1096 TFLOP/s, 2/8 1028, 4/8 1014, 6/8
+// 944, so the unit is not the binding limit of this schedule and the default keeps MUFU only.
+#ifndef COZY_POLY_PER_EIGHT
+#define COZY_POLY_PER_EIGHT 0
+#endif
+constexpr int kPolyPerEight = COZY_POLY_PER_EIGHT;
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+__device__ __forceinline__ float chunk_max(const uint32_t (&r)[32]) {
+  float m0 = fmaxf(__uint_as_float(r[0]), __uint_as_float(r[1]));
+  float m1 = fmaxf(__uint_as_float(r[2]), __uint_as_float(r[3]));
+#pragma unroll
+  for (int i = 4; i < 32; i += 4) {
+    m0 = fmax3(m0, __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+    m1 = fmax3(m1, __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
+  }
+  return fmaxf(m0, m1);
+}
+
+// Columns past `limit` (chunk-relative; may be negative) become -inf.
+__device__ __forceinline__ void mask_chunk(uint32_t (&r)[32], int limit) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i)
+    if (i > limit) r[i] = 0xff800000u;
+}
+
+// 2^t for a pair with t ≤ 8 on the FMA pipe: t = n + f with n = floor(t) (the round-down add of
+// 1.5·2^23 leaves n in the low mantissa bits), 2^f from the polynomial, n added to the exponent.
+// t is clamped at -120 first: the polynomial's value at f = 0 sits just below 1 (exponent field
+// 126), so the exponent add must stay well clear of the bottom of the range; 2^-120 is zero for
+// any probability sum it joins (masked keys land here).
+__device__ __forceinline__ float2 exp2_poly2(float2 t) {
+  const float2 magic = make_float2(12582912.0f, 12582912.0f);
+  t.x = fmaxf(t.x, -120.0f);
+  t.y = fmaxf(t.y, -120.0f);
+  const float2 r = __fadd2_rd(t, magic);
+  const float2 fl = __fadd2_rn(r, make_float2(-12582912.0f, -12582912.0f));
+  const float2 f = __ffma2_rn(fl, make_float2(-1.0f, -1.0f), t);
+  float2 p = __ffma2_rn(make_float2(kExp2C3, kExp2C3), f, make_float2(kExp2C2, kExp2C2));
+  p = __ffma2_rn(p, f, make_float2(kExp2C1, kExp2C1));
+  p = __ffma2_rn(p, f, make_float2(kExp2C0, kExp2C0));
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(r.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(r.y) << 23)));
+}
+
+// 32 scores -> 32 probabilities 2^(s·scale - m) as 16 packed bf16 pairs, summed into `acc`.
+__device__ __forceinline__ void exp_chunk(const uint32_t (&r)[32], float2 scale2, float2 negm2,
+                                          float2& acc, uint32_t (&pk)[16]) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float2 sv = make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+    const float2 t = __ffma2_rn(sv, scale2, negm2);
+    float2 e;
+    if ((i & 7) < kPolyPerEight) {
+      e = exp2_poly2(t);
+    } else {
+      e = make_float2(ex2_approx(t.x), ex2_approx(t.y));
+    }
+    acc = __fadd2_rn(acc, e);
+    pk[i] = pack_bf16x2(e.x, e.y);
+  }
+}
+
 template <int HD>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
@@ -103,9 +188,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* kv_full = bars + 1;
   uint64_t* kv_empty = bars + 1 + kStages;
   uint64_t* s_full = bars + 1 + 2 * kStages;
-  uint64_t* p_ready = s_full + 2;
-  uint64_t* o_final = s_full + 4;
-  uint64_t* drain = s_full + 6;
+  uint64_t* p_ready = s_full + 2;  // [tile][half]
+  uint64_t* o_final = s_full + 6;
+  uint64_t* drain = s_full + 8;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMiscOffset);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + L::kMiscOffset + 4);
 
@@ -130,7 +215,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
-      mbar_init(&p_ready[s], kBlockM);
+      mbar_init(&p_ready[2 * s], kBlockM);
+      mbar_init(&p_ready[2 * s + 1], kBlockM);
       mbar_init(&o_final[s], 1);
     }
     mbar_init(drain, 1);
@@ -152,6 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp < 8) {
     // ------------------------------------------------------------------ softmax warpgroups
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
     const int s = warp >> 2;
     const int quarter = warp & 3;
     const int q_row = q0 + s * kBlockM + quarter * 32 + lane;
@@ -179,26 +266,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       reg_fence(r1);
       reg_fence(r2);
       reg_fence(r3);
-      float x[128];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        x[i] = __uint_as_float(r0[i]);
-        x[32 + i] = __uint_as_float(r1[i]);
-        x[64 + i] = __uint_as_float(r2[i]);
-        x[96 + i] = __uint_as_float(r3[i]);
-      }
       const int kv0 = j * kBlockN;
       const bool ragged = kv0 + kBlockN > p.seq_k;
       const bool diagonal = p.causal && kv0 + kBlockN - 1 > visible;
       if (ragged || diagonal) {
         const int limit = min(p.seq_k - 1, p.causal ? visible : p.seq_k - 1) - kv0;
-#pragma unroll
-        for (int i = 0; i < 128; ++i)
-          if (i > limit) x[i] = -INFINITY;
+        mask_chunk(r0, limit);
+        mask_chunk(r1, limit - 32);
+        mask_chunk(r2, limit - 64);
+        mask_chunk(r3, limit - 96);
       }
-      float mt = x[0];
-#pragma unroll
-      for (int i = 1; i < 128; ++i) mt = fmaxf(mt, x[i]);
+      // row max: four independent 3-input chains, one per chunk
+      const float mt = fmaxf(fmaxf(chunk_max(r0), chunk_max(r1)), fmaxf(chunk_max(r2), chunk_max(r3)));
       const float m_new = fmaxf(m, mt * scale);
       if (j == 0) {
         m = m_new;
@@ -220,28 +299,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         m = m_new;
       }
       const float mu = (m == -INFINITY) ? 0.f : m;
-      float sum = 0.f;
-      uint32_t pk0[32], pk1[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float a = ex2_approx(fmaf(x[2 * i], scale, -mu));
-        const float c = ex2_approx(fmaf(x[2 * i + 1], scale, -mu));
-        sum += a + c;
-        pk0[i] = pack_bf16x2(a, c);
-      }
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float a = ex2_approx(fmaf(x[64 + 2 * i], scale, -mu));
-        const float c = ex2_approx(fmaf(x[64 + 2 * i + 1], scale, -mu));
-        sum += a + c;
-        pk1[i] = pack_bf16x2(a, c);
-      }
-      l += sum;
-      tmem_st32(tS + 0, pk0);
-      tmem_st32(tS + 32, pk1);
+      const float2 scale2 = make_float2(scale, scale);
+      const float2 negm2 = make_float2(-mu, -mu);
+      float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+      uint32_t pk[16];
+      // first half of P (keys 0..63): the MMA starts its product while the rest is formed
+      exp_chunk(r0, scale2, negm2, acc0, pk);
+      tmem_st16(tS + 0, pk);
+      exp_chunk(r1, scale2, negm2, acc1, pk);
+      tmem_st16(tS + 16, pk);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&p_ready[s]);
+      mbar_arrive(&p_ready[2 * s]);
+      exp_chunk(r2, scale2, negm2, acc0, pk);
+      tmem_st16(tS + 32, pk);
+      exp_chunk(r3, scale2, negm2, acc1, pk);
+      tmem_st16(tS + 48, pk);
+      const float2 acc = __fadd2_rn(acc0, acc1);
+      l += acc.x + acc.y;
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&p_ready[2 * s + 1]);
     }
     // ------------------------------------------------------------------------- epilogue
     if (ok && n_kv > 0) {
@@ -249,7 +327,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
     }
     if (ok) {
-      const float inv = (l > 0.f) ? 1.f / l : 0.f;
+      // rows that saw no key (bottom-right causal with seq_q > seq_k) are written as zeros
+      const float inv = (l > 0.f && m != -INFINITY) ? 1.f / l : 0.f;
       const bool valid = q_row < p.seq_q;
       __nv_bfloat16* dst = p.out + static_cast<long long>(b) * p.out_b +
                            static_cast<long long>(q_row) * p.out_s +
@@ -281,6 +360,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 8) {
     // ------------------------------------------------------------------------ TMA producer
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
     if (lane == 0) {
       mbar_expect_tx(q_full, kQTiles * L::kTileBytes);
       for (int s = 0; s < kQTiles; ++s)
@@ -308,8 +388,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         drain_wait(&kv_full[i % kStages], (i / kStages) & 1, p.status);
     }
     __syncwarp();
-  } else {
+  } else if (warp == 9) {
     // ------------------------------------------------------------------------- MMA issuer
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
     if (lane == 0 && n_kv > 0) {
       constexpr uint32_t kIdescQK = idesc_bf16_f32(kBlockM, kBlockN, false);
       constexpr uint32_t kIdescPV = idesc_bf16_f32(kBlockM, HD, true);
@@ -327,10 +408,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                  smem_desc_sw128(ka + off, 16, 1024), kIdescQK, kk > 0 ? 1u : 0u);
         }
       };
-      auto issue_pv = [&](int s, int stage, bool accumulate) {
+      auto issue_pv = [&](int s, int stage, bool accumulate, int half) {
         const uint32_t va = kv_base + stage * L::kTileBytes;
 #pragma unroll
-        for (int kk = 0; kk < kBlockN / 16; ++kk) {
+        for (int kk = half * (kBlockN / 32); kk < (half + 1) * (kBlockN / 32); ++kk) {
           // V is MN-major for this product: 16 key rows per step (2048 bytes); the two
           // 64-column halves of the head dimension are one box (16 KB) apart.
           mma_ts(tmem + 256u + s * HD, tmem + s * kBlockN + kk * 8,
@@ -355,7 +436,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!(ok = mbar_wait(&kv_full[sv], (iv / kStages) & 1, abort, p.status))) break;
         if (!(ok = mbar_wait(&p_ready[0], j & 1, abort, p.status))) break;
         tc_fence_after();
-        issue_pv(0, sv, j > 0);
+        issue_pv(0, sv, j > 0, 0);
+        if (!(ok = mbar_wait(&p_ready[1], j & 1, abort, p.status))) break;
+        tc_fence_after();
+        issue_pv(0, sv, j > 0, 1);
         if (!more) mma_commit(&o_final[0]);
         if (more) {
           if (!(ok = mbar_wait(&kv_full[sk], (ik / kStages) & 1, abort, p.status))) break;
@@ -363,9 +447,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           issue_qk(0, sk);
           mma_commit(&s_full[0]);
         }
-        if (!(ok = mbar_wait(&p_ready[1], j & 1, abort, p.status))) break;
+        if (!(ok = mbar_wait(&p_ready[2], j & 1, abort, p.status))) break;
         tc_fence_after();
-        issue_pv(1, sv, j > 0);
+        issue_pv(1, sv, j > 0, 0);
+        if (!(ok = mbar_wait(&p_ready[3], j & 1, abort, p.status))) break;
+        tc_fence_after();
+        issue_pv(1, sv, j > 0, 1);
         mma_commit(&kv_empty[sv]);
         if (!more) mma_commit(&o_final[1]);
         if (more) {
@@ -379,6 +466,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       drain_wait(drain, 0, p.status);
     }
     __syncwarp();
+  } else {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
   }
 
   tc_fence_before();
