@@ -7,7 +7,7 @@
 //   warps 0-3   softmax for query tile 0 (thread = one query row = one TMEM lane)
 //   warps 4-7   softmax for query tile 1
 //   warp  8     TMA producer: Q once, then K_j, V_j into a ring of shared-memory slots
-//   warp  9     MMA issuer (one thread): S = Q·Kᵀ into TMEM, O += P·V with P read from TMEM
+//   warp  9     MMA issuer (one elected lane): S = Q·Kᵀ into TMEM, O += P·V, P read from TMEM
 //   warps 10-11 idle (they complete the third warpgroup the register split needs)
 //
 // Tensor memory (512 columns × 128 lanes of 32 bits):
@@ -85,6 +85,21 @@ __device__ __forceinline__ void reg_fence(uint32_t (&r)[32]) {
                  "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
                  "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]),
                  "+r"(r[30]), "+r"(r[31]));
+}
+
+// One lane of a converged warp (the same lane every time).
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
+// mbar_wait by every lane of a warp, with one answer for the whole warp.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                          int* status) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, status));
 }
 
 // A wait that ignores the CTA's abort flag but still ends at the time limit: used to drain the
@@ -360,109 +375,133 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 8) {
     // ------------------------------------------------------------------------ TMA producer
+    // The whole warp walks the schedule (warp-uniform control flow); one elected lane issues.
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
-    if (lane == 0) {
+    if (elect_one()) {
       mbar_expect_tx(q_full, kQTiles * L::kTileBytes);
       for (int s = 0; s < kQTiles; ++s)
         for (int box = 0; box < L::kBoxes; ++box)
           tma_load_4d(sQ + s * L::kTileBytes + box * L::kBoxBytes, &tm_q, q_full, box * 64,
                       q0 + s * kBlockM, head, b);
-      int issued = 0;
-      for (int i = 0; i < 2 * n_kv; ++i) {
-        const int stage = i % kStages;
-        if (i >= kStages && !mbar_wait(&kv_empty[stage], ((i / kStages) - 1) & 1, abort,
-                                       p.status))
-          break;
-        const int j = i >> 1;
-        const CUtensorMap* map = (i & 1) ? &tm_v : &tm_k;
+    }
+    __syncwarp();
+    int issued = 0;
+    for (int i = 0; i < 2 * n_kv; ++i) {
+      const int stage = i % kStages;
+      if (i >= kStages && !warp_wait(&kv_empty[stage], ((i / kStages) - 1) & 1, abort, p.status))
+        break;
+      const int j = i >> 1;
+      const CUtensorMap* map = (i & 1) ? &tm_v : &tm_k;
+      if (elect_one()) {
         mbar_expect_tx(&kv_full[stage], L::kTileBytes);
         for (int box = 0; box < L::kBoxes; ++box)
           tma_load_4d(sKV + stage * L::kTileBytes + box * L::kBoxBytes, map, &kv_full[stage],
                       box * 64, j * kBlockN, kv_head, b);
-        issued = i + 1;
       }
-      // Every copy this CTA issued lands before the CTA unwinds (already true on the normal
-      // path, where the MMA thread waited for each one).
-      drain_wait(q_full, 0, p.status);
-      for (int i = max(0, issued - kStages); i < issued; ++i)
-        drain_wait(&kv_full[i % kStages], (i / kStages) & 1, p.status);
+      __syncwarp();
+      issued = i + 1;
     }
+    // Every copy this CTA issued lands before the CTA unwinds (already true on the normal path,
+    // where the MMA warp waited for each one).
+    drain_wait(q_full, 0, p.status);
+    for (int i = max(0, issued - kStages); i < issued; ++i)
+      drain_wait(&kv_full[i % kStages], (i / kStages) & 1, p.status);
     __syncwarp();
   } else if (warp == 9) {
     // ------------------------------------------------------------------------- MMA issuer
+    // Warp-uniform schedule, one elected lane issuing every MMA and commit (a commit tracks
+    // the MMAs of the thread that executes it, and elect.sync picks the same lane each time in
+    // a converged warp). Descriptors are a base per operand plus compile-time offsets.
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
-    if (lane == 0 && n_kv > 0) {
+    if (n_kv > 0) {
       constexpr uint32_t kIdescQK = idesc_bf16_f32(kBlockM, kBlockN, false);
       constexpr uint32_t kIdescPV = idesc_bf16_f32(kBlockM, HD, true);
-      const uint32_t q_base = smem_u32(sQ);
-      const uint32_t kv_base = smem_u32(sKV);
+      const uint64_t dq = smem_desc_sw128(smem_u32(sQ), 16, 1024);
+      const uint64_t dk = smem_desc_sw128(smem_u32(sKV), 16, 1024);
+      const uint64_t dv = smem_desc_sw128(smem_u32(sKV), L::kBoxBytes, 1024);
+      constexpr uint64_t kTileStep = L::kTileBytes >> 4;  // descriptor units (16 bytes)
       auto issue_qk = [&](int s, int stage) {
-        const uint32_t qa = q_base + s * L::kTileBytes;
-        const uint32_t ka = kv_base + stage * L::kTileBytes;
+        const uint64_t qa = dq + static_cast<uint64_t>(s) * kTileStep;
+        const uint64_t ka = dk + static_cast<uint64_t>(stage) * kTileStep;
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
           // K-major 128-byte swizzle: 16-element steps move 32 bytes inside a row's atom;
           // every 4 steps move to the next 64-column box.
-          const uint32_t off = (kk >> 2) * L::kBoxBytes + (kk & 3) * 32;
-          mma_ss(tmem + s * kBlockN, smem_desc_sw128(qa + off, 16, 1024),
-                 smem_desc_sw128(ka + off, 16, 1024), kIdescQK, kk > 0 ? 1u : 0u);
+          const uint64_t off = static_cast<uint64_t>(((kk >> 2) * L::kBoxBytes + (kk & 3) * 32) >> 4);
+          mma_ss(tmem + s * kBlockN, qa + off, ka + off, kIdescQK, kk > 0 ? 1u : 0u);
         }
       };
-      auto issue_pv = [&](int s, int stage, bool accumulate, int half) {
-        const uint32_t va = kv_base + stage * L::kTileBytes;
+      auto issue_pv = [&](int s, int stage, uint32_t accumulate, int half) {
+        const uint64_t va = dv + static_cast<uint64_t>(stage) * kTileStep;
 #pragma unroll
         for (int kk = half * (kBlockN / 32); kk < (half + 1) * (kBlockN / 32); ++kk) {
           // V is MN-major for this product: 16 key rows per step (2048 bytes); the two
           // 64-column halves of the head dimension are one box (16 KB) apart.
           mma_ts(tmem + 256u + s * HD, tmem + s * kBlockN + kk * 8,
-                 smem_desc_sw128(va + kk * 2048, L::kBoxBytes, 1024), kIdescPV,
-                 (accumulate || kk > 0) ? 1u : 0u);
+                 va + static_cast<uint64_t>((kk * 2048) >> 4), kIdescPV,
+                 kk > 0 ? 1u : accumulate);
         }
       };
-      bool ok = mbar_wait(q_full, 0, abort, p.status);
-      if (ok) ok = mbar_wait(&kv_full[0], 0, abort, p.status);
+      bool ok = warp_wait(q_full, 0, abort, p.status);
+      if (ok) ok = warp_wait(&kv_full[0], 0, abort, p.status);
       if (ok) {
         tc_fence_after();
-        issue_qk(0, 0);
-        mma_commit(&s_full[0]);
-        issue_qk(1, 0);
-        mma_commit(&s_full[1]);
-        mma_commit(&kv_empty[0]);
+        if (elect_one()) {
+          issue_qk(0, 0);
+          mma_commit(&s_full[0]);
+          issue_qk(1, 0);
+          mma_commit(&s_full[1]);
+          mma_commit(&kv_empty[0]);
+        }
+        __syncwarp();
       }
       for (int j = 0; ok && j < n_kv; ++j) {
         const int iv = 2 * j + 1, ik = 2 * j + 2;
         const int sv = iv % kStages, sk = ik % kStages;
         const bool more = j + 1 < n_kv;
-        if (!(ok = mbar_wait(&kv_full[sv], (iv / kStages) & 1, abort, p.status))) break;
-        if (!(ok = mbar_wait(&p_ready[0], j & 1, abort, p.status))) break;
+        const uint32_t acc = j > 0 ? 1u : 0u;
+        if (!(ok = warp_wait(&kv_full[sv], (iv / kStages) & 1, abort, p.status))) break;
+        if (!(ok = warp_wait(&p_ready[0], j & 1, abort, p.status))) break;
         tc_fence_after();
-        issue_pv(0, sv, j > 0, 0);
-        if (!(ok = mbar_wait(&p_ready[1], j & 1, abort, p.status))) break;
+        if (elect_one()) issue_pv(0, sv, acc, 0);
+        __syncwarp();
+        if (!(ok = warp_wait(&p_ready[1], j & 1, abort, p.status))) break;
         tc_fence_after();
-        issue_pv(0, sv, j > 0, 1);
-        if (!more) mma_commit(&o_final[0]);
+        if (elect_one()) {
+          issue_pv(0, sv, acc, 1);
+          if (!more) mma_commit(&o_final[0]);
+        }
+        __syncwarp();
         if (more) {
-          if (!(ok = mbar_wait(&kv_full[sk], (ik / kStages) & 1, abort, p.status))) break;
+          if (!(ok = warp_wait(&kv_full[sk], (ik / kStages) & 1, abort, p.status))) break;
           tc_fence_after();
-          issue_qk(0, sk);
-          mma_commit(&s_full[0]);
+          if (elect_one()) {
+            issue_qk(0, sk);
+            mma_commit(&s_full[0]);
+          }
+          __syncwarp();
         }
-        if (!(ok = mbar_wait(&p_ready[2], j & 1, abort, p.status))) break;
+        if (!(ok = warp_wait(&p_ready[2], j & 1, abort, p.status))) break;
         tc_fence_after();
-        issue_pv(1, sv, j > 0, 0);
-        if (!(ok = mbar_wait(&p_ready[3], j & 1, abort, p.status))) break;
+        if (elect_one()) issue_pv(1, sv, acc, 0);
+        __syncwarp();
+        if (!(ok = warp_wait(&p_ready[3], j & 1, abort, p.status))) break;
         tc_fence_after();
-        issue_pv(1, sv, j > 0, 1);
-        mma_commit(&kv_empty[sv]);
-        if (!more) mma_commit(&o_final[1]);
-        if (more) {
-          issue_qk(1, sk);
-          mma_commit(&s_full[1]);
-          mma_commit(&kv_empty[sk]);
+        if (elect_one()) {
+          issue_pv(1, sv, acc, 1);
+          mma_commit(&kv_empty[sv]);
+          if (!more) mma_commit(&o_final[1]);
+          if (more) {
+            issue_qk(1, sk);
+            mma_commit(&s_full[1]);
+            mma_commit(&kv_empty[sk]);
+          }
         }
+        __syncwarp();
       }
-      // Every MMA this thread issued completes before TMEM is released.
-      mma_commit(drain);
+      // Every MMA this warp issued completes before TMEM is released.
+      if (elect_one()) mma_commit(drain);
+      __syncwarp();
       drain_wait(drain, 0, p.status);
     }
     __syncwarp();
