@@ -118,11 +118,11 @@ constexpr float kExp2C0 = 0.99992478f;
 constexpr float kExp2C1 = 0.69583595f;
 constexpr float kExp2C2 = 0.22606595f;
 constexpr float kExp2C3 = 0.07802287f;
-// Pairs of every 8 whose exponentials run on the FMA pipe instead of the MUFU unit. Measured on
-// B200 at the C2 shape (24 heads × 33272 tokens): 0/8 1096 TFLOP/s, 2/8 1028, 4/8 1014, 6/8
-// 944, so the unit is not the binding limit of this schedule and the default keeps MUFU only.
+// Pairs of every 8 whose exponentials run on the FMA pipe instead of the MUFU unit (16 results
+// per clock per SM). Measured on B200 at the C2 shape (24 heads × 33272 tokens, elected MMA
+// warp): 0/8 1201-1219 TFLOP/s, 1/8 1232, 2/8 1253, 3/8 1234, 4/8 1137.
 #ifndef COZY_POLY_PER_EIGHT
-#define COZY_POLY_PER_EIGHT 0
+#define COZY_POLY_PER_EIGHT 2
 #endif
 constexpr int kPolyPerEight = COZY_POLY_PER_EIGHT;
 
