@@ -1,0 +1,107 @@
+"""The exchange over real NCCL between GPU processes (one per GPU), against the reference's golden
+outputs and the oracle. Needs two or more GPUs; skipped otherwise.
+
+Each case spawns W processes (W ≤ visible GPUs), every rank passes its `tensor_split` rows and
+the rows come from the store meeting (no `rows` argument), as the reference's exchange does.
+NVLS is off (`NCCL_NVLS_ENABLE=0`), as the reference's group formation sets it.
+"""
+
+import os
+import socket
+import tempfile
+
+import pytest
+import torch
+
+import oracle
+from tests._golden import load, tensor, ulysses_cases
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+MAX_ABS, MEAN_ABS = 2e-2, 2e-3
+
+
+def _gpus() -> int:
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+def _port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank(rank, world, port, inputs, causal, outdir, rope_args):
+    import torch.distributed as dist
+
+    from cozy_runtime_b200 import rope as rope_mod
+    from cozy_runtime_b200 import ulysses
+
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    device = torch.device("cuda", rank)
+    torch.cuda.set_device(device)
+    dist.init_process_group(
+        "nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+        device_id=device,
+    )
+    q, k, v = (torch.tensor_split(t, world, dim=1)[rank].contiguous().to(device) for t in inputs)
+    spec = None
+    if rope_args is not None:
+        spec = rope_mod.axial(rope_args[0], (44, 42, 42), after=rope_args[1]).to(device)
+    out = ulysses.exchange(q, k, v, dist.group.WORLD, None, causal=causal, rope=spec)
+    out2 = ulysses.exchange(q, k, v, dist.group.WORLD, None, causal=causal, rope=spec)
+    torch.cuda.synchronize()
+    assert torch.equal(out, out2), "two calls differ"
+    torch.save(out.cpu(), os.path.join(outdir, f"{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _run(inputs, world, causal=False, rope_args=None) -> torch.Tensor:
+    import torch.multiprocessing as mp
+
+    with tempfile.TemporaryDirectory() as tmp:
+        mp.spawn(_rank, args=(world, _port(), inputs, causal, tmp, rope_args), nprocs=world,
+                 join=True)
+        return torch.cat([torch.load(os.path.join(tmp, f"{r}.pt")) for r in range(world)], dim=1)
+
+
+def _check(got, want):
+    err = (got.float() - want.float()).abs()
+    assert err.max().item() <= MAX_ABS, f"max-abs {err.max().item():.3e}"
+    assert err.mean().item() <= MEAN_ABS, f"mean-abs {err.mean().item():.3e}"
+
+
+@pytest.mark.parametrize("name", ulysses_cases())
+def test_nccl_exchange_matches_reference_golden(name):
+    case = load(name)
+    world = int(case["world"])
+    if world < 2 or world > _gpus():
+        pytest.skip(f"needs {world} GPUs")
+    inputs = tuple(tensor(case[key]) for key in ("q", "k", "v"))
+    got = _run(inputs, world, causal=bool(case["causal"]))
+    _check(got, tensor(case["out"]).float())
+
+
+@pytest.mark.parametrize(
+    "world,hq,hkv,causal,rotate",
+    [(2, 8, 8, False, True), (4, 8, 2, True, False), (8, 8, 8, False, True), (8, 32, 8, True, False),
+     (3, 5, 5, False, True)],
+)
+def test_nccl_exchange_against_oracle(world, hq, hkv, causal, rotate):
+    if world > _gpus():
+        pytest.skip(f"needs {world} GPUs")
+    from cozy_runtime_b200 import rope as rope_mod
+
+    g = torch.Generator().manual_seed(world + hq)
+    grid, text = (2, 6, 10), 17
+    seq = 2 * 6 * 10 + text
+    q = torch.randn(1, seq, hq, 128, generator=g).to(torch.bfloat16)
+    k = torch.randn(1, seq, hkv, 128, generator=g).to(torch.bfloat16)
+    v = torch.randn(1, seq, hkv, 128, generator=g).to(torch.bfloat16)
+    got = _run((q, k, v), world, causal=causal, rope_args=(grid, text) if rotate else None)
+    if rotate:
+        spec = rope_mod.axial(grid, (44, 42, 42), after=text)
+        q, k = (oracle.head_norm_rope(t.float(), spec.cos, spec.sin, rotary=128, interleaved=True,
+                                      normalize=False).to(torch.bfloat16) for t in (q, k))
+    _check(got, oracle.attention_fp32(q, k, v, causal=causal))
