@@ -61,6 +61,24 @@ class HeadMap(Structure):
     _fields_ = [("group", c_int), ("q_base", c_int), ("kv_base", c_int)]
 
 
+class Scatter(Structure):
+    """`CozyScatter`."""
+
+    _fields_ = [
+        ("world", c_int),
+        ("head_offset", c_int),
+        ("row_start", c_int * (MAX_PEERS + 1)),
+        ("out", c_void_p * MAX_PEERS),
+        ("strides", (c_longlong * 3) * MAX_PEERS),
+    ]
+
+
+class PeerSlots(Structure):
+    """`CozyPeerSlots`."""
+
+    _fields_ = [("count", c_int), ("slot", c_void_p * MAX_PEERS)]
+
+
 class CudaCallError(RuntimeError):
     """A library entry point returned a non-zero cudaError_t."""
 
@@ -77,7 +95,7 @@ SIGNATURES = {
     "cozy_attention_fwd": (
         [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int,
          POINTER(c_longlong), POINTER(c_longlong), POINTER(c_longlong), POINTER(c_longlong),
-         POINTER(HeadMap), c_int, c_float, c_void_p, c_uint64],
+         POINTER(HeadMap), POINTER(Scatter), c_int, c_float, c_void_p, c_uint64],
         c_int,
     ),
     "cozy_ulysses_pack": (
@@ -89,6 +107,13 @@ SIGNATURES = {
          POINTER(c_longlong), c_uint64],
         c_int,
     ),
+    "cozy_ipc_alloc": ([ctypes.c_ulonglong, POINTER(c_void_p), c_void_p], c_int),
+    "cozy_ipc_open": ([c_void_p, POINTER(c_void_p)], c_int),
+    "cozy_ipc_close": ([c_void_p], c_int),
+    "cozy_ipc_free": ([c_void_p], c_int),
+    "cozy_ipc_handle_bytes": ([], c_int),
+    "cozy_peer_signal": ([POINTER(PeerSlots), c_longlong, c_uint64], c_int),
+    "cozy_peer_wait": ([c_void_p, c_int, c_longlong, c_longlong, c_void_p, c_uint64], c_int),
     "cozy_error_name": ([c_int], c_char_p),
     "cozy_abi_version": ([], c_int),
 }

@@ -59,7 +59,7 @@ def refusal(query: Tensor, key: Tensor, options: dict) -> str:
 
 
 def attention_into(
-    out: Tensor,
+    out: Tensor | None,
     query: Tensor,
     key: Tensor,
     value: Tensor,
@@ -67,19 +67,24 @@ def attention_into(
     causal: bool = False,
     scale: float | None = None,
     head_map: tuple[int, int, int] | None = None,
+    scatter: _lib.Scatter | None = None,
 ) -> None:
     """softmax(QKᵀ·scale)V of [B, Sq, Hq, D] queries over [B, Sk, Hkv, D] keys/values, into
     `out` ([B, Sq, Hq, D], any strides with D contiguous), on the current stream.
-    `head_map` = (group, q_base, kv_base): query head h reads key head (h+q_base)//group-kv_base."""
+    `head_map` = (group, q_base, kv_base): query head h reads key head (h+q_base)//group-kv_base.
+    `scatter`: rows go to their owners' outputs instead (`out` is then None)."""
     batch, sq, hq, dim = query.shape
     sk, hkv = key.shape[1], key.shape[2]
     scale = 1.0 / math.sqrt(dim) if scale is None else float(scale)
     mapping = None if head_map is None else ctypes.byref(_lib.HeadMap(*head_map))
     code = _lib.load().cozy_attention_fwd(
-        query.data_ptr(), key.data_ptr(), value.data_ptr(), out.data_ptr(),
+        query.data_ptr(), key.data_ptr(), value.data_ptr(),
+        None if out is None else out.data_ptr(),
         batch, sq, sk, hq, hkv, dim,
-        _strides(query), _strides(key), _strides(value), _strides(out),
-        mapping, int(causal), scale, status_word(query.device).data_ptr(),
+        _strides(query), _strides(key), _strides(value),
+        None if out is None else _strides(out),
+        mapping, None if scatter is None else ctypes.byref(scatter), int(causal), scale,
+        status_word(query.device).data_ptr(),
         torch.cuda.current_stream(query.device).cuda_stream,
     )
     _lib.check("cozy_attention_fwd", code)

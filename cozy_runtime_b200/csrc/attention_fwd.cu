@@ -57,6 +57,11 @@ struct AttentionParams {
   __nv_bfloat16* out;
   long long out_s, out_h, out_b;  // element strides of O
   int* status;
+  // scatter: rows go to their owners' outputs (possibly other GPUs' memory) instead of `out`
+  int scatter, world, head_offset;
+  int row_start[COZY_MAX_PEERS + 1];
+  __nv_bfloat16* outs[COZY_MAX_PEERS];
+  long long outs_strides[COZY_MAX_PEERS][3];
 };
 
 template <int HD>
@@ -345,9 +350,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       // rows that saw no key (bottom-right causal with seq_q > seq_k) are written as zeros
       const float inv = (l > 0.f && m != -INFINITY) ? 1.f / l : 0.f;
       const bool valid = q_row < p.seq_q;
-      __nv_bfloat16* dst = p.out + static_cast<long long>(b) * p.out_b +
-                           static_cast<long long>(q_row) * p.out_s +
-                           static_cast<long long>(head) * p.out_h;
+      __nv_bfloat16* dst;
+      if (p.scatter) {
+        // the row's owner: the rank whose sequence rows contain it (rows are contiguous per rank)
+        int owner = 0;
+        while (owner + 1 < p.world && q_row >= p.row_start[owner + 1]) ++owner;
+        dst = p.outs[owner] + static_cast<long long>(b) * p.outs_strides[owner][2] +
+              static_cast<long long>(q_row - p.row_start[owner]) * p.outs_strides[owner][0] +
+              static_cast<long long>(head + p.head_offset) * p.outs_strides[owner][1];
+      } else {
+        dst = p.out + static_cast<long long>(b) * p.out_b +
+              static_cast<long long>(q_row) * p.out_s + static_cast<long long>(head) * p.out_h;
+      }
 #pragma unroll
       for (int c = 0; c < HD / 32; ++c) {
         uint32_t o[32];
@@ -577,8 +591,8 @@ int attention_forward(const void* q, const void* k, const void* v, void* out, in
                       int seq_q, int seq_k, int heads_q, int heads_kv, int head_dim,
                       const long long* q_strides, const long long* k_strides,
                       const long long* v_strides, const long long* o_strides,
-                      const CozyHeadMap* head_map, int causal, float scale, int* status,
-                      cudaStream_t stream) {
+                      const CozyHeadMap* head_map, const CozyScatter* scatter, int causal,
+                      float scale, int* status, cudaStream_t stream) {
   if (head_dim != 64 && head_dim != 128) return cudaErrorNotSupported;
   if (batch <= 0 || seq_q <= 0 || seq_k <= 0 || heads_q <= 0 || heads_kv <= 0)
     return cudaErrorInvalidValue;
@@ -594,13 +608,27 @@ int attention_forward(const void* q, const void* k, const void* v, void* out, in
   const int kv_last = (heads_q - 1 + map.q_base) / map.group - map.kv_base;
   if (kv_first < 0 || kv_last >= heads_kv) return cudaErrorInvalidValue;
   if (batch > 65535 || heads_q > 65535) return cudaErrorInvalidValue;
-  const void* ptrs[4] = {q, k, v, out};
+  const void* ptrs[4] = {q, k, v, scatter ? q : out};
   for (const void* ptr : ptrs)
     if (ptr == nullptr || reinterpret_cast<uintptr_t>(ptr) % 16 != 0) return cudaErrorInvalidValue;
-  const long long* all[4] = {q_strides, k_strides, v_strides, o_strides};
+  const long long* all[4] = {q_strides, k_strides, v_strides, scatter ? q_strides : o_strides};
   for (const long long* st : all)
     for (int i = 0; i < 3; ++i)
       if (st[i] <= 0 || st[i] % 8 != 0) return cudaErrorInvalidValue;
+  if (scatter != nullptr) {
+    if (scatter->world < 1 || scatter->world > COZY_MAX_PEERS || scatter->head_offset < 0)
+      return cudaErrorInvalidValue;
+    if (scatter->row_start[0] != 0 || scatter->row_start[scatter->world] != seq_q)
+      return cudaErrorInvalidValue;
+    for (int w = 0; w < scatter->world; ++w) {
+      if (scatter->row_start[w + 1] < scatter->row_start[w]) return cudaErrorInvalidValue;
+      if (scatter->row_start[w + 1] == scatter->row_start[w]) continue;
+      if (scatter->out[w] == nullptr || reinterpret_cast<uintptr_t>(scatter->out[w]) % 16)
+        return cudaErrorInvalidValue;
+      for (int i = 0; i < 3; ++i)
+        if (scatter->strides[w][i] <= 0 || scatter->strides[w][i] % 8) return cudaErrorInvalidValue;
+    }
+  }
   CUtensorMap mq, mk, mv;
   int e;
   if ((e = make_map(&mq, q, head_dim, seq_q, heads_q, batch, q_strides[0], q_strides[1],
@@ -626,10 +654,23 @@ int attention_forward(const void* q, const void* k, const void* v, void* out, in
   p.q_blocks = (seq_q + kQTiles * kBlockM - 1) / (kQTiles * kBlockM);
   p.scale_log2 = scale * 1.4426950408889634f;
   p.out = static_cast<__nv_bfloat16*>(out);
-  p.out_s = o_strides[0];
-  p.out_h = o_strides[1];
-  p.out_b = o_strides[2];
+  p.out_s = o_strides ? o_strides[0] : 0;
+  p.out_h = o_strides ? o_strides[1] : 0;
+  p.out_b = o_strides ? o_strides[2] : 0;
   p.status = status;
+  p.scatter = 0;
+  p.world = 1;
+  p.head_offset = 0;
+  if (scatter != nullptr) {
+    p.scatter = 1;
+    p.world = scatter->world;
+    p.head_offset = scatter->head_offset;
+    for (int w = 0; w <= scatter->world; ++w) p.row_start[w] = scatter->row_start[w];
+    for (int w = 0; w < scatter->world; ++w) {
+      p.outs[w] = static_cast<__nv_bfloat16*>(scatter->out[w]);
+      for (int i = 0; i < 3; ++i) p.outs_strides[w][i] = scatter->strides[w][i];
+    }
+  }
   if (head_dim == 128) return launch<128>(mq, mk, mv, p, stream);
   return launch<64>(mq, mk, mv, p, stream);
 }

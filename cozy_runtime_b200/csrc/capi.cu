@@ -11,8 +11,8 @@ int attention_forward(const void* q, const void* k, const void* v, void* out, in
                       int seq_q, int seq_k, int heads_q, int heads_kv, int head_dim,
                       const long long* q_strides, const long long* k_strides,
                       const long long* v_strides, const long long* o_strides,
-                      const CozyHeadMap* head_map, int causal, float scale, int* status,
-                      cudaStream_t stream);
+                      const CozyHeadMap* head_map, const CozyScatter* scatter, int causal,
+                      float scale, int* status, cudaStream_t stream);
 int ulysses_pack(const CozyPackTensor* tensors, int count, int world, int rows, int batch,
                  int head_dim, const CozyRope* rope, cudaStream_t stream);
 int ulysses_land(const void* returned, int world, int rows, int batch, int head_dim,
@@ -28,11 +28,12 @@ int cozy_attention_fwd(const void* q, const void* k, const void* v, void* out, i
                        int seq_q, int seq_k, int heads_q, int heads_kv, int head_dim,
                        const long long* q_strides, const long long* k_strides,
                        const long long* v_strides, const long long* o_strides,
-                       const CozyHeadMap* head_map, int causal, float scale, int* status,
-                       uintptr_t stream) {
-  if (!q_strides || !k_strides || !v_strides || !o_strides) return cudaErrorInvalidValue;
+                       const CozyHeadMap* head_map, const CozyScatter* scatter, int causal,
+                       float scale, int* status, uintptr_t stream) {
+  if (!q_strides || !k_strides || !v_strides || (!o_strides && !scatter))
+    return cudaErrorInvalidValue;
   return cozy::attention_forward(q, k, v, out, batch, seq_q, seq_k, heads_q, heads_kv, head_dim,
-                                 q_strides, k_strides, v_strides, o_strides, head_map, causal, scale,
+                                 q_strides, k_strides, v_strides, o_strides, head_map, scatter, causal, scale,
                                  status, as_stream(stream));
 }
 

@@ -1,0 +1,209 @@
+"""The in-kernel NVLink exchange of one process group: buffers every GPU of the node maps, and the
+arrival flags the ranks signal each other through.
+
+It replaces the reference's copy-engine exchange (`src/cozy_runtime/internal/parallel/
+copy_engine.py:136-251`: a mapped receive buffer per GPU, NCCL all-reduce barriers around DMA
+copies) with stores issued by the kernels themselves: the first stage writes each peer's heads
+straight into that peer's receive buffer, the attention writes each output row straight into its
+owner's landing buffer, and a 64-bit flag per (kind, source) in the receiver's memory says that a
+call's writes have landed (`cozy_peer_signal` / `cozy_peer_wait`, bounded waits).
+
+Receive and landing buffers are double-buffered by call parity. A rank writes call n into a
+peer's set n % 2 only after it saw every rank's first-stage flag of call n, so every peer has
+finished call n - 1, and with it every read of set n % 2 from call n - 2: no extra barrier.
+
+Buffers are mapped when a group first runs a shape (all ranks together: they agree on sizes,
+which follow from the agreed rows) and grow, never shrink, as shapes grow.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+import weakref
+
+import torch
+import torch.distributed as dist
+
+from cozy_runtime_b200 import _lib
+
+#: How long a rank waits for its peers' writes before it reports a peer timeout (status 2).
+WAIT_LIMIT_NS = 10_000_000_000
+#: flag kinds: a call's Q/K/V have landed; its output rows have landed
+QKV, OUT = 0, 1
+
+
+class _Ptr:
+    """A CUDA array interface over raw device memory, to view it as a torch tensor."""
+
+    def __init__(self, ptr: int, numel: int) -> None:
+        self.__cuda_array_interface__ = {
+            "shape": (numel,),
+            "typestr": "<i2",
+            "data": (ptr, False),
+            "version": 3,
+            "strides": None,
+            "stream": None,
+        }
+
+
+def _tensor(ptr: int, numel: int, device: torch.device) -> torch.Tensor:
+    return torch.as_tensor(_Ptr(ptr, numel), device=device).view(torch.bfloat16)
+
+
+class _Alloc:
+    """One IPC-shareable allocation of this rank."""
+
+    def __init__(self, nbytes: int) -> None:
+        lib = _lib.load()
+        self.ptr = ctypes.c_void_p()
+        self.handle = ctypes.create_string_buffer(lib.cozy_ipc_handle_bytes())
+        _lib.check("cozy_ipc_alloc", lib.cozy_ipc_alloc(nbytes, ctypes.byref(self.ptr), self.handle))
+        self.nbytes = nbytes
+
+    def free(self) -> None:
+        if self.ptr.value:
+            _lib.load().cozy_ipc_free(self.ptr)
+            self.ptr = ctypes.c_void_p()
+
+
+class PeerGroup:
+    """One rank's view of a group's mapped buffers."""
+
+    #: buffers per set: q, k, v receive; landing
+    KINDS = ("q", "k", "v", "land")
+
+    def __init__(self, handle, device: torch.device) -> None:
+        self.handle = handle
+        self.device = device
+        self.rank = dist.get_rank(handle)
+        self.world = dist.get_world_size(handle)
+        self.seq = 0
+        self.lock = threading.Lock()
+        self.sizes: tuple[int, ...] | None = None  # elements per kind, this rank
+        self.local: dict[tuple[int, str], _Alloc] = {}
+        self.peer_ptrs: dict[tuple[int, int, str], int] = {}  # (peer, set, kind) -> address
+        self.opened: list[ctypes.c_void_p] = []
+        self.views: dict[tuple[int, str], torch.Tensor] = {}
+        self.flags = _Alloc(2 * self.world * 8)
+        self.peer_flags = self._exchange_handles({("flags", 0): self.flags})
+        self.flag_view = {}
+
+    # ------------------------------------------------------------------ mapping
+    def _exchange_handles(self, allocs: dict) -> dict:
+        """All-gather this rank's handles; open every peer's; return {(peer, key): address}."""
+        mine = {key: bytes(a.handle.raw) for key, a in allocs.items()}
+        gathered: list = [None] * self.world
+        dist.all_gather_object(gathered, mine, group=self.handle)
+        lib = _lib.load()
+        out = {}
+        for peer, handles in enumerate(gathered):
+            for key, raw in handles.items():
+                if peer == self.rank:
+                    out[(peer, key)] = allocs[key].ptr.value
+                    continue
+                ptr = ctypes.c_void_p()
+                buf = ctypes.create_string_buffer(raw, len(raw))
+                _lib.check("cozy_ipc_open", lib.cozy_ipc_open(buf, ctypes.byref(ptr)))
+                self.opened.append(ptr)
+                out[(peer, key)] = ptr.value
+        return out
+
+    def ensure(self, sizes: tuple[int, ...]) -> None:
+        """Map buffers of at least `sizes` elements (q, k, v, landing) on every rank. Every rank
+        calls with sizes that follow from the same agreed rows, so all decide alike."""
+        if self.sizes is not None and all(n <= have for n, have in zip(sizes, self.sizes)):
+            return
+        grow = sizes if self.sizes is None else tuple(max(a, b) for a, b in zip(sizes, self.sizes))
+        torch.cuda.synchronize(self.device)
+        self._release_sets()
+        dist.barrier(group=self.handle)
+        allocs = {}
+        for s in (0, 1):
+            for kind, n in zip(self.KINDS, grow, strict=True):
+                allocs[(kind, s)] = self.local[(s, kind)] = _Alloc(max(16, n * 2))
+        ptrs = self._exchange_handles(allocs)
+        for (peer, (kind, s)), addr in ptrs.items():
+            self.peer_ptrs[(peer, s, kind)] = addr
+        for s in (0, 1):
+            for kind, n in zip(self.KINDS, grow, strict=True):
+                self.views[(s, kind)] = _tensor(self.local[(s, kind)].ptr.value, n, self.device)
+        self.sizes = grow
+
+    def _release_sets(self) -> None:
+        lib = _lib.load()
+        keep = []
+        flag_addrs = {addr for (_, key), addr in self.peer_flags.items()}
+        for ptr in self.opened:
+            if ptr.value in flag_addrs:
+                keep.append(ptr)
+            else:
+                lib.cozy_ipc_close(ptr)
+        self.opened = keep
+        self.peer_ptrs.clear()
+        self.views.clear()
+        for alloc in self.local.values():
+            alloc.free()
+        self.local.clear()
+
+    def close(self) -> None:
+        torch.cuda.synchronize(self.device)
+        self._release_sets()
+        lib = _lib.load()
+        for ptr in self.opened:
+            lib.cozy_ipc_close(ptr)
+        self.opened = []
+        self.flags.free()
+
+    # ------------------------------------------------------------------ calls
+    def next_seq(self) -> int:
+        self.seq += 1
+        return self.seq
+
+    def peer(self, peer: int, s: int, kind: str) -> int:
+        return self.peer_ptrs[(peer, s, kind)]
+
+    def view(self, s: int, kind: str) -> torch.Tensor:
+        return self.views[(s, kind)]
+
+    def signal(self, kind: int, seq: int) -> None:
+        """Store `seq` into this rank's flag of `kind` in every rank's memory."""
+        slots = _lib.PeerSlots()
+        slots.count = self.world
+        for p in range(self.world):
+            slots.slot[p] = self.peer_flags[(p, ("flags", 0))] + (kind * self.world + self.rank) * 8
+        code = _lib.load().cozy_peer_signal(
+            ctypes.byref(slots), seq, torch.cuda.current_stream(self.device).cuda_stream
+        )
+        _lib.check("cozy_peer_signal", code)
+
+    def wait(self, kind: int, seq: int, status_ptr: int) -> None:
+        """The stream waits until every rank's flag of `kind` here reaches `seq`."""
+        base = self.flags.ptr.value + kind * self.world * 8
+        code = _lib.load().cozy_peer_wait(
+            base, self.world, seq, WAIT_LIMIT_NS, status_ptr,
+            torch.cuda.current_stream(self.device).cuda_stream,
+        )
+        _lib.check("cozy_peer_wait", code)
+
+
+_GROUPS: weakref.WeakKeyDictionary = weakref.WeakKeyDictionary()
+_GROUPS_LOCK = threading.Lock()
+
+
+def group_for(handle, device: torch.device) -> PeerGroup:
+    """This rank's mapped buffers for `handle` (formed on first use; collective)."""
+    with _GROUPS_LOCK:
+        found = _GROUPS.get(handle)
+        if found is None:
+            found = _GROUPS[handle] = PeerGroup(handle, device)
+        return found
+
+
+def close(handle) -> None:
+    """Unmap and free the group's buffers (collective with the group's other ranks)."""
+    with _GROUPS_LOCK:
+        found = _GROUPS.pop(handle, None)
+    if found is not None:
+        found.close()
+        dist.barrier(group=handle)

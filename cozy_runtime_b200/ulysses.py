@@ -25,6 +25,7 @@ passes `rows`.
 from __future__ import annotations
 
 import json
+import os
 import threading
 import weakref
 from collections.abc import Callable, Sequence
@@ -34,7 +35,7 @@ import torch
 import torch.distributed as dist
 from torch import Tensor
 
-from cozy_runtime_b200 import _lib, attention
+from cozy_runtime_b200 import _lib, attention, peer
 from cozy_runtime_b200.rope import RopeSpec
 
 Compute = Callable[[Tensor, Tensor, Tensor], Tensor]
@@ -326,10 +327,7 @@ class RankStep:
         self.kv_in = [r * batch * self.kvn * dim for r in rows]
         self.back_sizes = list(self.q_sizes)  # O returns as Q left: my rows, peer p's heads
         self.back_in = list(self.q_in)
-        dev, dt = query.device, query.dtype
-        self.q_send = torch.empty(sum(self.q_sizes), dtype=dt, device=dev)
-        self.k_send = torch.empty(sum(self.kv_sizes), dtype=dt, device=dev)
-        self.v_send = torch.empty(sum(self.kv_sizes), dtype=dt, device=dev)
+        self.q_send = self.k_send = self.v_send = None
 
     def receive_buffers(self) -> tuple[Tensor, Tensor, Tensor]:
         total, dev, dt = self.layout.total, self.query.device, self.query.dtype
@@ -340,18 +338,32 @@ class RankStep:
         )
 
     def pack(self) -> None:
-        """Stage 1: norm/RoPE/transposition of Q, K, V into the send blocks (one launch)."""
+        """Stage 1 into local send blocks (an NCCL crossing follows): norm/RoPE/transposition
+        of Q, K, V in one launch."""
         el = self.query.element_size()
+        dev, dt = self.query.device, self.query.dtype
+        self.q_send = torch.empty(sum(self.q_sizes), dtype=dt, device=dev)
+        self.k_send = torch.empty(sum(self.kv_sizes), dtype=dt, device=dev)
+        self.v_send = torch.empty(sum(self.kv_sizes), dtype=dt, device=dev)
 
         def ptrs(buf: Tensor, sizes: Sequence[int]) -> list[int]:
             return [buf.data_ptr() + off * el for off in _offsets(sizes)]
 
+        self.pack_to(
+            ptrs(self.q_send, self.q_sizes),
+            ptrs(self.k_send, self.kv_sizes),
+            ptrs(self.v_send, self.kv_sizes),
+        )
+
+    def pack_to(self, q_dst: Sequence[int], k_dst: Sequence[int], v_dst: Sequence[int]) -> None:
+        """Stage 1 into the given per-peer block addresses (local, or in the peers' own receive
+        buffers over NVLink): one launch for Q, K and V."""
         lay, rotate = self.layout, self.rope is not None
         pack(
             [
-                (self.query, ptrs(self.q_send, self.q_sizes), lay.q_lo, lay.q_n, rotate, self.norm_q),
-                (self.key, ptrs(self.k_send, self.kv_sizes), lay.kv_lo, lay.kv_n, rotate, self.norm_k),
-                (self.value, ptrs(self.v_send, self.kv_sizes), lay.kv_lo, lay.kv_n, False, None),
+                (self.query, q_dst, lay.q_lo, lay.q_n, rotate, self.norm_q),
+                (self.key, k_dst, lay.kv_lo, lay.kv_n, rotate, self.norm_k),
+                (self.value, v_dst, lay.kv_lo, lay.kv_n, False, None),
             ],
             self.mine,
             self.rope,
@@ -367,13 +379,16 @@ class RankStep:
         causal: bool,
         scale: float | None,
         into: Tensor | None = None,
+        scatter: _lib.Scatter | None = None,
     ) -> Tensor:
         """Attention over this rank's heads of the whole sequence, read in place from the
         receive buffers ([total][B][n][D]); returns the O send buffer in the same layout, or
         writes `into` ([B, total, n, D], any strides; degree 1: the output itself)."""
         lay, total, batch, dim = self.layout, self.layout.total, self.batch, self.dim
         qn, kvn = self.qn, self.kvn
-        if into is None:
+        if scatter is not None:
+            o_send, ov = None, None
+        elif into is None:
             o_send = torch.empty(
                 total * batch * qn * dim, dtype=self.query.dtype, device=self.query.device
             )
@@ -387,7 +402,10 @@ class RankStep:
         vv = v_recv.view(total, batch, kvn, dim).permute(1, 0, 2, 3)
         if compute is None:
             head_map = (lay.group, lay.q_lo[self.rank], lay.kv_lo[self.rank])
-            attention.attention_into(ov, qv, kv, vv, causal=causal, scale=scale, head_map=head_map)
+            attention.attention_into(
+                None if scatter is not None else ov, qv, kv, vv, causal=causal, scale=scale,
+                head_map=head_map, scatter=scatter,
+            )
             return o_send
         if kvn != qn or lay.group != 1:
             idx = torch.tensor(
@@ -435,6 +453,7 @@ def exchange(
     rope: RopeSpec | None = None,
     norm_q: Norm | None = None,
     norm_k: Norm | None = None,
+    transport: str | None = None,
 ) -> Tensor:
     """Sequence shards -> whole sequences per head subset -> attention -> back.
 
@@ -442,7 +461,9 @@ def exchange(
     takes the native attention with `causal`/`scale`. `rows`: every rank's row count, when the
     caller knows them (skips the store meeting). `rope`: tables over the whole sequence, applied
     to Q and K by global position in the first stage; `norm_q`/`norm_k`: per-head RMSNorm before
-    it. Returns [B, S_r, H, D] in the query's dtype.
+    it. `transport`: "peer" (in-kernel NVLink stores between the GPUs of one node) or "nccl"
+    (NCCL all-to-all); default `COZY_ULYSSES_TRANSPORT`, else "peer" for native attention on a
+    CUDA group of one node. Returns [B, S_r, H, D] in the query's dtype.
     """
     wide = narrow(0) if callable(narrow) else narrow
     if wide:
@@ -480,6 +501,10 @@ def exchange(
         _CLOCK.add((began, first, _Clock.mark(query), _Clock.mark(query)), 0)
         return out
 
+    if world > 1 and compute is None and _transport(handle, transport) == "peer":
+        return _exchange_peer(
+            query, key, value, handle, layout, rank, began, causal, scale, rope, norm_q, norm_k
+        )
     step = RankStep(query, key, value, layout, rank, rope=rope, norm_q=norm_q, norm_k=norm_k)
     step.pack()
     crossed = False
@@ -508,6 +533,87 @@ def exchange(
         if crossed:
             _abort(handle)
         raise
+    _CLOCK.add((began, first, last, _Clock.mark(query)), step.moved())
+    return out
+
+
+def _transport(handle, asked: str | None) -> str:
+    choice = asked or os.environ.get("COZY_ULYSSES_TRANSPORT", "") or "peer"
+    if choice not in ("peer", "nccl"):
+        raise ValueError(f"unknown Ulysses transport {choice!r} (peer or nccl)")
+    if choice == "peer" and dist.get_backend(handle) != "nccl":
+        return "nccl"  # a CPU/gloo group has no device peers
+    return choice
+
+
+def _exchange_peer(
+    query: Tensor,
+    key: Tensor,
+    value: Tensor,
+    handle,
+    layout: Plan,
+    rank: int,
+    began,
+    causal: bool,
+    scale: float | None,
+    rope: RopeSpec | None,
+    norm_q: Norm | None,
+    norm_k: Norm | None,
+) -> Tensor:
+    """The exchange over NVLink stores issued by the kernels themselves (`peer.PeerGroup`):
+    stage 1 writes every peer's heads into that peer's receive buffer, the attention writes every
+    output row into its owner's landing buffer; flags say when a call's writes have landed."""
+    batch, mine, heads, dim = (int(n) for n in query.shape)
+    device = query.device
+    world, total = layout.world, layout.total
+    rows = layout.rows
+    sizes = (
+        total * batch * max(layout.q_n) * dim,
+        total * batch * max(layout.kv_n) * dim,
+        total * batch * max(layout.kv_n) * dim,
+        batch * max(rows) * heads * dim,
+    )
+    pg = peer.group_for(handle, device)
+    status = attention.status_word(device).data_ptr()
+    with pg.lock:
+        pg.ensure(sizes)
+        seq = pg.next_seq()
+        s = seq & 1
+        step = RankStep(query, key, value, layout, rank, rope=rope, norm_q=norm_q, norm_k=norm_k)
+        start = layout.start(rank)
+        el = query.element_size()
+        q_dst = [pg.peer(p, s, "q") + start * batch * layout.q_n[p] * dim * el for p in range(world)]
+        k_dst = [pg.peer(p, s, "k") + start * batch * layout.kv_n[p] * dim * el for p in range(world)]
+        v_dst = [pg.peer(p, s, "v") + start * batch * layout.kv_n[p] * dim * el for p in range(world)]
+        step.pack_to(q_dst, k_dst, v_dst)
+        pg.signal(peer.QKV, seq)
+        pg.wait(peer.QKV, seq, status)
+        first = _Clock.mark(query)
+        qn, kvn = layout.q_n[rank], layout.kv_n[rank]
+        if qn:
+            scatter = _lib.Scatter()
+            scatter.world = world
+            scatter.head_offset = layout.q_lo[rank]
+            acc = 0
+            for p in range(world):
+                scatter.row_start[p] = acc
+                acc += rows[p]
+                scatter.out[p] = pg.peer(p, s, "land")
+                scatter.strides[p][0] = heads * dim
+                scatter.strides[p][1] = dim
+                scatter.strides[p][2] = rows[p] * heads * dim
+            scatter.row_start[world] = acc
+            step.attend(
+                pg.view(s, "q")[: total * batch * qn * dim],
+                pg.view(s, "k")[: total * batch * kvn * dim],
+                pg.view(s, "v")[: total * batch * kvn * dim],
+                None, causal, scale, scatter=scatter,
+            )
+        last = _Clock.mark(query)
+        pg.signal(peer.OUT, seq)
+        pg.wait(peer.OUT, seq, status)
+        out = torch.empty((batch, mine, heads, dim), dtype=query.dtype, device=device)
+        out.copy_(pg.view(s, "land")[: batch * mine * heads * dim].view(batch, mine, heads, dim))
     _CLOCK.add((began, first, last, _Clock.mark(query)), step.moved())
     return out
 

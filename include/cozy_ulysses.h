@@ -37,6 +37,19 @@ typedef struct CozyHeadMap {
   int kv_base;
 } CozyHeadMap;
 
+/* Where the attention writes its output rows when they go straight to their owners (the head->seq
+ * crossing done by the attention's own stores over NVLink): output row r (global sequence
+ * position) of batch b and local head h lands in owner p (row_start[p] <= r < row_start[p+1]) at
+ * out[p] + b*strides[p][2] + (r - row_start[p])*strides[p][0] + (h + head_offset)*strides[p][1].
+ * out[p] may be another GPU's memory (cozy_ipc_open). */
+typedef struct CozyScatter {
+  int world;
+  int head_offset;
+  int row_start[COZY_MAX_PEERS + 1];
+  void* out[COZY_MAX_PEERS];
+  long long strides[COZY_MAX_PEERS][3];
+} CozyScatter;
+
 /* Local attention over whole sequences: softmax(Q Kᵀ·scale) V for every (batch, query head),
  * query head h reading the key/value head `head_map` names. Causal masks align bottom-right
  * (key j visible to query i when j <= i + seq_k - seq_q).
@@ -44,13 +57,14 @@ typedef struct CozyHeadMap {
  * src/cozy_runtime/internal/attention_upstream.py:191-215 (`cudnn`, torch SDPA on cuDNN) and
  * :109-147 (`sdpa`), on [batch, seq, heads, dim] operands.
  * Strides are in elements, ordered {seq, head, batch}; each a multiple of 8; pointers 16-byte
- * aligned. head_dim 64 or 128. */
+ * aligned. head_dim 64 or 128. With `scatter` non-NULL the output goes where it says and
+ * `out`/`o_strides` are ignored. */
 COZY_API int cozy_attention_fwd(const void* q, const void* k, const void* v, void* out, int batch,
                        int seq_q, int seq_k, int heads_q, int heads_kv, int head_dim,
                        const long long* q_strides, const long long* k_strides,
                        const long long* v_strides, const long long* o_strides,
-                       const CozyHeadMap* head_map, int causal, float scale, int* status,
-                       uintptr_t stream);
+                       const CozyHeadMap* head_map, const CozyScatter* scatter, int causal,
+                       float scale, int* status, uintptr_t stream);
 
 /* One tensor of the seq->head exchange's first stage (Q, K or V): this rank's rows
  * [batch, rows, heads, head_dim] (`src`, element strides {seq, head, batch}), optionally
@@ -101,6 +115,32 @@ COZY_API int cozy_ulysses_pack(const CozyPackTensor* tensors, int count, int wor
 COZY_API int cozy_ulysses_land(const void* returned, int world, int rows, int batch, int head_dim,
                       const int* head_lo, const int* head_n, void* out,
                       const long long* out_strides, uintptr_t stream);
+
+/* ---------------------------------------------------------------- peer memory (one node)
+ * The NVLink exchange keeps its receive and landing buffers in memory every GPU of the group
+ * maps. These replace the reference's copy-engine exchange buffers
+ * (src/cozy_runtime/internal/parallel/copy_engine.py:136-251, mapped at group formation, never
+ * inside a call). cozy_ipc_alloc zero-fills `bytes` of device memory and writes its IPC handle
+ * (cozy_ipc_handle_bytes() bytes) to `handle`; another process opens it with cozy_ipc_open. */
+COZY_API int cozy_ipc_alloc(unsigned long long bytes, void** ptr, void* handle);
+COZY_API int cozy_ipc_open(const void* handle, void** ptr);
+COZY_API int cozy_ipc_close(void* ptr);
+COZY_API int cozy_ipc_free(void* ptr);
+COZY_API int cozy_ipc_handle_bytes(void);
+
+/* Arrival flags: `slot[i]` is this rank's 64-bit flag word in peer i's memory. cozy_peer_signal
+ * fences this GPU's earlier writes at system scope and stores `seq` into every slot (release).
+ * cozy_peer_wait blocks the stream until each of flags[0..count) reaches `seq` (acquire), or
+ * gives up after `limit_ns` nanoseconds and sets *status to 2. Replaces the NCCL all-reduce
+ * barriers of the copy-engine exchange (copy_engine.py:167). */
+typedef struct CozyPeerSlots {
+  int count;
+  long long* slot[COZY_MAX_PEERS];
+} CozyPeerSlots;
+
+COZY_API int cozy_peer_signal(const CozyPeerSlots* slots, long long seq, uintptr_t stream);
+COZY_API int cozy_peer_wait(const long long* flags, int count, long long seq, long long limit_ns,
+                            int* status, uintptr_t stream);
 
 /* Name of a code returned above (a cudaError_t, or one of this library's). */
 COZY_API const char* cozy_error_name(int code);

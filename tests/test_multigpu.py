@@ -1,5 +1,6 @@
-"""The exchange over real NCCL between GPU processes (one per GPU), against the reference's golden
-outputs and the oracle. Needs two or more GPUs; skipped otherwise.
+"""The exchange between GPU processes (one per GPU) over both transports — in-kernel NVLink peer
+stores and NCCL all-to-all — against the reference's golden outputs and the oracle. Needs two or
+more GPUs; skipped otherwise.
 
 Each case spawns W processes (W ≤ visible GPUs), every rank passes its `tensor_split` rows and
 the rows come from the store meeting (no `rows` argument), as the reference's exchange does.
@@ -31,7 +32,7 @@ def _port() -> int:
         return s.getsockname()[1]
 
 
-def _rank(rank, world, port, inputs, causal, outdir, rope_args):
+def _rank(rank, world, port, inputs, causal, outdir, rope_args, transport):
     import torch.distributed as dist
 
     from cozy_runtime_b200 import rope as rope_mod
@@ -48,21 +49,28 @@ def _rank(rank, world, port, inputs, causal, outdir, rope_args):
     spec = None
     if rope_args is not None:
         spec = rope_mod.axial(rope_args[0], (44, 42, 42), after=rope_args[1]).to(device)
-    out = ulysses.exchange(q, k, v, dist.group.WORLD, None, causal=causal, rope=spec)
-    out2 = ulysses.exchange(q, k, v, dist.group.WORLD, None, causal=causal, rope=spec)
+    outs = [
+        ulysses.exchange(q, k, v, dist.group.WORLD, None, causal=causal, rope=spec,
+                         transport=transport)
+        for _ in range(3)
+    ]
     torch.cuda.synchronize()
-    assert torch.equal(out, out2), "two calls differ"
+    from cozy_runtime_b200 import attention
+
+    attention.check_status(device)
+    out = outs[0]
+    assert all(torch.equal(out, o) for o in outs[1:]), "repeated calls differ"
     torch.save(out.cpu(), os.path.join(outdir, f"{rank}.pt"))
     dist.barrier()
     dist.destroy_process_group()
 
 
-def _run(inputs, world, causal=False, rope_args=None) -> torch.Tensor:
+def _run(inputs, world, causal=False, rope_args=None, transport="peer") -> torch.Tensor:
     import torch.multiprocessing as mp
 
     with tempfile.TemporaryDirectory() as tmp:
-        mp.spawn(_rank, args=(world, _port(), inputs, causal, tmp, rope_args), nprocs=world,
-                 join=True)
+        mp.spawn(_rank, args=(world, _port(), inputs, causal, tmp, rope_args, transport),
+                 nprocs=world, join=True)
         return torch.cat([torch.load(os.path.join(tmp, f"{r}.pt")) for r in range(world)], dim=1)
 
 
@@ -72,14 +80,15 @@ def _check(got, want):
     assert err.mean().item() <= MEAN_ABS, f"mean-abs {err.mean().item():.3e}"
 
 
+@pytest.mark.parametrize("transport", ["peer", "nccl"])
 @pytest.mark.parametrize("name", ulysses_cases())
-def test_nccl_exchange_matches_reference_golden(name):
+def test_exchange_matches_reference_golden(name, transport):
     case = load(name)
     world = int(case["world"])
     if world < 2 or world > _gpus():
         pytest.skip(f"needs {world} GPUs")
     inputs = tuple(tensor(case[key]) for key in ("q", "k", "v"))
-    got = _run(inputs, world, causal=bool(case["causal"]))
+    got = _run(inputs, world, causal=bool(case["causal"]), transport=transport)
     _check(got, tensor(case["out"]).float())
 
 
@@ -88,7 +97,8 @@ def test_nccl_exchange_matches_reference_golden(name):
     [(2, 8, 8, False, True), (4, 8, 2, True, False), (8, 8, 8, False, True), (8, 32, 8, True, False),
      (3, 5, 5, False, True)],
 )
-def test_nccl_exchange_against_oracle(world, hq, hkv, causal, rotate):
+@pytest.mark.parametrize("transport", ["peer", "nccl"])
+def test_exchange_against_oracle(world, hq, hkv, causal, rotate, transport):
     if world > _gpus():
         pytest.skip(f"needs {world} GPUs")
     from cozy_runtime_b200 import rope as rope_mod
@@ -99,7 +109,8 @@ def test_nccl_exchange_against_oracle(world, hq, hkv, causal, rotate):
     q = torch.randn(1, seq, hq, 128, generator=g).to(torch.bfloat16)
     k = torch.randn(1, seq, hkv, 128, generator=g).to(torch.bfloat16)
     v = torch.randn(1, seq, hkv, 128, generator=g).to(torch.bfloat16)
-    got = _run((q, k, v), world, causal=causal, rope_args=(grid, text) if rotate else None)
+    got = _run((q, k, v), world, causal=causal, rope_args=(grid, text) if rotate else None,
+               transport=transport)
     if rotate:
         spec = rope_mod.axial(grid, (44, 42, 42), after=text)
         q, k = (oracle.head_norm_rope(t.float(), spec.cos, spec.sin, rotary=128, interleaved=True,
