@@ -80,6 +80,72 @@ def peaks() -> tuple[float, str]:
     return FALLBACK_BF16_TFLOPS, "fallback"
 
 
+class NvmlSampler:
+    """SM clock and clock-event reasons read through NVML every 2 ms during the timed region
+    (read-only queries; no setting is changed). Falls back to `ClockSampler` without NVML."""
+
+    REASONS = (
+        ("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+        ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+        ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+        ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"),
+    )
+
+    def __init__(self, gpu: int) -> None:
+        import threading
+
+        import pynvml
+
+        self.nvml = pynvml
+        pynvml.nvmlInit()
+        self.handle = pynvml.nvmlDeviceGetHandleByIndex(gpu)
+        self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+        self.samples: list[tuple[int, int]] = []
+        self.stop = threading.Event()
+        self.thread = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self) -> None:
+        n = self.nvml
+        while not self.stop.is_set():
+            try:
+                mhz = n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM)
+                reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                self.samples.append((mhz, reasons))
+            except n.NVMLError:
+                pass
+            time.sleep(0.002)
+
+    def __enter__(self):
+        self.thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self.stop.set()
+        self.thread.join(timeout=5)
+
+    def summary(self) -> dict | None:
+        if not self.samples:
+            return None
+        reasons = sorted(
+            {name for _, bits in self.samples for name, attr in self.REASONS
+             if bits & getattr(self.nvml, attr)}
+        )
+        return {
+            "sm_mhz": statistics.median(s[0] for s in self.samples),
+            "sm_max_mhz": self.max_mhz,
+            "reasons": reasons,
+            "samples": len(self.samples),
+            "source": "nvml",
+        }
+
+
+def clock_sampler(gpu: int):
+    try:
+        return NvmlSampler(gpu)
+    except Exception:  # noqa: BLE001 - no NVML: sample through nvidia-smi instead
+        return ClockSampler(gpu)
+
+
 class ClockSampler:
     """nvidia-smi samples of the SM clock and throttle reasons during the timed region."""
 
@@ -279,7 +345,7 @@ def main() -> None:
     torch.cuda.synchronize()
 
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    sampler = ClockSampler(local_gpu_index(local))
+    sampler = clock_sampler(local_gpu_index(local))
     with sampler:
         e0.record()
         for _ in range(args.steps):
