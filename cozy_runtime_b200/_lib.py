@@ -114,6 +114,12 @@ SIGNATURES = {
     "cozy_ipc_handle_bytes": ([], c_int),
     "cozy_peer_signal": ([POINTER(PeerSlots), c_longlong, c_uint64], c_int),
     "cozy_peer_wait": ([c_void_p, c_int, c_longlong, c_longlong, c_void_p, c_uint64], c_int),
+    "cozy_rope_attention_fwd_noalloc": (
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
+         POINTER(c_longlong), POINTER(c_longlong), POINTER(c_longlong), POINTER(c_longlong),
+         POINTER(Rope), c_int, c_float, c_int, c_float, c_void_p, c_uint64],
+        c_int,
+    ),
     "cozy_error_name": ([c_int], c_char_p),
     "cozy_abi_version": ([], c_int),
 }

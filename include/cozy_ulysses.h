@@ -116,6 +116,27 @@ COZY_API int cozy_ulysses_land(const void* returned, int world, int rows, int ba
                       const int* head_lo, const int* head_n, void* out,
                       const long long* out_strides, uintptr_t stream);
 
+/* ------------------------------------------------------------ allocation-free degree-1 call
+ * No counterpart in the reference: an addition for callers that must not allocate device memory
+ * while they run — a stream being captured into a CUDA graph (cudaMalloc cannot be captured), a
+ * serving loop that owns all device memory up front in a fixed arena, or a latency-bound host
+ * thread (cudaMalloc can synchronize the device). Same result as the degree-1 first stage
+ * (RoPE per `rope`, per-head RMSNorm with unit weight when `normalize`) followed by
+ * cozy_attention_fwd, but the rotated Q and K live in a static device array of
+ * COZY_NOALLOC_SCRATCH_BYTES that every GPU loading this library holds until the process exits.
+ * The caller passes inputs and output; nothing is allocated. A call needing more than the array
+ * ((heads_q + heads_kv) * seq * batch * head_dim * 2 bytes) returns cudaErrorInvalidValue.
+ * Every call on a device shares the array: calls whose kernels overlap on the GPU race, so
+ * serialize them. The first call on a device looks up the array's address; make it before any
+ * stream capture. Strides as cozy_attention_fwd ({seq, head, batch}, elements). */
+#define COZY_NOALLOC_SCRATCH_BYTES (64ull << 20)
+
+COZY_API int cozy_rope_attention_fwd_noalloc(
+    const void* q, const void* k, const void* v, void* out, int batch, int seq, int heads_q,
+    int heads_kv, int head_dim, const long long* q_strides, const long long* k_strides,
+    const long long* v_strides, const long long* o_strides, const CozyRope* rope, int normalize,
+    float norm_eps, int causal, float scale, int* status, uintptr_t stream);
+
 /* ---------------------------------------------------------------- peer memory (one node)
  * The NVLink exchange keeps its receive and landing buffers in memory every GPU of the group
  * maps. These replace the reference's copy-engine exchange buffers
