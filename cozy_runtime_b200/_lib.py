@@ -79,6 +79,54 @@ class PeerSlots(Structure):
     _fields_ = [("count", c_int), ("slot", c_void_p * MAX_PEERS)]
 
 
+class Fp8Stats(Structure):
+    """`CozyFp8Stats`."""
+
+    _fields_ = [
+        ("key", c_void_p),
+        ("value", c_void_p),
+        ("k_strides", c_longlong * 3),
+        ("v_strides", c_longlong * 3),
+        ("rows", c_int),
+        ("batch", c_int),
+        ("heads", c_int),
+        ("head_dim", c_int),
+        ("k_sum", c_void_p),
+        ("v_amax", c_void_p),
+    ]
+
+
+class Fp8Tensor(Structure):
+    """`CozyFp8Tensor`."""
+
+    _fields_ = [
+        ("src", c_void_p),
+        ("src_strides", c_longlong * 3),
+        ("heads", c_int),
+        ("hadamard", c_int),
+        ("mean_sum", c_void_p),
+        ("mean_inv_count", c_float),
+        ("channel_scale", c_void_p),
+        ("dst", c_void_p * MAX_PEERS),
+        ("scale_dst", c_void_p * MAX_PEERS),
+        ("scale_seq", c_longlong),
+        ("head_lo", c_int * MAX_PEERS),
+        ("head_n", c_int * MAX_PEERS),
+    ]
+
+
+class Fp8Pack(Structure):
+    """`CozyFp8Pack`."""
+
+    _fields_ = [
+        ("t", Fp8Tensor * 3),
+        ("world", c_int),
+        ("rows", c_int),
+        ("batch", c_int),
+        ("head_dim", c_int),
+    ]
+
+
 class CudaCallError(RuntimeError):
     """A library entry point returned a non-zero cudaError_t."""
 
@@ -118,6 +166,15 @@ SIGNATURES = {
         [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
          POINTER(c_longlong), POINTER(c_longlong), POINTER(c_longlong), POINTER(c_longlong),
          POINTER(Rope), c_int, c_float, c_int, c_float, c_void_p, c_uint64],
+        c_int,
+    ),
+    "cozy_fp8_stats": ([POINTER(Fp8Stats), c_uint64], c_int),
+    "cozy_fp8_pack": ([POINTER(Fp8Pack), c_uint64], c_int),
+    "cozy_attention_fwd_fp8": (
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_longlong, c_void_p,
+         c_int, c_int, c_int, c_int, c_int, c_int,
+         POINTER(c_longlong), POINTER(c_longlong), POINTER(c_longlong), POINTER(c_longlong),
+         POINTER(HeadMap), POINTER(Scatter), c_int, c_float, c_void_p, c_uint64],
         c_int,
     ),
     "cozy_error_name": ([c_int], c_char_p),

@@ -62,11 +62,18 @@ struct AttentionParams {
   int row_start[COZY_MAX_PEERS + 1];
   __nv_bfloat16* outs[COZY_MAX_PEERS];
   long long outs_strides[COZY_MAX_PEERS][3];
+  // FP8 operands: per-token scales of Q rows and K columns ([batch][heads][scale_seq]) and the
+  // per-channel scale of V ([batch][heads_kv][head_dim]); unused by the bf16 kernel
+  const float* q_scale;
+  const float* k_scale;
+  const float* v_scale;
+  long long scale_seq;
 };
 
-template <int HD>
+template <int HD, bool FP8>
 struct AttentionSmem {
-  static constexpr int kBoxes = HD / 64;              // 128-byte swizzle atoms per row
+  static constexpr int kElem = FP8 ? 1 : 2;            // bytes per element
+  static constexpr int kBoxes = HD * kElem / 128;     // 128-byte swizzle atoms per row
   static constexpr int kBoxBytes = 128 * 128;         // one box: 128 rows × 128 bytes
   static constexpr int kTileBytes = kBoxes * kBoxBytes;
   static constexpr int kQOffset = 0;
@@ -192,12 +199,60 @@ __device__ __forceinline__ void exp_chunk(const uint32_t (&r)[32], float2 scale2
   }
 }
 
-template <int HD>
+// ------------------------------------------------------------------------------ FP8 helpers
+// P is stored as e4m3 codes of p·2^8: with the running max exact to within 2^0.5 (the FP8
+// kernel rescales O whenever a row's max grows by more than that) every code is at most
+// 2^8.5 ≈ 362 < 448, and values down to 2^-9·2^-8 stay representable.
+constexpr float kPScaleLog2 = 8.0f;
+constexpr float kRescaleLog2Fp8 = 0.5f;
+
+// 32 scores (in TMEM order) times their keys' scales (32 consecutive floats).
+__device__ __forceinline__ void scale_chunk(uint32_t (&r)[32], const float4* ks) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 k = ks[i];
+    const float2 a = __fmul2_rn(make_float2(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1])),
+                                make_float2(k.x, k.y));
+    const float2 c = __fmul2_rn(make_float2(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])),
+                                make_float2(k.z, k.w));
+    r[4 * i] = __float_as_uint(a.x);
+    r[4 * i + 1] = __float_as_uint(a.y);
+    r[4 * i + 2] = __float_as_uint(c.x);
+    r[4 * i + 3] = __float_as_uint(c.y);
+  }
+}
+
+// 32 scores -> 32 e4m3 codes of 2^(s·scale + bias) packed four to a word, summed into `acc`.
+__device__ __forceinline__ void exp_chunk_fp8(const uint32_t (&r)[32], float2 scale2, float2 bias2,
+                                              float2& acc, uint32_t* pk) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float2 e[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int k = 4 * i + 2 * h;
+      const float2 sv = make_float2(__uint_as_float(r[k]), __uint_as_float(r[k + 1]));
+      const float2 t = __ffma2_rn(sv, scale2, bias2);
+      if (((2 * i + h) & 7) < kPolyPerEight) {
+        e[h] = exp2_poly2(t);
+      } else {
+        e[h] = make_float2(ex2_approx(t.x), ex2_approx(t.y));
+      }
+      acc = __fadd2_rn(acc, e[h]);
+    }
+    uint16_t lo, hi;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %2, %1;" : "=h"(lo) : "f"(e[0].x), "f"(e[0].y));
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %2, %1;" : "=h"(hi) : "f"(e[1].x), "f"(e[1].y));
+    pk[i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+  }
+}
+
+template <int HD, bool FP8>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                          const __grid_constant__ CUtensorMap tm_k,
                          const __grid_constant__ CUtensorMap tm_v, const AttentionParams p) {
-  using L = AttentionSmem<HD>;
+  using L = AttentionSmem<HD, FP8>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -266,7 +321,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tS = tmem + lane_bits + static_cast<uint32_t>(s * kBlockN);
     const uint32_t tO = tmem + lane_bits + 256u + static_cast<uint32_t>(s * HD);
     const int visible = q_row + p.causal_offset;  // last key column this row sees (causal)
-    const float scale = p.scale_log2;
+    // FP8: a row's scores carry its Q block scale; the columns' K scales are applied per key
+    float scale = p.scale_log2;
+    const float* k_scale_row = nullptr;
+    if constexpr (FP8) {
+      const long long qh = static_cast<long long>(b) * p.heads_q + head;
+      scale *= (q_row < p.seq_q) ? p.q_scale[qh * p.scale_seq + q_row] : 0.f;
+      k_scale_row = p.k_scale + (static_cast<long long>(b) * p.heads_kv + kv_head) * p.scale_seq;
+    }
     float m = -INFINITY;  // running max, log2 domain, of the probabilities' reference point
     float l = 0.f;        // running row sum against m
     bool ok = true;
@@ -287,6 +349,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       reg_fence(r2);
       reg_fence(r3);
       const int kv0 = j * kBlockN;
+      if constexpr (FP8) {  // scores of the codes times each key's scale
+        const float4* ks = reinterpret_cast<const float4*>(k_scale_row + kv0);
+        scale_chunk(r0, ks);
+        scale_chunk(r1, ks + 8);
+        scale_chunk(r2, ks + 16);
+        scale_chunk(r3, ks + 24);
+      }
       const bool ragged = kv0 + kBlockN > p.seq_k;
       const bool diagonal = p.causal && kv0 + kBlockN - 1 > visible;
       if (ragged || diagonal) {
@@ -301,7 +370,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float m_new = fmaxf(m, mt * scale);
       if (j == 0) {
         m = m_new;
-      } else if (__any_sync(0xffffffffu, m_new > m + kRescaleLog2)) {
+      } else if (__any_sync(0xffffffffu, m_new > m + (FP8 ? kRescaleLog2Fp8 : kRescaleLog2))) {
         // O row rescale: this warp's rows, once PV of the previous tile completed (the commit
         // behind s_full covers every earlier MMA of the issuing thread).
         const float factor = (m == -INFINITY) ? 0.f : ex2_approx(m - m_new);
@@ -320,21 +389,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const float mu = (m == -INFINITY) ? 0.f : m;
       const float2 scale2 = make_float2(scale, scale);
-      const float2 negm2 = make_float2(-mu, -mu);
       float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
-      uint32_t pk[16];
-      // first half of P (keys 0..63): the MMA starts its product while the rest is formed
-      exp_chunk(r0, scale2, negm2, acc0, pk);
-      tmem_st16(tS + 0, pk);
-      exp_chunk(r1, scale2, negm2, acc1, pk);
-      tmem_st16(tS + 16, pk);
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&p_ready[2 * s]);
-      exp_chunk(r2, scale2, negm2, acc0, pk);
-      tmem_st16(tS + 32, pk);
-      exp_chunk(r3, scale2, negm2, acc1, pk);
-      tmem_st16(tS + 48, pk);
+      if constexpr (FP8) {
+        // P as e4m3 codes of 2^(t + 8) (≤ 256·2^0.5 < 448); the row sum carries the same 2^8
+        const float2 negm2 = make_float2(kPScaleLog2 - mu, kPScaleLog2 - mu);
+        uint32_t pk[16];
+        exp_chunk_fp8(r0, scale2, negm2, acc0, pk);
+        exp_chunk_fp8(r1, scale2, negm2, acc1, pk + 8);
+        tmem_st16(tS + 0, pk);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&p_ready[2 * s]);
+        exp_chunk_fp8(r2, scale2, negm2, acc0, pk);
+        exp_chunk_fp8(r3, scale2, negm2, acc1, pk + 8);
+        tmem_st16(tS + 16, pk);
+      } else {
+        const float2 negm2 = make_float2(-mu, -mu);
+        uint32_t pk[16];
+        // first half of P (keys 0..63): the MMA starts its product while the rest is formed
+        exp_chunk(r0, scale2, negm2, acc0, pk);
+        tmem_st16(tS + 0, pk);
+        exp_chunk(r1, scale2, negm2, acc1, pk);
+        tmem_st16(tS + 16, pk);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&p_ready[2 * s]);
+        exp_chunk(r2, scale2, negm2, acc0, pk);
+        tmem_st16(tS + 32, pk);
+        exp_chunk(r3, scale2, negm2, acc1, pk);
+        tmem_st16(tS + 48, pk);
+      }
       const float2 acc = __fadd2_rn(acc0, acc1);
       l += acc.x + acc.y;
       tmem_wait_st();
@@ -374,10 +458,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 32; ++i) o[i] = 0u;
         }
         uint32_t packed[16];
+        if constexpr (FP8) {  // V's per-channel scales
+          const float* vs = p.v_scale +
+                            (static_cast<long long>(b) * p.heads_kv + kv_head) * HD + c * 32;
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-          packed[i] = pack_bf16x2(__uint_as_float(o[2 * i]) * inv,
-                                  __uint_as_float(o[2 * i + 1]) * inv);
+          for (int i = 0; i < 16; ++i)
+            packed[i] = pack_bf16x2(__uint_as_float(o[2 * i]) * inv * vs[2 * i],
+                                    __uint_as_float(o[2 * i + 1]) * inv * vs[2 * i + 1]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            packed[i] = pack_bf16x2(__uint_as_float(o[2 * i]) * inv,
+                                    __uint_as_float(o[2 * i + 1]) * inv);
+        }
         if (valid) {
           uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
 #pragma unroll
@@ -428,8 +521,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     // a converged warp). Descriptors are a base per operand plus compile-time offsets.
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
     if (n_kv > 0) {
-      constexpr uint32_t kIdescQK = idesc_bf16_f32(kBlockM, kBlockN, false);
-      constexpr uint32_t kIdescPV = idesc_bf16_f32(kBlockM, HD, true);
+      constexpr uint32_t kIdescQK =
+          FP8 ? idesc_e4m3_f32(kBlockM, kBlockN, false) : idesc_bf16_f32(kBlockM, kBlockN, false);
+      constexpr uint32_t kIdescPV =
+          FP8 ? idesc_e4m3_f32(kBlockM, HD, true) : idesc_bf16_f32(kBlockM, HD, true);
+      // one MMA takes 32 bytes of K: 16 bf16 or 32 e4m3 elements
+      constexpr int kQKSteps = HD * L::kElem / 32;
+      constexpr int kPVSteps = kBlockN * L::kElem / 32;
+      constexpr int kPVRows = 32 / L::kElem;  // key rows per PV step
       const uint64_t dq = smem_desc_sw128(smem_u32(sQ), 16, 1024);
       const uint64_t dk = smem_desc_sw128(smem_u32(sKV), 16, 1024);
       const uint64_t dv = smem_desc_sw128(smem_u32(sKV), L::kBoxBytes, 1024);
@@ -438,22 +537,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint64_t qa = dq + static_cast<uint64_t>(s) * kTileStep;
         const uint64_t ka = dk + static_cast<uint64_t>(stage) * kTileStep;
 #pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          // K-major 128-byte swizzle: 16-element steps move 32 bytes inside a row's atom;
-          // every 4 steps move to the next 64-column box.
+        for (int kk = 0; kk < kQKSteps; ++kk) {
+          // K-major 128-byte swizzle: each step moves 32 bytes inside a row's atom; every 4
+          // steps move to the next box of 128-byte rows.
           const uint64_t off = static_cast<uint64_t>(((kk >> 2) * L::kBoxBytes + (kk & 3) * 32) >> 4);
-          mma_ss(tmem + s * kBlockN, qa + off, ka + off, kIdescQK, kk > 0 ? 1u : 0u);
+          if constexpr (FP8) mma_ss_f8(tmem + s * kBlockN, qa + off, ka + off, kIdescQK, kk > 0 ? 1u : 0u);
+          else mma_ss(tmem + s * kBlockN, qa + off, ka + off, kIdescQK, kk > 0 ? 1u : 0u);
         }
       };
       auto issue_pv = [&](int s, int stage, uint32_t accumulate, int half) {
         const uint64_t va = dv + static_cast<uint64_t>(stage) * kTileStep;
 #pragma unroll
-        for (int kk = half * (kBlockN / 32); kk < (half + 1) * (kBlockN / 32); ++kk) {
-          // V is MN-major for this product: 16 key rows per step (2048 bytes); the two
-          // 64-column halves of the head dimension are one box (16 KB) apart.
-          mma_ts(tmem + 256u + s * HD, tmem + s * kBlockN + kk * 8,
-                 va + static_cast<uint64_t>((kk * 2048) >> 4), kIdescPV,
-                 kk > 0 ? 1u : accumulate);
+        for (int kk = half * (kPVSteps / 2); kk < (half + 1) * (kPVSteps / 2); ++kk) {
+          // V is MN-major for this product: kPVRows key rows of 128 bytes per step; with bf16
+          // the two 64-column halves of the head dimension are one box (16 KB) apart. P's
+          // step is 8 TMEM columns either way (16 bf16 or 32 e4m3 codes a lane).
+          const uint64_t vo = static_cast<uint64_t>((kk * kPVRows * 128) >> 4);
+          if constexpr (FP8)
+            mma_ts_f8(tmem + 256u + s * HD, tmem + s * kBlockN + kk * 8, va + vo, kIdescPV,
+                      kk > 0 ? 1u : accumulate);
+          else
+            mma_ts(tmem + 256u + s * HD, tmem + s * kBlockN + kk * 8, va + vo, kIdescPV,
+                   kk > 0 ? 1u : accumulate);
         }
       };
       bool ok = warp_wait(q_full, 0, abort, p.status);
@@ -550,50 +655,63 @@ static EncodeTiled encode_tiled() {
   return fn;
 }
 
-// A 4-D bf16 tensor map over (head_dim, seq, heads, batch) with element strides
-// (1, s_stride, h_stride, b_stride) and a 64 × 128 box in 128-byte swizzle.
-static int make_map(CUtensorMap* map, const void* base, int head_dim, int seq, int heads,
-                    int batch, long long s_stride, long long h_stride, long long b_stride) {
+// A 4-D tensor map over (head_dim, seq, heads, batch) with element strides
+// (1, s_stride, h_stride, b_stride) and a box of 128 bytes × 128 rows in 128-byte swizzle:
+// 64 bf16 or 128 e4m3 elements a row.
+static int make_map(CUtensorMap* map, const void* base, int elem_bytes, int head_dim, int seq,
+                    int heads, int batch, long long s_stride, long long h_stride,
+                    long long b_stride) {
   EncodeTiled fn = encode_tiled();
   if (fn == nullptr) return cudaErrorNotSupported;
   cuuint64_t dims[4] = {static_cast<cuuint64_t>(head_dim), static_cast<cuuint64_t>(seq),
                         static_cast<cuuint64_t>(heads), static_cast<cuuint64_t>(batch)};
-  cuuint64_t strides[3] = {static_cast<cuuint64_t>(s_stride) * 2,
-                           static_cast<cuuint64_t>(h_stride) * 2,
-                           static_cast<cuuint64_t>(b_stride) * 2};
-  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(s_stride) * elem_bytes,
+                           static_cast<cuuint64_t>(h_stride) * elem_bytes,
+                           static_cast<cuuint64_t>(b_stride) * elem_bytes};
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(128 / elem_bytes), 128, 1, 1};
   cuuint32_t elem[4] = {1, 1, 1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims,
-                  strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+  const CUtensorMapDataType type =
+      elem_bytes == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUresult r = fn(map, type, 4, const_cast<void*>(base), dims, strides, box, elem,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? 0 : cudaErrorInvalidValue;
 }
 
-template <int HD>
+template <int HD, bool FP8>
 static int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                   const AttentionParams& p, cudaStream_t stream) {
-  using L = AttentionSmem<HD>;
+  using L = AttentionSmem<HD, FP8>;
   static bool configured[64] = {};
   int device = 0;
   cudaGetDevice(&device);
   if (device < 64 && !configured[device]) {
-    cudaError_t e = cudaFuncSetAttribute(attention_fwd_kernel<HD>,
+    cudaError_t e = cudaFuncSetAttribute(attention_fwd_kernel<HD, FP8>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
     if (e != cudaSuccess) return e;
     configured[device] = true;
   }
   dim3 grid(p.q_blocks, p.heads_q, p.batch);
-  attention_fwd_kernel<HD><<<grid, kThreads, L::kAlloc, stream>>>(mq, mk, mv, p);
+  attention_fwd_kernel<HD, FP8><<<grid, kThreads, L::kAlloc, stream>>>(mq, mk, mv, p);
   return cudaGetLastError();
 }
 
-int attention_forward(const void* q, const void* k, const void* v, void* out, int batch,
-                      int seq_q, int seq_k, int heads_q, int heads_kv, int head_dim,
-                      const long long* q_strides, const long long* k_strides,
-                      const long long* v_strides, const long long* o_strides,
-                      const CozyHeadMap* head_map, const CozyScatter* scatter, int causal,
-                      float scale, int* status, cudaStream_t stream) {
+struct Fp8Operands {
+  const float* q_scale;
+  const float* k_scale;
+  const float* v_scale;
+  long long scale_seq;
+};
+
+static int attention_launch(const void* q, const void* k, const void* v, void* out, int batch,
+                            int seq_q, int seq_k, int heads_q, int heads_kv, int head_dim,
+                            const long long* q_strides, const long long* k_strides,
+                            const long long* v_strides, const long long* o_strides,
+                            const CozyHeadMap* head_map, const CozyScatter* scatter, int causal,
+                            float scale, int* status, const Fp8Operands* fp8,
+                            cudaStream_t stream) {
   if (head_dim != 64 && head_dim != 128) return cudaErrorNotSupported;
+  if (fp8 != nullptr && head_dim != 128) return cudaErrorNotSupported;
   if (batch <= 0 || seq_q <= 0 || seq_k <= 0 || heads_q <= 0 || heads_kv <= 0)
     return cudaErrorInvalidValue;
   CozyHeadMap map = {heads_q / heads_kv, 0, 0};
@@ -611,10 +729,22 @@ int attention_forward(const void* q, const void* k, const void* v, void* out, in
   const void* ptrs[4] = {q, k, v, scatter ? q : out};
   for (const void* ptr : ptrs)
     if (ptr == nullptr || reinterpret_cast<uintptr_t>(ptr) % 16 != 0) return cudaErrorInvalidValue;
-  const long long* all[4] = {q_strides, k_strides, v_strides, scatter ? q_strides : o_strides};
-  for (const long long* st : all)
+  // operand rows must start on 16-byte boundaries (TMA): 8 bf16 or 16 e4m3 elements
+  const long long in_align = fp8 != nullptr ? 16 : 8;
+  const long long* ins[3] = {q_strides, k_strides, v_strides};
+  for (const long long* st : ins)
     for (int i = 0; i < 3; ++i)
-      if (st[i] <= 0 || st[i] % 8 != 0) return cudaErrorInvalidValue;
+      if (st[i] <= 0 || st[i] % in_align != 0) return cudaErrorInvalidValue;
+  if (scatter == nullptr)
+    for (int i = 0; i < 3; ++i)
+      if (o_strides[i] <= 0 || o_strides[i] % 8 != 0) return cudaErrorInvalidValue;
+  if (fp8 != nullptr) {
+    if (!fp8->q_scale || !fp8->k_scale || !fp8->v_scale) return cudaErrorInvalidValue;
+    // the kernel reads K scales 128 keys at a time: the scale rows are padded to whole tiles
+    if (fp8->scale_seq < ((seq_k + 127) / 128) * 128 || fp8->scale_seq < seq_q ||
+        fp8->scale_seq % 4 != 0 || reinterpret_cast<uintptr_t>(fp8->k_scale) % 16)
+      return cudaErrorInvalidValue;
+  }
   if (scatter != nullptr) {
     if (scatter->world < 1 || scatter->world > COZY_MAX_PEERS || scatter->head_offset < 0)
       return cudaErrorInvalidValue;
@@ -629,15 +759,16 @@ int attention_forward(const void* q, const void* k, const void* v, void* out, in
         if (scatter->strides[w][i] <= 0 || scatter->strides[w][i] % 8) return cudaErrorInvalidValue;
     }
   }
+  const int eb = fp8 != nullptr ? 1 : 2;
   CUtensorMap mq, mk, mv;
   int e;
-  if ((e = make_map(&mq, q, head_dim, seq_q, heads_q, batch, q_strides[0], q_strides[1],
+  if ((e = make_map(&mq, q, eb, head_dim, seq_q, heads_q, batch, q_strides[0], q_strides[1],
                     q_strides[2])))
     return e;
-  if ((e = make_map(&mk, k, head_dim, seq_k, heads_kv, batch, k_strides[0], k_strides[1],
+  if ((e = make_map(&mk, k, eb, head_dim, seq_k, heads_kv, batch, k_strides[0], k_strides[1],
                     k_strides[2])))
     return e;
-  if ((e = make_map(&mv, v, head_dim, seq_k, heads_kv, batch, v_strides[0], v_strides[1],
+  if ((e = make_map(&mv, v, eb, head_dim, seq_k, heads_kv, batch, v_strides[0], v_strides[1],
                     v_strides[2])))
     return e;
   AttentionParams p;
@@ -671,8 +802,41 @@ int attention_forward(const void* q, const void* k, const void* v, void* out, in
       for (int i = 0; i < 3; ++i) p.outs_strides[w][i] = scatter->strides[w][i];
     }
   }
-  if (head_dim == 128) return launch<128>(mq, mk, mv, p, stream);
-  return launch<64>(mq, mk, mv, p, stream);
+  p.q_scale = p.k_scale = p.v_scale = nullptr;
+  p.scale_seq = 0;
+  if (fp8 != nullptr) {
+    p.q_scale = fp8->q_scale;
+    p.k_scale = fp8->k_scale;
+    p.v_scale = fp8->v_scale;
+    p.scale_seq = fp8->scale_seq;
+    return launch<128, true>(mq, mk, mv, p, stream);
+  }
+  if (head_dim == 128) return launch<128, false>(mq, mk, mv, p, stream);
+  return launch<64, false>(mq, mk, mv, p, stream);
+}
+
+int attention_forward(const void* q, const void* k, const void* v, void* out, int batch,
+                      int seq_q, int seq_k, int heads_q, int heads_kv, int head_dim,
+                      const long long* q_strides, const long long* k_strides,
+                      const long long* v_strides, const long long* o_strides,
+                      const CozyHeadMap* head_map, const CozyScatter* scatter, int causal,
+                      float scale, int* status, cudaStream_t stream) {
+  return attention_launch(q, k, v, out, batch, seq_q, seq_k, heads_q, heads_kv, head_dim,
+                          q_strides, k_strides, v_strides, o_strides, head_map, scatter, causal,
+                          scale, status, nullptr, stream);
+}
+
+int attention_forward_fp8(const void* q, const void* k, const void* v, const float* q_scale,
+                          const float* k_scale, const float* v_scale, long long scale_seq,
+                          void* out, int batch, int seq_q, int seq_k, int heads_q, int heads_kv,
+                          int head_dim, const long long* q_strides, const long long* k_strides,
+                          const long long* v_strides, const long long* o_strides,
+                          const CozyHeadMap* head_map, const CozyScatter* scatter, int causal,
+                          float scale, int* status, cudaStream_t stream) {
+  const Fp8Operands fp8 = {q_scale, k_scale, v_scale, scale_seq};
+  return attention_launch(q, k, v, out, batch, seq_q, seq_k, heads_q, heads_kv, head_dim,
+                          q_strides, k_strides, v_strides, o_strides, head_map, scatter, causal,
+                          scale, status, &fp8, stream);
 }
 
 }  // namespace cozy

@@ -1,0 +1,196 @@
+// The FP8 first stage of the exchange: e4m3 Q, K and V crossing the wire with their scales.
+//
+// Recipe (the FP8 video configuration): K less its per-(batch, head) mean over the WHOLE
+// sequence (attention is unchanged by a shift of every key; the reference's narrow wire does the
+// same with one all-reduce, src/cozy_runtime/internal/parallel/ulysses.py:588-604); Q and K
+// quantised with one fp32 scale per 64-token × head block, scale = max(absmax / 448, 1e-12)
+// (the reference's per-head law, src/cozy_runtime/internal/attention_fp8.py:162-169, at block
+// granularity; blocks start at each rank's first row); V quantised with one fp32 scale per
+// (batch, head, channel) over the whole sequence. Codes are round-to-nearest-even, saturating.
+//
+// fp8_stats_kernel: this rank's partial K sums and V channel absmax (the host all-reduces them).
+// fp8_pack_kernel:  one CTA per (64-row block, head, batch) of one tensor: rows loaded once,
+//                   mean subtracted, block absmax reduced in the CTA, codes written to every
+//                   peer that owns the head, one scale per row to its per-token scale array.
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/cozy_ulysses.h"
+
+namespace cozy {
+
+constexpr float kE4M3Max = 448.0f;
+constexpr float kScaleFloor = 1e-12f;
+
+__global__ void __launch_bounds__(128) fp8_stats_kernel(CozyFp8Stats a) {
+  const int d = threadIdx.x;  // one channel per thread (head_dim 128)
+  const int head = blockIdx.y, b = blockIdx.z;
+  const int r0 = blockIdx.x * 256;
+  const int r1 = min(a.rows, r0 + 256);
+  const __nv_bfloat16* k = static_cast<const __nv_bfloat16*>(a.key) + b * a.k_strides[2] +
+                           head * a.k_strides[1] + d;
+  const __nv_bfloat16* v = static_cast<const __nv_bfloat16*>(a.value) + b * a.v_strides[2] +
+                           head * a.v_strides[1] + d;
+  float sum = 0.f, amax = 0.f;
+  for (int r = r0; r < r1; ++r) {
+    sum += __bfloat162float(k[r * a.k_strides[0]]);
+    amax = fmaxf(amax, fabsf(__bfloat162float(v[r * a.v_strides[0]])));
+  }
+  const int o = (b * a.heads + head) * 128 + d;
+  atomicAdd(a.k_sum + o, sum);
+  // non-negative floats order like their bit patterns
+  atomicMax(reinterpret_cast<unsigned int*>(a.v_amax) + o, __float_as_uint(amax));
+}
+
+__device__ __forceinline__ uint32_t e4m3x4(float a, float b, float c, float d) {
+  uint16_t lo, hi;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %2, %1;" : "=h"(lo) : "f"(a), "f"(b));
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %2, %1;" : "=h"(hi) : "f"(c), "f"(d));
+  return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+}
+
+// blockIdx: x = 64-row block of this rank, y = head, z = batch * 3 + tensor (0 Q, 1 K, 2 V).
+// 256 threads: 16 per row (8 channels each), 16 rows per pass, 4 passes.
+__global__ void __launch_bounds__(256) fp8_pack_kernel(const CozyFp8Pack a) {
+  const int tensor = blockIdx.z % 3;
+  const int b = blockIdx.z / 3;
+  const int head = blockIdx.y;
+  const CozyFp8Tensor& t = a.t[tensor];
+  if (head >= t.heads) return;
+  const int chunk = threadIdx.x & 15;
+  const int row_in = threadIdx.x >> 4;
+  const int d0 = chunk * 8;
+  const int block0 = blockIdx.x * 64;
+  const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(t.src) + b * t.src_strides[2] +
+                             head * t.src_strides[1] + d0;
+  float mean[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (t.mean_sum != nullptr) {
+    const float* ms = t.mean_sum + (b * t.heads + head) * 128 + d0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) mean[i] = ms[i] * t.mean_inv_count;
+  }
+  float x[4][8];
+  float amax = 0.f;
+#pragma unroll
+  for (int pass = 0; pass < 4; ++pass) {
+    const int r = block0 + pass * 16 + row_in;
+    if (r < a.rows) {
+      const uint4 v = *reinterpret_cast<const uint4*>(src + r * t.src_strides[0]);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(h[i]);
+        x[pass][2 * i] = f.x - mean[2 * i];
+        x[pass][2 * i + 1] = f.y - mean[2 * i + 1];
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x[pass][i] = 0.f;
+    }
+  }
+  if (t.hadamard) {
+    // Fast Walsh-Hadamard transform of each row (128 channels, index bits 0-6): bits 0-2 are
+    // this thread's 8 channels, bits 3-6 its chunk, i.e. lanes 1, 2, 4, 8 apart in the row's
+    // group of 16. Butterfly (a, b) -> (a + b, a - b); then the orthonormal 1/sqrt(128).
+#pragma unroll
+    for (int pass = 0; pass < 4; ++pass) {
+#pragma unroll
+      for (int bit = 1; bit < 8; bit <<= 1)
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (!(i & bit)) {
+            const float u = x[pass][i], w = x[pass][i | bit];
+            x[pass][i] = u + w;
+            x[pass][i | bit] = u - w;
+          }
+#pragma unroll
+      for (int lanes = 1; lanes < 16; lanes <<= 1) {
+        const bool high = (chunk & lanes) != 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float other = __shfl_xor_sync(0xffffffffu, x[pass][i], lanes);
+          x[pass][i] = high ? other - x[pass][i] : x[pass][i] + other;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x[pass][i] *= 0.08838834764831845f;  // 1/sqrt(128)
+    }
+  }
+#pragma unroll
+  for (int pass = 0; pass < 4; ++pass)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(x[pass][i]));
+  float inv[8];
+  float scale = 0.f;
+  if (t.channel_scale != nullptr) {  // per-channel (V): scale from the global channel absmax
+    const float* cs = t.channel_scale + (b * t.heads + head) * 128 + d0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) inv[i] = 1.f / cs[i];
+  } else {  // per 64-token block: reduce the absmax over the CTA
+    __shared__ float warp_max[8];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    float m = warp_max[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) m = fmaxf(m, warp_max[w]);
+    scale = fmaxf(m / kE4M3Max, kScaleFloor);
+    const float is = 1.f / scale;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) inv[i] = is;
+  }
+  for (int p = 0; p < a.world; ++p) {
+    const int lo = t.head_lo[p], n = t.head_n[p];
+    if (head < lo || head >= lo + n) continue;
+    const int hh = head - lo;
+    uint8_t* dst = static_cast<uint8_t*>(t.dst[p]);
+    float* sdst = t.scale_dst[p];
+#pragma unroll
+    for (int pass = 0; pass < 4; ++pass) {
+      const int r = block0 + pass * 16 + row_in;
+      if (r >= a.rows) continue;
+      const uint2 codes = make_uint2(
+          e4m3x4(x[pass][0] * inv[0], x[pass][1] * inv[1], x[pass][2] * inv[2], x[pass][3] * inv[3]),
+          e4m3x4(x[pass][4] * inv[4], x[pass][5] * inv[5], x[pass][6] * inv[6], x[pass][7] * inv[7]));
+      // destination [rows][batch][n][128] bytes
+      *reinterpret_cast<uint2*>(dst + ((static_cast<long long>(r) * a.batch + b) * n + hh) * 128 + d0) =
+          codes;
+      if (sdst != nullptr && chunk == 0)  // per-token scales [batch][n][scale_seq] at this rank's row
+        sdst[(static_cast<long long>(b) * n + hh) * t.scale_seq + r] = scale;
+    }
+  }
+}
+
+int fp8_stats(const CozyFp8Stats* a, cudaStream_t stream) {
+  if (a->head_dim != 128 || a->rows < 0 || a->batch < 1 || a->heads < 1) return cudaErrorNotSupported;
+  if (a->rows == 0) return cudaSuccess;
+  dim3 grid((a->rows + 255) / 256, a->heads, a->batch);
+  fp8_stats_kernel<<<grid, 128, 0, stream>>>(*a);
+  return cudaGetLastError();
+}
+
+int fp8_pack(const CozyFp8Pack* a, cudaStream_t stream) {
+  if (a->head_dim != 128) return cudaErrorNotSupported;
+  if (a->world < 1 || a->world > COZY_MAX_PEERS || a->rows < 0 || a->batch < 1)
+    return cudaErrorInvalidValue;
+  int heads = 0;
+  for (int i = 0; i < 3; ++i) {
+    const CozyFp8Tensor& t = a->t[i];
+    if (t.src == nullptr || reinterpret_cast<uintptr_t>(t.src) % 16) return cudaErrorInvalidValue;
+    for (int k = 0; k < 3; ++k)
+      if (t.src_strides[k] % 8) return cudaErrorInvalidValue;
+    for (int p = 0; p < a->world; ++p)
+      if (t.head_n[p] > 0 && (t.dst[p] == nullptr || reinterpret_cast<uintptr_t>(t.dst[p]) % 8))
+        return cudaErrorInvalidValue;
+    heads = t.heads > heads ? t.heads : heads;
+  }
+  if (a->rows == 0) return cudaSuccess;
+  dim3 grid((a->rows + 63) / 64, heads, a->batch * 3);
+  fp8_pack_kernel<<<grid, 256, 0, stream>>>(*a);
+  return cudaGetLastError();
+}
+
+}  // namespace cozy

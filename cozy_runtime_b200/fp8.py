@@ -1,0 +1,156 @@
+"""The FP8 variant of the exchange's stages (the FP8 video configuration's recipe).
+
+Per rank and call: partial statistics of its rows (K sums, V channel absmax; `cozy_fp8_stats`),
+made global by the caller (one all-reduce each: SUM, MAX — the reference's `_Shift` does the
+K mean the same way, `src/cozy_runtime/internal/parallel/ulysses.py:588-604`); the first stage
+(`cozy_fp8_pack`) writes e4m3 codes of Q and K (one scale per 64-token × head block, K less the
+global mean, both rotated by the orthonormal Hadamard of order 128 first, as the reference's
+FA4-fp8 row does, `src/cozy_runtime/internal/attention_upstream.py:276-317`) and V (one scale per
+channel) into every peer's receive buffers with Q/K's
+per-token scales beside them; the attention (`cozy_attention_fwd_fp8`) reads the codes in place
+and writes bf16 output rows to their owners.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+from collections.abc import Sequence
+
+import torch
+from torch import Tensor
+
+from cozy_runtime_b200 import _lib, attention
+
+E4M3_MAX = 448.0
+SCALE_FLOOR = 1e-12
+BLOCK = 64
+
+
+def scale_seq(total: int) -> int:
+    """Per-token scale rows are padded to whole 128-key tiles (the kernel reads them so)."""
+    return -(-total // 128) * 128
+
+
+class Fp8Step:
+    """One rank's FP8 stages of one exchange (`ulysses.Plan` layout, `rank`)."""
+
+    def __init__(self, query: Tensor, key: Tensor, value: Tensor, layout, rank: int) -> None:
+        if query.shape[3] != 128:
+            raise ValueError("the FP8 path serves head_dim 128")
+        self.query, self.key, self.value = query, key, value
+        self.layout, self.rank = layout, rank
+        self.batch, self.mine, self.heads, self.dim = (int(n) for n in query.shape)
+        self.heads_kv = int(key.shape[2])
+        self.total = layout.total
+        self.sseq = scale_seq(self.total)
+
+    # --------------------------------------------------------------- statistics
+    def stats_into(self, k_sum: Tensor, v_amax: Tensor) -> None:
+        """Add this rank's K sums into `k_sum` and max its |V| into `v_amax` ([B, Hkv, 128] fp32)."""
+        st = _lib.Fp8Stats()
+        st.key = self.key.data_ptr()
+        st.value = self.value.data_ptr()
+        st.k_strides[:] = [self.key.stride(1), self.key.stride(2), self.key.stride(0)]
+        st.v_strides[:] = [self.value.stride(1), self.value.stride(2), self.value.stride(0)]
+        st.rows, st.batch, st.heads, st.head_dim = self.mine, self.batch, self.heads_kv, self.dim
+        st.k_sum, st.v_amax = k_sum.data_ptr(), v_amax.data_ptr()
+        code = _lib.load().cozy_fp8_stats(
+            ctypes.byref(st), torch.cuda.current_stream(self.query.device).cuda_stream
+        )
+        _lib.check("cozy_fp8_stats", code)
+
+    @staticmethod
+    def channel_scale(v_amax: Tensor) -> Tensor:
+        """V's per-channel scale from its global absmax: max(amax / 448, 1e-12)."""
+        return (v_amax / E4M3_MAX).clamp_(min=SCALE_FLOOR)
+
+    # --------------------------------------------------------------- first stage
+    def pack_to(
+        self,
+        k_sum: Tensor,
+        v_scale: Tensor,
+        q_dst: Sequence[int],
+        k_dst: Sequence[int],
+        v_dst: Sequence[int],
+        qs_dst: Sequence[int],
+        ks_dst: Sequence[int],
+    ) -> None:
+        """Codes into every peer's receive buffers (addresses of this rank's first row there)
+        and Q/K per-token scales into their scale arrays (addresses of this rank's first token)."""
+        lay = self.layout
+        pk = _lib.Fp8Pack()
+        pk.world, pk.rows, pk.batch, pk.head_dim = lay.world, self.mine, self.batch, self.dim
+        specs = [
+            (self.query, lay.q_lo, lay.q_n, q_dst, qs_dst, None, None),
+            (self.key, lay.kv_lo, lay.kv_n, k_dst, ks_dst, k_sum, None),
+            (self.value, lay.kv_lo, lay.kv_n, v_dst, None, None, v_scale),
+        ]
+        for i, (src, lo, n, dst, sdst, mean, chan) in enumerate(specs):
+            t = pk.t[i]
+            t.src = src.data_ptr()
+            t.src_strides[:] = [src.stride(1), src.stride(2), src.stride(0)]
+            t.heads = src.shape[2]
+            t.hadamard = int(i < 2)  # Q and K, as the reference's FA4-fp8 row rotates them
+            t.mean_sum = mean.data_ptr() if mean is not None else None
+            t.mean_inv_count = 1.0 / self.total
+            t.channel_scale = chan.data_ptr() if chan is not None else None
+            t.scale_seq = self.sseq
+            for p in range(lay.world):
+                t.dst[p] = dst[p]
+                t.scale_dst[p] = sdst[p] if sdst is not None else None
+                t.head_lo[p] = lo[p]
+                t.head_n[p] = n[p]
+        code = _lib.load().cozy_fp8_pack(
+            ctypes.byref(pk), torch.cuda.current_stream(self.query.device).cuda_stream
+        )
+        _lib.check("cozy_fp8_pack", code)
+
+    # --------------------------------------------------------------- attention
+    def attend(
+        self,
+        q8: Tensor,
+        k8: Tensor,
+        v8: Tensor,
+        qs: Tensor,
+        ks: Tensor,
+        v_scale_local: Tensor,
+        *,
+        causal: bool,
+        scale: float | None,
+        scatter: _lib.Scatter | None = None,
+        into: Tensor | None = None,
+    ) -> None:
+        """Attention over this rank's heads from its receive buffers (uint8 codes
+        [total][B][n][128], per-token scales [B][n][scale_seq], V scales [B][n_kv][128] of this
+        rank's K/V heads) into `into` ([B, total, n, 128] view) or to the owners (`scatter`)."""
+        lay, rank = self.layout, self.rank
+        qn, kvn = lay.q_n[rank], lay.kv_n[rank]
+        if not qn:
+            return
+        total, batch, dim = self.total, self.batch, self.dim
+        qv = q8[: total * batch * qn * dim].view(total, batch, qn, dim).permute(1, 0, 2, 3)
+        kv = k8[: total * batch * kvn * dim].view(total, batch, kvn, dim).permute(1, 0, 2, 3)
+        vv = v8[: total * batch * kvn * dim].view(total, batch, kvn, dim).permute(1, 0, 2, 3)
+
+        def strides(t: Tensor):
+            return _lib.strides3((t.stride(1), t.stride(2), t.stride(0)))
+
+        head_map = _lib.HeadMap(lay.group, lay.q_lo[rank], lay.kv_lo[rank])
+        sc = 1.0 / math.sqrt(dim) if scale is None else float(scale)
+        code = _lib.load().cozy_attention_fwd_fp8(
+            qv.data_ptr(), kv.data_ptr(), vv.data_ptr(), qs.data_ptr(), ks.data_ptr(),
+            v_scale_local.data_ptr(), self.sseq,
+            None if into is None else into.data_ptr(),
+            batch, total, total, qn, kvn, dim,
+            strides(qv), strides(kv), strides(vv), None if into is None else strides(into),
+            ctypes.byref(head_map), None if scatter is None else ctypes.byref(scatter),
+            int(causal), sc, attention.status_word(self.query.device).data_ptr(),
+            torch.cuda.current_stream(self.query.device).cuda_stream,
+        )
+        _lib.check("cozy_attention_fwd_fp8", code)
+
+    def local_v_scale(self, v_scale: Tensor) -> Tensor:
+        """V scales of this rank's K/V heads, contiguous [B, n_kv, 128]."""
+        lo, n = self.layout.kv_lo[self.rank], self.layout.kv_n[self.rank]
+        return v_scale[:, lo : lo + n].contiguous()

@@ -116,6 +116,70 @@ COZY_API int cozy_ulysses_land(const void* returned, int world, int rows, int ba
                       const int* head_lo, const int* head_n, void* out,
                       const long long* out_strides, uintptr_t stream);
 
+/* ------------------------------------------------------------------------------- FP8 path
+ * The FP8 recipe of the video configuration: K less its per-(batch, head) mean over the whole
+ * sequence (the reference's narrow wire shifts K the same way, with one all-reduce:
+ * src/cozy_runtime/internal/parallel/ulysses.py:588-604), Q and K as e4m3 with one fp32 scale
+ * per 64-token × head block (max(absmax/448, 1e-12); blocks start at each rank's first row), V as
+ * e4m3 with one fp32 scale per (batch, head, channel) over the whole sequence, P as e4m3,
+ * softmax and accumulation in fp32. The per-head law is src/cozy_runtime/internal/
+ * attention_fp8.py:162-169 (`quantise_eager`); the reference's B200 FP8 kernel is FA4-fp8
+ * (attention_upstream.py:293-317). head_dim 128. */
+
+/* This rank's partial statistics: k_sum[b][h][d] += Σ_rows key, v_amax[b][h][d] = max(|value|)
+ * (the caller zero-fills both and all-reduces them: SUM and MAX). */
+typedef struct CozyFp8Stats {
+  const void* key;
+  const void* value;
+  long long k_strides[3];
+  long long v_strides[3];
+  int rows, batch, heads, head_dim;
+  float* k_sum;
+  float* v_amax;
+} CozyFp8Stats;
+
+/* One tensor of the FP8 first stage. Block mode (Q, K): `channel_scale` NULL; the per-token
+ * scale of row r goes to scale_dst[p][(b * head_n[p] + h) * scale_seq + r] (point scale_dst[p]
+ * at this rank's first row). Channel mode (V): codes = x / channel_scale[b][h][d], no per-token
+ * scales. `mean_sum` (K): subtracts mean_sum[b][h][d] * mean_inv_count. `hadamard` (Q and K):
+ * the row times the orthonormal Hadamard matrix (QKᵀ is unchanged; a channel outlier spreads over
+ * the head before its block scale is taken), as the reference's FA4-fp8 path rotates Q and K
+ * (src/cozy_runtime/internal/attention_upstream.py:276-317). Codes go to dst[p] as
+ * [rows][batch][head_n[p]][128] bytes, as CozyPackTensor. */
+typedef struct CozyFp8Tensor {
+  const void* src;
+  long long src_strides[3];
+  int heads;
+  int hadamard;             /* rotate each row by the orthonormal Hadamard of order 128 first */
+  const float* mean_sum;
+  float mean_inv_count;
+  const float* channel_scale;
+  void* dst[COZY_MAX_PEERS];
+  float* scale_dst[COZY_MAX_PEERS];
+  long long scale_seq;
+  int head_lo[COZY_MAX_PEERS];
+  int head_n[COZY_MAX_PEERS];
+} CozyFp8Tensor;
+
+typedef struct CozyFp8Pack {
+  CozyFp8Tensor t[3]; /* Q, K, V */
+  int world, rows, batch, head_dim;
+} CozyFp8Pack;
+
+COZY_API int cozy_fp8_stats(const CozyFp8Stats* stats, uintptr_t stream);
+COZY_API int cozy_fp8_pack(const CozyFp8Pack* pack, uintptr_t stream);
+
+/* cozy_attention_fwd on e4m3 operands: q/k/v codes with element (= byte) strides, each a
+ * multiple of 16; q_scale/k_scale per token [batch][heads][scale_seq] (scale_seq ≥ seq_k
+ * rounded up to 128, padding zero), v_scale [batch][heads_kv][128]. Output bf16. */
+COZY_API int cozy_attention_fwd_fp8(
+    const void* q, const void* k, const void* v, const float* q_scale, const float* k_scale,
+    const float* v_scale, long long scale_seq, void* out, int batch, int seq_q, int seq_k,
+    int heads_q, int heads_kv, int head_dim, const long long* q_strides,
+    const long long* k_strides, const long long* v_strides, const long long* o_strides,
+    const CozyHeadMap* head_map, const CozyScatter* scatter, int causal, float scale,
+    int* status, uintptr_t stream);
+
 /* ------------------------------------------------------------ allocation-free degree-1 call
  * No counterpart in the reference: an addition for callers that must not allocate device memory
  * while they run — a stream being captured into a CUDA graph (cudaMalloc cannot be captured), a

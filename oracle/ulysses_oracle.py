@@ -171,6 +171,75 @@ def quantise_e4m3_per_head(x: Tensor) -> tuple[Tensor, Tensor]:
     return scaled.to(torch.float8_e4m3fn), descale.contiguous()
 
 
+def fp8_attention_law(
+    queries: Sequence[Tensor],
+    keys: Sequence[Tensor],
+    values: Sequence[Tensor],
+    *,
+    causal: bool = False,
+    block: int = 64,
+    p_scale: float = 256.0,
+    hadamard: bool = True,
+) -> Tensor:
+    """The FP8 recipe of the video configuration over W ranks' rows, in fp32, returning the whole
+    [B, S, H, D] output: K less its per-(batch, head) mean over the whole sequence (the shift of
+    src/cozy_runtime/internal/parallel/ulysses.py:588-604); Q and K rotated by the orthonormal
+    Hadamard (the reference's FA4-fp8 row, attention_upstream.py:293-317); Q and K as e4m3 with one scale per
+    `block` rows × head, blocks starting at each rank's first row (`quantise_fp8_blocks` per
+    rank); V as e4m3 with one scale per (batch, head, channel) over the whole sequence
+    (max(absmax/448, 1e-12)); P = exp(s - rowmax) · `p_scale` as e4m3; the row sum over the
+    unquantised P; O = (P codes · V codes) · V scale / row sum. Grouped K/V heads as
+    `attention_fp32`."""
+    q = torch.cat(list(queries), dim=1).float()
+    k = torch.cat(list(keys), dim=1).float()
+    v = torch.cat(list(values), dim=1).float()
+    k = k - k.mean(dim=1, keepdim=True)
+    if hadamard:  # src/cozy_runtime/internal/attention_upstream.py:276-287 (`_hadamard`)
+        h = hadamard_matrix(q.shape[-1])
+        q, k = q @ h, k @ h
+    starts = [0]
+    for part in queries:
+        starts.append(starts[-1] + int(part.shape[1]))
+
+    def blocks(x: Tensor) -> Tensor:
+        out = torch.empty_like(x)
+        for a, b in zip(starts[:-1], starts[1:], strict=True):
+            codes, descale = quantise_fp8_blocks(x[:, a:b], block)
+            scale = descale.repeat_interleave(block, dim=1)[:, : b - a]
+            out[:, a:b] = codes.float() * scale[..., None]
+        return out
+
+    qd, kd = blocks(q), blocks(k)
+    vamax = v.abs().amax(dim=1, keepdim=True)
+    vscale = (vamax / E4M3_MAX).clamp(min=SCALE_FLOOR)
+    vcodes = (v / vscale).clamp(-E4M3_MAX, E4M3_MAX).to(torch.float8_e4m3fn).float()
+    batch, seq, hq, dim = q.shape
+    group = hq // k.shape[2]
+    out = torch.empty(batch, seq, hq, dim)
+    mask = None
+    if causal:
+        mask = torch.arange(seq)[None, :] > torch.arange(seq)[:, None]
+    for b in range(batch):
+        for h in range(hq):
+            s = (qd[b, :, h] @ kd[b, :, h // group].T) / math.sqrt(dim)
+            if mask is not None:
+                s = s.masked_fill(mask, float("-inf"))
+            p = torch.exp(s - s.amax(dim=-1, keepdim=True)) * p_scale
+            pq = p.clamp(max=E4M3_MAX).to(torch.float8_e4m3fn).float()
+            o = pq @ vcodes[b, :, h // group]
+            out[b, :, h] = o * vscale[b, 0, h // group] / p.sum(dim=-1, keepdim=True)
+    return out
+
+
+def hadamard_matrix(n: int) -> Tensor:
+    """The orthonormal Sylvester Hadamard matrix of order n (a power of two), built as
+    src/cozy_runtime/internal/attention_upstream.py:276-287 (`_hadamard`) builds it."""
+    h = torch.ones(1, 1)
+    while h.shape[0] < n:
+        h = torch.cat([torch.cat([h, h], 1), torch.cat([h, -h], 1)])
+    return h / math.sqrt(n)
+
+
 def quantise_fp8_blocks(x: Tensor, block: int = 64) -> tuple[Tensor, Tensor]:
     """e4m3 with one fp32 descale per `block` tokens × head: descale = max(amax/448, 1e-12) of the
     block, codes = RTNE(x/descale) clamped to ±448. This is the block form of the per-head law
