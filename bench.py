@@ -44,6 +44,13 @@ CONFIGS = {
         "batch": 2, "heads": 24, "heads_kv": 24, "dim": 128, "seq": 4608, "causal": False,
         "rope": ("axial", (1, 64, 64), (16, 56, 56), 10000.0, 512, 0), "norm": True, "amp": 1.0,
     },
+    "c4": {
+        "workload": "C4 FP8 video attention: B=1 H=40 D=128 S=21x45x80=75600, non-causal; Q/K "
+        "e4m3 with one scale per 64-token x head block (Hadamard turn, K less its global mean), "
+        "V e4m3 per-channel scales, P e4m3, fp32 softmax/accumulation; N(0,1), 1% of K x8",
+        "batch": 1, "heads": 40, "heads_kv": 40, "dim": 128, "seq": 75600, "causal": False,
+        "rope": None, "norm": False, "amp": 1.0, "fp8": True, "k_outliers": 0.01,
+    },
     "c5": {
         "workload": "C5 causal GQA prefill: B=1 Hq=32 Hkv=8 D=128 S=131071, causal, "
         "1D RoPE theta 500000",
@@ -65,6 +72,8 @@ def layer_flops(cfg: dict, heads: int | None = None) -> float:
 def make_rope(cfg: dict):
     from cozy_runtime_b200 import rope
 
+    if cfg["rope"] is None:
+        return None
     kind = cfg["rope"][0]
     if kind == "axial":
         _, grid, dims, theta, before, after = cfg["rope"]
@@ -72,11 +81,17 @@ def make_rope(cfg: dict):
     return rope.llama(cfg["seq"], cfg["dim"], cfg["rope"][1])
 
 
-def peaks() -> tuple[float, str]:
+def peaks(fp8: bool = False) -> tuple[float, str]:
+    """The tensor roofline denominator. FP8 has no measured figure on this pool: twice the
+    measured bf16 burst (the dense e4m3:bf16 ratio of the part), labelled as such."""
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
         data = json.loads(path.read_text())
+        if fp8:
+            return 2 * float(data["bf16_tflops"]), "2 x measured bf16 burst (MEASURED_PEAKS.json)"
         return float(data["bf16_tflops"]), "measured (MEASURED_PEAKS.json bf16_tflops, burst)"
+    if fp8:
+        return 2 * FALLBACK_BF16_TFLOPS, "2 x fallback bf16"
     return FALLBACK_BF16_TFLOPS, "fallback"
 
 
@@ -328,12 +343,17 @@ def main() -> None:
             torch.bfloat16)
 
     q, k, v = randn(heads), randn(hkv), randn(hkv)
-    spec = make_rope(cfg).to(device)
+    if cfg.get("k_outliers"):
+        hit = torch.rand(k.shape, generator=gen, device=device) < cfg["k_outliers"]
+        k = torch.where(hit, k * 8, k)
+    spec = make_rope(cfg)
+    spec = spec.to(device) if spec is not None else None
     norm = ulysses.Norm() if cfg["norm"] else None
+    fp8 = bool(cfg.get("fp8"))
 
     def step(qq, kk, vv):
         return ulysses.exchange(qq, kk, vv, group, None, rows=rows, causal=cfg["causal"],
-                                rope=spec, norm_q=norm, norm_k=norm)
+                                rope=spec, norm_q=norm, norm_k=norm, fp8=fp8)
 
     for _ in range(args.warmup):
         step(q, k, v)
@@ -402,9 +422,12 @@ def main() -> None:
 
     flops = layer_flops(cfg)
     if rank == 0:
-        peak, peak_src = peaks()
+        peak, peak_src = peaks(fp8)
         ach = achieved.item()
-        per_step = 2 + (1 if world > 1 else 0)  # pack + attention (+ land)
+        # my kernels a step: first stage + attention, then per transport the land (NCCL) or
+        # two signal and two wait kernels (peer); FP8 adds the statistics kernel
+        transport = os.environ.get("COZY_ULYSSES_TRANSPORT", "peer")
+        per_step = 2 + (0 if world == 1 else (1 if transport == "nccl" else 4)) + (1 if fp8 else 0)
         profile = ROOT / "profiles" / f"attention_fwd_{args.config}_traffic.json"
         traffic = None
         if profile.exists():
@@ -420,7 +443,7 @@ def main() -> None:
             "higher_is_better": True,
             "scaling": "strong",
             "vs_baseline": None,
-            "dtype": "bf16",
+            "dtype": "e4m3" if fp8 else "bf16",
             "data": "synthetic",
             "config": {
                 "workload": cfg["workload"],
@@ -452,7 +475,7 @@ def main() -> None:
             "gpu_launches": per_step * args.steps,
             "roofline": {
                 "bound": "tensor",
-                "kernel": "attention_fwd_kernel<128>",
+                "kernel": f"attention_fwd_kernel<128, {'true' if fp8 else 'false'}>",
                 "achieved": round(ach, 2),
                 "peak": peak,
                 "unit": "TFLOP/s",

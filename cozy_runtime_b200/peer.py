@@ -36,10 +36,10 @@ QKV, OUT = 0, 1
 class _Ptr:
     """A CUDA array interface over raw device memory, to view it as a torch tensor."""
 
-    def __init__(self, ptr: int, numel: int) -> None:
+    def __init__(self, ptr: int, nbytes: int) -> None:
         self.__cuda_array_interface__ = {
-            "shape": (numel,),
-            "typestr": "<i2",
+            "shape": (nbytes,),
+            "typestr": "|u1",
             "data": (ptr, False),
             "version": 3,
             "strides": None,
@@ -47,8 +47,9 @@ class _Ptr:
         }
 
 
-def _tensor(ptr: int, numel: int, device: torch.device) -> torch.Tensor:
-    return torch.as_tensor(_Ptr(ptr, numel), device=device).view(torch.bfloat16)
+def _tensor(ptr: int, nbytes: int, device: torch.device) -> torch.Tensor:
+    """Bytes at `ptr` as a uint8 tensor (callers `.view()` the dtype they store)."""
+    return torch.as_tensor(_Ptr(ptr, nbytes), device=device)
 
 
 class _Alloc:
@@ -70,9 +71,6 @@ class _Alloc:
 class PeerGroup:
     """One rank's view of a group's mapped buffers."""
 
-    #: buffers per set: q, k, v receive; landing
-    KINDS = ("q", "k", "v", "land")
-
     def __init__(self, handle, device: torch.device) -> None:
         self.handle = handle
         self.device = device
@@ -80,14 +78,13 @@ class PeerGroup:
         self.world = dist.get_world_size(handle)
         self.seq = 0
         self.lock = threading.Lock()
-        self.sizes: tuple[int, ...] | None = None  # elements per kind, this rank
+        self.sizes: dict[str, int] = {}  # bytes per named buffer (one of each per set)
         self.local: dict[tuple[int, str], _Alloc] = {}
-        self.peer_ptrs: dict[tuple[int, int, str], int] = {}  # (peer, set, kind) -> address
+        self.peer_ptrs: dict[tuple[int, int, str], int] = {}  # (peer, set, name) -> address
         self.opened: list[ctypes.c_void_p] = []
         self.views: dict[tuple[int, str], torch.Tensor] = {}
         self.flags = _Alloc(2 * self.world * 8)
         self.peer_flags = self._exchange_handles({("flags", 0): self.flags})
-        self.flag_view = {}
 
     # ------------------------------------------------------------------ mapping
     def _exchange_handles(self, allocs: dict) -> dict:
@@ -109,25 +106,27 @@ class PeerGroup:
                 out[(peer, key)] = ptr.value
         return out
 
-    def ensure(self, sizes: tuple[int, ...]) -> None:
-        """Map buffers of at least `sizes` elements (q, k, v, landing) on every rank. Every rank
-        calls with sizes that follow from the same agreed rows, so all decide alike."""
-        if self.sizes is not None and all(n <= have for n, have in zip(sizes, self.sizes)):
+    def ensure(self, sizes: dict[str, int]) -> None:
+        """Map two sets of buffers named as `sizes` (bytes; at least that large) on every rank.
+        Every rank calls with sizes that follow from the same agreed rows, so all decide alike;
+        a set only grows."""
+        if all(self.sizes.get(name, -1) >= n for name, n in sizes.items()):
             return
-        grow = sizes if self.sizes is None else tuple(max(a, b) for a, b in zip(sizes, self.sizes))
+        grow = dict(self.sizes)
+        for name, n in sizes.items():
+            grow[name] = max(n, grow.get(name, 0))
         torch.cuda.synchronize(self.device)
         self._release_sets()
         dist.barrier(group=self.handle)
         allocs = {}
         for s in (0, 1):
-            for kind, n in zip(self.KINDS, grow, strict=True):
-                allocs[(kind, s)] = self.local[(s, kind)] = _Alloc(max(16, n * 2))
+            for name, n in sorted(grow.items()):
+                allocs[(name, s)] = self.local[(s, name)] = _Alloc(max(256, -(-n // 256) * 256))
         ptrs = self._exchange_handles(allocs)
-        for (peer, (kind, s)), addr in ptrs.items():
-            self.peer_ptrs[(peer, s, kind)] = addr
-        for s in (0, 1):
-            for kind, n in zip(self.KINDS, grow, strict=True):
-                self.views[(s, kind)] = _tensor(self.local[(s, kind)].ptr.value, n, self.device)
+        for (peer, (name, s)), addr in ptrs.items():
+            self.peer_ptrs[(peer, s, name)] = addr
+        for (s, name), alloc in self.local.items():
+            self.views[(s, name)] = _tensor(alloc.ptr.value, grow[name], self.device)
         self.sizes = grow
 
     def _release_sets(self) -> None:
@@ -163,8 +162,9 @@ class PeerGroup:
     def peer(self, peer: int, s: int, kind: str) -> int:
         return self.peer_ptrs[(peer, s, kind)]
 
-    def view(self, s: int, kind: str) -> torch.Tensor:
-        return self.views[(s, kind)]
+    def view(self, s: int, kind: str, dtype: torch.dtype = torch.uint8) -> torch.Tensor:
+        """This rank's buffer `kind` of set `s` as a flat tensor of `dtype`."""
+        return self.views[(s, kind)].view(dtype)
 
     def signal(self, kind: int, seq: int) -> None:
         """Store `seq` into this rank's flag of `kind` in every rank's memory."""

@@ -36,6 +36,7 @@ import torch.distributed as dist
 from torch import Tensor
 
 from cozy_runtime_b200 import _lib, attention, peer
+from cozy_runtime_b200 import fp8 as fp8_mod
 from cozy_runtime_b200.rope import RopeSpec
 
 Compute = Callable[[Tensor, Tensor, Tensor], Tensor]
@@ -454,6 +455,7 @@ def exchange(
     norm_q: Norm | None = None,
     norm_k: Norm | None = None,
     transport: str | None = None,
+    fp8: bool = False,
 ) -> Tensor:
     """Sequence shards -> whole sequences per head subset -> attention -> back.
 
@@ -463,7 +465,10 @@ def exchange(
     to Q and K by global position in the first stage; `norm_q`/`norm_k`: per-head RMSNorm before
     it. `transport`: "peer" (in-kernel NVLink stores between the GPUs of one node) or "nccl"
     (NCCL all-to-all); default `COZY_ULYSSES_TRANSPORT`, else "peer" for native attention on a
-    CUDA group of one node. Returns [B, S_r, H, D] in the query's dtype.
+    CUDA group of one node. `fp8`: Q, K and V cross and multiply as e4m3 (`fp8.Fp8Step`: K less
+    its global mean, Q/K Hadamard-rotated with 64-token block scales, V per-channel scales, P as
+    e4m3; head_dim 128, native attention, degree 1 or the peer transport). Returns
+    [B, S_r, H, D] in the query's dtype.
     """
     wide = narrow(0) if callable(narrow) else narrow
     if wide:
@@ -494,6 +499,12 @@ def exchange(
     layout = plan(rows, heads, heads_kv)
     began = _Clock.mark(query)
 
+    if fp8:
+        if compute is not None or rope is not None or norm_q is not None or norm_k is not None:
+            raise NotImplementedError("the FP8 path serves native attention without RoPE/RMSNorm")
+        if world > 1 and _transport(handle, transport) != "peer":
+            raise NotImplementedError("the FP8 path crosses over the peer transport only")
+        return _exchange_fp8(query, key, value, handle, layout, rank, began, causal, scale)
     if world == 1 and rope is None and norm_q is None and norm_k is None and compute is None:
         out = torch.empty((batch, mine, heads, dim), dtype=query.dtype, device=query.device)
         first = _Clock.mark(query)
@@ -567,12 +578,13 @@ def _exchange_peer(
     device = query.device
     world, total = layout.world, layout.total
     rows = layout.rows
-    sizes = (
-        total * batch * max(layout.q_n) * dim,
-        total * batch * max(layout.kv_n) * dim,
-        total * batch * max(layout.kv_n) * dim,
-        batch * max(rows) * heads * dim,
-    )
+    el = query.element_size()
+    sizes = {
+        "q": total * batch * max(layout.q_n) * dim * el,
+        "k": total * batch * max(layout.kv_n) * dim * el,
+        "v": total * batch * max(layout.kv_n) * dim * el,
+        "land": batch * max(rows) * heads * dim * el,
+    }
     pg = peer.group_for(handle, device)
     status = attention.status_word(device).data_ptr()
     with pg.lock:
@@ -581,7 +593,6 @@ def _exchange_peer(
         s = seq & 1
         step = RankStep(query, key, value, layout, rank, rope=rope, norm_q=norm_q, norm_k=norm_k)
         start = layout.start(rank)
-        el = query.element_size()
         q_dst = [pg.peer(p, s, "q") + start * batch * layout.q_n[p] * dim * el for p in range(world)]
         k_dst = [pg.peer(p, s, "k") + start * batch * layout.kv_n[p] * dim * el for p in range(world)]
         v_dst = [pg.peer(p, s, "v") + start * batch * layout.kv_n[p] * dim * el for p in range(world)]
@@ -604,18 +615,123 @@ def _exchange_peer(
                 scatter.strides[p][2] = rows[p] * heads * dim
             scatter.row_start[world] = acc
             step.attend(
-                pg.view(s, "q")[: total * batch * qn * dim],
-                pg.view(s, "k")[: total * batch * kvn * dim],
-                pg.view(s, "v")[: total * batch * kvn * dim],
+                pg.view(s, "q", query.dtype)[: total * batch * qn * dim],
+                pg.view(s, "k", query.dtype)[: total * batch * kvn * dim],
+                pg.view(s, "v", query.dtype)[: total * batch * kvn * dim],
                 None, causal, scale, scatter=scatter,
             )
         last = _Clock.mark(query)
         pg.signal(peer.OUT, seq)
         pg.wait(peer.OUT, seq, status)
         out = torch.empty((batch, mine, heads, dim), dtype=query.dtype, device=device)
-        out.copy_(pg.view(s, "land")[: batch * mine * heads * dim].view(batch, mine, heads, dim))
+        land = pg.view(s, "land", query.dtype)[: batch * mine * heads * dim]
+        out.copy_(land.view(batch, mine, heads, dim))
     _CLOCK.add((began, first, last, _Clock.mark(query)), step.moved())
     return out
+
+
+def _exchange_fp8(
+    query: Tensor,
+    key: Tensor,
+    value: Tensor,
+    handle,
+    layout: Plan,
+    rank: int,
+    began,
+    causal: bool,
+    scale: float | None,
+) -> Tensor:
+    """The FP8 exchange: statistics all-reduced (K sums, V channel absmax), e4m3 codes and their
+    scales written into every owner's receive buffers (peer transport; local at degree 1), the
+    e4m3 attention, bf16 rows to their owners."""
+    batch, mine, heads, dim = (int(n) for n in query.shape)
+    heads_kv = int(key.shape[2])
+    device = query.device
+    world, total, rows = layout.world, layout.total, layout.rows
+    step = fp8_mod.Fp8Step(query, key, value, layout, rank)
+    k_sum = torch.zeros(batch, heads_kv, dim, dtype=torch.float32, device=device)
+    v_amax = torch.zeros(batch, heads_kv, dim, dtype=torch.float32, device=device)
+    step.stats_into(k_sum, v_amax)
+    if world > 1:
+        dist.all_reduce(k_sum, op=dist.ReduceOp.SUM, group=handle)
+        dist.all_reduce(v_amax, op=dist.ReduceOp.MAX, group=handle)
+    v_scale = fp8_mod.Fp8Step.channel_scale(v_amax)
+    v_local = step.local_v_scale(v_scale)
+    sseq = step.sseq
+    qn, kvn = layout.q_n[rank], layout.kv_n[rank]
+    if world == 1:
+        u8, f32 = torch.uint8, torch.float32
+        q8 = torch.empty(total * batch * qn * dim, dtype=u8, device=device)
+        k8 = torch.empty(total * batch * kvn * dim, dtype=u8, device=device)
+        v8 = torch.empty(total * batch * kvn * dim, dtype=u8, device=device)
+        qs = torch.zeros(batch * qn * sseq, dtype=f32, device=device)
+        ks = torch.zeros(batch * kvn * sseq, dtype=f32, device=device)
+        step.pack_to(k_sum, v_scale, [q8.data_ptr()], [k8.data_ptr()], [v8.data_ptr()],
+                     [qs.data_ptr()], [ks.data_ptr()])
+        out = torch.empty((batch, mine, heads, dim), dtype=query.dtype, device=device)
+        first = _Clock.mark(query)
+        step.attend(q8, k8, v8, qs, ks, v_local, causal=causal, scale=scale, into=out)
+        _CLOCK.add((began, first, _Clock.mark(query), _Clock.mark(query)), 0)
+        return out
+    sizes = {
+        "q8": total * batch * max(layout.q_n) * dim,
+        "k8": total * batch * max(layout.kv_n) * dim,
+        "v8": total * batch * max(layout.kv_n) * dim,
+        "qs": batch * max(layout.q_n) * sseq * 4,
+        "ks": batch * max(layout.kv_n) * sseq * 4,
+        "land": batch * max(rows) * heads * dim * query.element_size(),
+    }
+    pg = peer.group_for(handle, device)
+    status = attention.status_word(device).data_ptr()
+    with pg.lock:
+        pg.ensure(sizes)
+        seq = pg.next_seq()
+        s = seq & 1
+        start = layout.start(rank)
+        r = range(world)
+        step.pack_to(
+            k_sum, v_scale,
+            [pg.peer(p, s, "q8") + start * batch * layout.q_n[p] * dim for p in r],
+            [pg.peer(p, s, "k8") + start * batch * layout.kv_n[p] * dim for p in r],
+            [pg.peer(p, s, "v8") + start * batch * layout.kv_n[p] * dim for p in r],
+            [pg.peer(p, s, "qs") + start * 4 for p in r],
+            [pg.peer(p, s, "ks") + start * 4 for p in r],
+        )
+        pg.signal(peer.QKV, seq)
+        pg.wait(peer.QKV, seq, status)
+        first = _Clock.mark(query)
+        if qn:
+            scatter = _scatter(layout, rank, heads, dim, lambda p: pg.peer(p, s, "land"))
+            step.attend(
+                pg.view(s, "q8"), pg.view(s, "k8"), pg.view(s, "v8"),
+                pg.view(s, "qs", torch.float32), pg.view(s, "ks", torch.float32), v_local,
+                causal=causal, scale=scale, scatter=scatter,
+            )
+        last = _Clock.mark(query)
+        pg.signal(peer.OUT, seq)
+        pg.wait(peer.OUT, seq, status)
+        out = torch.empty((batch, mine, heads, dim), dtype=query.dtype, device=device)
+        land = pg.view(s, "land", query.dtype)[: batch * mine * heads * dim]
+        out.copy_(land.view(batch, mine, heads, dim))
+    _CLOCK.add((began, first, last, _Clock.mark(query)), 0)
+    return out
+
+
+def _scatter(layout: Plan, rank: int, heads: int, dim: int, landing) -> _lib.Scatter:
+    """Where each output row goes: owner p's landing buffer [B][rows_p][H][D] at `landing(p)`."""
+    sc = _lib.Scatter()
+    sc.world = layout.world
+    sc.head_offset = layout.q_lo[rank]
+    acc = 0
+    for p in range(layout.world):
+        sc.row_start[p] = acc
+        acc += layout.rows[p]
+        sc.out[p] = landing(p)
+        sc.strides[p][0] = heads * dim
+        sc.strides[p][1] = dim
+        sc.strides[p][2] = layout.rows[p] * heads * dim
+    sc.row_start[layout.world] = acc
+    return sc
 
 
 def _abort(handle) -> None:

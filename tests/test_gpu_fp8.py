@@ -119,3 +119,17 @@ def test_fp8_exchange(world, batch, seq, hq, hkv, causal):
     assert err.mean().item() <= 2.5e-3, f"vs law mean-abs {err.mean().item():.3e}"
     assert cos_law.min().item() >= 0.999, f"vs law cosine {cos_law.min().item():.5f}"
     assert cos.min().item() >= 0.995, f"cosine {cos.min().item():.5f}"
+
+
+def test_fp8_exchange_public_call_degree1():
+    """`ulysses.exchange(..., fp8=True)` at degree 1 against the oracle's FP8 law."""
+    from cozy_runtime_b200 import attention, ulysses
+
+    q, k, v = _inputs(1, 900, 3, 3, 77)
+    got = ulysses.exchange(q.cuda(), k.cuda(), v.cuda(), None, None, fp8=True)
+    torch.cuda.synchronize()
+    attention.check_status(torch.device("cuda"))
+    law = oracle.fp8_attention_law([q], [k], [v])
+    assert _cosine_per_head(got.float().cpu(), law).min().item() >= 0.999
+    exact = oracle.attention_fp32(q, k, v)
+    assert _cosine_per_head(got.float().cpu(), exact).min().item() >= 0.995

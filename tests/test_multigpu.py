@@ -32,7 +32,7 @@ def _port() -> int:
         return s.getsockname()[1]
 
 
-def _rank(rank, world, port, inputs, causal, outdir, rope_args, transport):
+def _rank(rank, world, port, inputs, causal, outdir, rope_args, transport, fp8=False):
     import torch.distributed as dist
 
     from cozy_runtime_b200 import rope as rope_mod
@@ -51,7 +51,7 @@ def _rank(rank, world, port, inputs, causal, outdir, rope_args, transport):
         spec = rope_mod.axial(rope_args[0], (44, 42, 42), after=rope_args[1]).to(device)
     outs = [
         ulysses.exchange(q, k, v, dist.group.WORLD, None, causal=causal, rope=spec,
-                         transport=transport)
+                         transport=transport, fp8=fp8)
         for _ in range(3)
     ]
     torch.cuda.synchronize()
@@ -65,11 +65,11 @@ def _rank(rank, world, port, inputs, causal, outdir, rope_args, transport):
     dist.destroy_process_group()
 
 
-def _run(inputs, world, causal=False, rope_args=None, transport="peer") -> torch.Tensor:
+def _run(inputs, world, causal=False, rope_args=None, transport="peer", fp8=False):
     import torch.multiprocessing as mp
 
     with tempfile.TemporaryDirectory() as tmp:
-        mp.spawn(_rank, args=(world, _port(), inputs, causal, tmp, rope_args, transport),
+        mp.spawn(_rank, args=(world, _port(), inputs, causal, tmp, rope_args, transport, fp8),
                  nprocs=world, join=True)
         return torch.cat([torch.load(os.path.join(tmp, f"{r}.pt")) for r in range(world)], dim=1)
 
@@ -116,3 +116,29 @@ def test_exchange_against_oracle(world, hq, hkv, causal, rotate, transport):
         q, k = (oracle.head_norm_rope(t.float(), spec.cos, spec.sin, rotary=128, interleaved=True,
                                       normalize=False).to(torch.bfloat16) for t in (q, k))
     _check(got, oracle.attention_fp32(q, k, v, causal=causal))
+
+
+@pytest.mark.parametrize("world,hq,hkv,causal", [(2, 4, 4, False), (8, 16, 16, False), (4, 8, 2, True)])
+def test_fp8_exchange_peer_against_law(world, hq, hkv, causal):
+    """The FP8 path over the NVLink transport (statistics all-reduced, e4m3 codes and scales
+    stored into the owners' buffers) against the oracle's FP8 law and exact attention."""
+    if world > _gpus():
+        pytest.skip(f"needs {world} GPUs")
+    g = torch.Generator().manual_seed(world * 7 + hq)
+    seq = 1000
+    q = torch.randn(1, seq, hq, 128, generator=g)
+    k = torch.randn(1, seq, hkv, 128, generator=g)
+    v = torch.randn(1, seq, hkv, 128, generator=g)
+    k = torch.where(torch.rand(k.shape, generator=g) < 0.01, k * 8, k)
+    q, k, v = (t.to(torch.bfloat16) for t in (q, k, v))
+    got = _run((q, k, v), world, causal=causal, fp8=True).float()
+    rows = [t.shape[0] for t in torch.tensor_split(torch.empty(seq), world)]
+    law = oracle.fp8_attention_law(*(torch.split(t, rows, dim=1) for t in (q, k, v)), causal=causal)
+
+    def cos(a, b):
+        a = a.permute(0, 2, 1, 3).reshape(a.shape[2], -1)
+        b = b.permute(0, 2, 1, 3).reshape(b.shape[2], -1)
+        return torch.nn.functional.cosine_similarity(a, b, dim=1).min().item()
+
+    assert cos(got, law) >= 0.999
+    assert cos(got, oracle.attention_fp32(q, k, v, causal=causal)) >= 0.995
