@@ -388,67 +388,65 @@ def main() -> None:
     ms_max, attn_max, exposed_max = stats.tolist()
 
     # ---- end to end through the public call, host buffers in and out every step
-    if args.no_e2e:
+    e2e_ms = h2d = d2h = None
+    if not args.no_e2e:
+        # Every step copies its own inputs in from pinned host memory and its output back out, inside
+        # the timed region; the copies run on their own streams, double-buffered, so step i+1's
+        # inputs cross PCIe while step i computes and step i's output crosses while i+1 computes.
+        hq = [t.cpu().pin_memory() for t in (q, k, v)]
+        slots = [[torch.empty_like(t) for t in (q, k, v)] for _ in range(2)]
+        host_outs = [torch.empty((batch, mine, heads, dim), dtype=torch.bfloat16).pin_memory()
+                     for _ in range(2)]
+        compute = torch.cuda.current_stream(device)
+        h2d_stream, d2h_stream = torch.cuda.Stream(device), torch.cuda.Stream(device)
+        loaded = [torch.cuda.Event() for _ in range(2)]
+        freed = [torch.cuda.Event() for _ in range(2)]
+
+        def issue_h2d(i):
+            s = i % 2
+            h2d_stream.wait_event(freed[s])  # the slot's previous step has read it
+            with torch.cuda.stream(h2d_stream):
+                for src, dst in zip(hq, slots[s], strict=True):
+                    dst.copy_(src, non_blocking=True)
+            loaded[s].record(h2d_stream)
+
+        def run_step(i):
+            s = i % 2
+            compute.wait_event(loaded[s])
+            out = step(*slots[s])
+            freed[s].record(compute)
+            d2h_stream.wait_event(freed[s])
+            with torch.cuda.stream(d2h_stream):
+                host_outs[s].copy_(out, non_blocking=True)
+            out.record_stream(d2h_stream)
+
+        def e2e_run(n):
+            for ev in freed:
+                ev.record(compute)
+            h2d_stream.wait_stream(compute)
+            d2h_stream.wait_stream(compute)
+            issue_h2d(0)
+            for i in range(n):
+                if i + 1 < n:
+                    issue_h2d(i + 1)
+                run_step(i)
+            compute.wait_stream(d2h_stream)
+
+        e2e_run(2)
+        torch.cuda.synchronize()
         if group is not None:
-            dist.destroy_process_group()
-        return
-    # Every step copies its own inputs in from pinned host memory and its output back out, inside
-    # the timed region; the copies run on their own streams, double-buffered, so step i+1's
-    # inputs cross PCIe while step i computes and step i's output crosses while i+1 computes.
-    hq = [t.cpu().pin_memory() for t in (q, k, v)]
-    slots = [[torch.empty_like(t) for t in (q, k, v)] for _ in range(2)]
-    host_outs = [torch.empty((batch, mine, heads, dim), dtype=torch.bfloat16).pin_memory()
-                 for _ in range(2)]
-    compute = torch.cuda.current_stream(device)
-    h2d_stream, d2h_stream = torch.cuda.Stream(device), torch.cuda.Stream(device)
-    loaded = [torch.cuda.Event() for _ in range(2)]
-    freed = [torch.cuda.Event() for _ in range(2)]
-
-    def issue_h2d(i):
-        s = i % 2
-        h2d_stream.wait_event(freed[s])  # the slot's previous step has read it
-        with torch.cuda.stream(h2d_stream):
-            for src, dst in zip(hq, slots[s], strict=True):
-                dst.copy_(src, non_blocking=True)
-        loaded[s].record(h2d_stream)
-
-    def run_step(i):
-        s = i % 2
-        compute.wait_event(loaded[s])
-        out = step(*slots[s])
-        freed[s].record(compute)
-        d2h_stream.wait_event(freed[s])
-        with torch.cuda.stream(d2h_stream):
-            host_outs[s].copy_(out, non_blocking=True)
-        out.record_stream(d2h_stream)
-
-    def e2e_run(n):
-        for ev in freed:
-            ev.record(compute)
-        h2d_stream.wait_stream(compute)
-        d2h_stream.wait_stream(compute)
-        issue_h2d(0)
-        for i in range(n):
-            if i + 1 < n:
-                issue_h2d(i + 1)
-            run_step(i)
-        compute.wait_stream(d2h_stream)
-
-    e2e_run(2)
-    torch.cuda.synchronize()
-    if group is not None:
-        dist.barrier()
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e2e_steps = max(3, args.steps // 2)
-    f0.record(compute)
-    e2e_run(e2e_steps)
-    f1.record(compute)
-    torch.cuda.synchronize()
-    e2e_ms = torch.tensor([f0.elapsed_time(f1) / e2e_steps], dtype=torch.float64, device=device)
-    if group is not None:
-        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-    h2d = sum(t.numel() * t.element_size() for t in hq)
-    d2h = host_outs[0].numel() * host_outs[0].element_size()
+            dist.barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e2e_steps = max(3, args.steps // 2)
+        f0.record(compute)
+        e2e_run(e2e_steps)
+        f1.record(compute)
+        torch.cuda.synchronize()
+        e2e_ms = torch.tensor([f0.elapsed_time(f1) / e2e_steps], dtype=torch.float64, device=device)
+        if group is not None:
+            dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+        h2d = sum(t.numel() * t.element_size() for t in hq)
+        d2h = host_outs[0].numel() * host_outs[0].element_size()
 
     flops = layer_flops(cfg)
     if rank == 0:
@@ -494,7 +492,7 @@ def main() -> None:
                 "exposed_frac": round(exposed_max / ms_max, 4) if ms_max else None,
             },
             "clocks": sampler.summary(),
-            "e2e": {
+            "e2e": None if e2e_ms is None else {
                 "value": round(flops / (e2e_ms.item() * 1e-3) / 1e12, 2),
                 "unit": "TFLOP/s",
                 "ms_per_step": round(e2e_ms.item(), 4),

@@ -124,6 +124,7 @@ class Fp8Pack(Structure):
         ("rows", c_int),
         ("batch", c_int),
         ("head_dim", c_int),
+        ("row0", c_int),
     ]
 
 
@@ -171,7 +172,8 @@ SIGNATURES = {
     "cozy_fp8_stats": ([POINTER(Fp8Stats), c_uint64], c_int),
     "cozy_fp8_pack": ([POINTER(Fp8Pack), c_uint64], c_int),
     "cozy_attention_fwd_fp8": (
-        [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_longlong, c_void_p,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_longlong,
+         POINTER(c_int), c_int, c_void_p,
          c_int, c_int, c_int, c_int, c_int, c_int,
          POINTER(c_longlong), POINTER(c_longlong), POINTER(c_longlong), POINTER(c_longlong),
          POINTER(HeadMap), POINTER(Scatter), c_int, c_float, c_void_p, c_uint64],

@@ -68,6 +68,10 @@ struct AttentionParams {
   const float* k_scale;
   const float* v_scale;
   long long scale_seq;
+  // rows where one rank's rows end and the next one's begin: the only places a 64-key block of
+  // K scales can change inside a 64-key half of a tile
+  int n_cuts;
+  int cuts[COZY_MAX_PEERS];
 };
 
 template <int HD, bool FP8>
@@ -349,12 +353,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       reg_fence(r2);
       reg_fence(r3);
       const int kv0 = j * kBlockN;
-      if constexpr (FP8) {  // scores of the codes times each key's scale
-        const float4* ks = reinterpret_cast<const float4*>(k_scale_row + kv0);
-        scale_chunk(r0, ks);
-        scale_chunk(r1, ks + 8);
-        scale_chunk(r2, ks + 16);
-        scale_chunk(r3, ks + 24);
+      // multipliers of the two 64-key halves (bf16: the softmax scale)
+      float sc_lo = scale, sc_hi = scale;
+      if constexpr (FP8) {
+        bool split = false;
+        for (int c = 0; c < p.n_cuts; ++c) {
+          const int cut = p.cuts[c];
+          split |= cut > kv0 && cut < kv0 + kBlockN && cut != kv0 + 64;
+        }
+        if (split) {  // a rank boundary inside a half: each key's own scale
+          const float4* ks = reinterpret_cast<const float4*>(k_scale_row + kv0);
+          scale_chunk(r0, ks);
+          scale_chunk(r1, ks + 8);
+          scale_chunk(r2, ks + 16);
+          scale_chunk(r3, ks + 24);
+        } else {  // one K block scale per half, folded into the exponent's multiplier
+          sc_lo = scale * k_scale_row[kv0];
+          sc_hi = scale * k_scale_row[kv0 + 64];
+          // keys past the sequence have scale 0 and are masked: keep the multiplier positive
+          if (!(sc_lo > 0.f)) sc_lo = scale;
+          if (!(sc_hi > 0.f)) sc_hi = scale;
+        }
       }
       const bool ragged = kv0 + kBlockN > p.seq_k;
       const bool diagonal = p.causal && kv0 + kBlockN - 1 > visible;
@@ -365,9 +384,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         mask_chunk(r2, limit - 64);
         mask_chunk(r3, limit - 96);
       }
-      // row max: four independent 3-input chains, one per chunk
-      const float mt = fmaxf(fmaxf(chunk_max(r0), chunk_max(r1)), fmaxf(chunk_max(r2), chunk_max(r3)));
-      const float m_new = fmaxf(m, mt * scale);
+      // row max: four independent 3-input chains, one per chunk, scaled per half
+      const float mlo = fmaxf(chunk_max(r0), chunk_max(r1));
+      const float mhi = fmaxf(chunk_max(r2), chunk_max(r3));
+      const float mt = fmaxf(mlo == -INFINITY ? -INFINITY : mlo * sc_lo,
+                             mhi == -INFINITY ? -INFINITY : mhi * sc_hi);
+      const float m_new = fmaxf(m, mt);
       if (j == 0) {
         m = m_new;
       } else if (__any_sync(0xffffffffu, m_new > m + (FP8 ? kRescaleLog2Fp8 : kRescaleLog2))) {
@@ -388,35 +410,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         m = m_new;
       }
       const float mu = (m == -INFINITY) ? 0.f : m;
-      const float2 scale2 = make_float2(scale, scale);
+      const float2 scale_lo = make_float2(sc_lo, sc_lo), scale_hi = make_float2(sc_hi, sc_hi);
       float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
       if constexpr (FP8) {
         // P as e4m3 codes of 2^(t + 8) (≤ 256·2^0.5 < 448); the row sum carries the same 2^8
         const float2 negm2 = make_float2(kPScaleLog2 - mu, kPScaleLog2 - mu);
         uint32_t pk[16];
-        exp_chunk_fp8(r0, scale2, negm2, acc0, pk);
-        exp_chunk_fp8(r1, scale2, negm2, acc1, pk + 8);
+        exp_chunk_fp8(r0, scale_lo, negm2, acc0, pk);
+        exp_chunk_fp8(r1, scale_lo, negm2, acc1, pk + 8);
         tmem_st16(tS + 0, pk);
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&p_ready[2 * s]);
-        exp_chunk_fp8(r2, scale2, negm2, acc0, pk);
-        exp_chunk_fp8(r3, scale2, negm2, acc1, pk + 8);
+        exp_chunk_fp8(r2, scale_hi, negm2, acc0, pk);
+        exp_chunk_fp8(r3, scale_hi, negm2, acc1, pk + 8);
         tmem_st16(tS + 16, pk);
       } else {
         const float2 negm2 = make_float2(-mu, -mu);
         uint32_t pk[16];
         // first half of P (keys 0..63): the MMA starts its product while the rest is formed
-        exp_chunk(r0, scale2, negm2, acc0, pk);
+        exp_chunk(r0, scale_lo, negm2, acc0, pk);
         tmem_st16(tS + 0, pk);
-        exp_chunk(r1, scale2, negm2, acc1, pk);
+        exp_chunk(r1, scale_lo, negm2, acc1, pk);
         tmem_st16(tS + 16, pk);
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&p_ready[2 * s]);
-        exp_chunk(r2, scale2, negm2, acc0, pk);
+        exp_chunk(r2, scale_hi, negm2, acc0, pk);
         tmem_st16(tS + 32, pk);
-        exp_chunk(r3, scale2, negm2, acc1, pk);
+        exp_chunk(r3, scale_hi, negm2, acc1, pk);
         tmem_st16(tS + 48, pk);
       }
       const float2 acc = __fadd2_rn(acc0, acc1);
@@ -701,6 +723,8 @@ struct Fp8Operands {
   const float* k_scale;
   const float* v_scale;
   long long scale_seq;
+  const int* cuts;
+  int n_cuts;
 };
 
 static int attention_launch(const void* q, const void* k, const void* v, void* out, int batch,
@@ -740,6 +764,8 @@ static int attention_launch(const void* q, const void* k, const void* v, void* o
       if (o_strides[i] <= 0 || o_strides[i] % 8 != 0) return cudaErrorInvalidValue;
   if (fp8 != nullptr) {
     if (!fp8->q_scale || !fp8->k_scale || !fp8->v_scale) return cudaErrorInvalidValue;
+    if (fp8->n_cuts < 0 || fp8->n_cuts > COZY_MAX_PEERS || (fp8->n_cuts > 0 && !fp8->cuts))
+      return cudaErrorInvalidValue;
     // the kernel reads K scales 128 keys at a time: the scale rows are padded to whole tiles
     if (fp8->scale_seq < ((seq_k + 127) / 128) * 128 || fp8->scale_seq < seq_q ||
         fp8->scale_seq % 4 != 0 || reinterpret_cast<uintptr_t>(fp8->k_scale) % 16)
@@ -804,11 +830,14 @@ static int attention_launch(const void* q, const void* k, const void* v, void* o
   }
   p.q_scale = p.k_scale = p.v_scale = nullptr;
   p.scale_seq = 0;
+  p.n_cuts = 0;
   if (fp8 != nullptr) {
     p.q_scale = fp8->q_scale;
     p.k_scale = fp8->k_scale;
     p.v_scale = fp8->v_scale;
     p.scale_seq = fp8->scale_seq;
+    p.n_cuts = fp8->n_cuts;
+    for (int c = 0; c < fp8->n_cuts; ++c) p.cuts[c] = fp8->cuts[c];
     return launch<128, true>(mq, mk, mv, p, stream);
   }
   if (head_dim == 128) return launch<128, false>(mq, mk, mv, p, stream);
@@ -828,12 +857,12 @@ int attention_forward(const void* q, const void* k, const void* v, void* out, in
 
 int attention_forward_fp8(const void* q, const void* k, const void* v, const float* q_scale,
                           const float* k_scale, const float* v_scale, long long scale_seq,
-                          void* out, int batch, int seq_q, int seq_k, int heads_q, int heads_kv,
+                          const int* cuts, int n_cuts, void* out, int batch, int seq_q, int seq_k, int heads_q, int heads_kv,
                           int head_dim, const long long* q_strides, const long long* k_strides,
                           const long long* v_strides, const long long* o_strides,
                           const CozyHeadMap* head_map, const CozyScatter* scatter, int causal,
                           float scale, int* status, cudaStream_t stream) {
-  const Fp8Operands fp8 = {q_scale, k_scale, v_scale, scale_seq};
+  const Fp8Operands fp8 = {q_scale, k_scale, v_scale, scale_seq, cuts, n_cuts};
   return attention_launch(q, k, v, out, batch, seq_q, seq_k, heads_q, heads_kv, head_dim,
                           q_strides, k_strides, v_strides, o_strides, head_map, scatter, causal,
                           scale, status, &fp8, stream);

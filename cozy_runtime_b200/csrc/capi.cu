@@ -63,7 +63,7 @@ int cozy_abi_version(void) { return 100; }
 namespace cozy {
 int attention_forward_fp8(const void* q, const void* k, const void* v, const float* q_scale,
                           const float* k_scale, const float* v_scale, long long scale_seq,
-                          void* out, int batch, int seq_q, int seq_k, int heads_q, int heads_kv,
+                          const int* cuts, int n_cuts, void* out, int batch, int seq_q, int seq_k, int heads_q, int heads_kv,
                           int head_dim, const long long* q_strides, const long long* k_strides,
                           const long long* v_strides, const long long* o_strides,
                           const CozyHeadMap* head_map, const CozyScatter* scatter, int causal,
@@ -87,14 +87,15 @@ int cozy_fp8_pack(const CozyFp8Pack* pack, uintptr_t stream) {
 
 int cozy_attention_fwd_fp8(const void* q, const void* k, const void* v, const float* q_scale,
                            const float* k_scale, const float* v_scale, long long scale_seq,
-                           void* out, int batch, int seq_q, int seq_k, int heads_q, int heads_kv,
+                           const int* cuts, int n_cuts, void* out, int batch, int seq_q, int seq_k, int heads_q, int heads_kv,
                            int head_dim, const long long* q_strides, const long long* k_strides,
                            const long long* v_strides, const long long* o_strides,
                            const CozyHeadMap* head_map, const CozyScatter* scatter, int causal,
                            float scale, int* status, uintptr_t stream) {
   if (!q_strides || !k_strides || !v_strides || (!o_strides && !scatter))
     return cudaErrorInvalidValue;
-  return cozy::attention_forward_fp8(q, k, v, q_scale, k_scale, v_scale, scale_seq, out, batch,
+  return cozy::attention_forward_fp8(q, k, v, q_scale, k_scale, v_scale, scale_seq, cuts, n_cuts,
+                                     out, batch,
                                      seq_q, seq_k, heads_q, heads_kv, head_dim, q_strides,
                                      k_strides, v_strides, o_strides, head_map, scatter, causal,
                                      scale, status, as_stream(stream));

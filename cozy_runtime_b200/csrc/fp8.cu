@@ -5,11 +5,12 @@
 // same with one all-reduce, src/cozy_runtime/internal/parallel/ulysses.py:588-604); Q and K
 // quantised with one fp32 scale per 64-token × head block, scale = max(absmax / 448, 1e-12)
 // (the reference's per-head law, src/cozy_runtime/internal/attention_fp8.py:162-169, at block
-// granularity; blocks start at each rank's first row); V quantised with one fp32 scale per
+// granularity; a block is 64 rows of the whole sequence starting at a multiple of 64, clipped to
+// this rank's rows); V quantised with one fp32 scale per
 // (batch, head, channel) over the whole sequence. Codes are round-to-nearest-even, saturating.
 //
 // fp8_stats_kernel: this rank's partial K sums and V channel absmax (the host all-reduces them).
-// fp8_pack_kernel:  one CTA per (64-row block, head, batch) of one tensor: rows loaded once,
+// fp8_pack_kernel:  one CTA per (block, head, batch) of one tensor: rows loaded once,
 //                   mean subtracted, block absmax reduced in the CTA, codes written to every
 //                   peer that owns the head, one scale per row to its per-token scale array.
 #include <cuda_bf16.h>
@@ -62,7 +63,11 @@ __global__ void __launch_bounds__(256) fp8_pack_kernel(const CozyFp8Pack a) {
   const int chunk = threadIdx.x & 15;
   const int row_in = threadIdx.x >> 4;
   const int d0 = chunk * 8;
-  const int block0 = blockIdx.x * 64;
+  // global block of this CTA, clipped to this rank's rows [row0, row0 + rows)
+  const int gblock = a.row0 / 64 + static_cast<int>(blockIdx.x);
+  const int lo_row = max(gblock * 64, a.row0) - a.row0;
+  const int hi_row = min(gblock * 64 + 64, a.row0 + a.rows) - a.row0;
+  const int block0 = gblock * 64 - a.row0;  // may be negative: rows below lo_row are skipped
   const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(t.src) + b * t.src_strides[2] +
                              head * t.src_strides[1] + d0;
   float mean[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -76,7 +81,7 @@ __global__ void __launch_bounds__(256) fp8_pack_kernel(const CozyFp8Pack a) {
 #pragma unroll
   for (int pass = 0; pass < 4; ++pass) {
     const int r = block0 + pass * 16 + row_in;
-    if (r < a.rows) {
+    if (r >= lo_row && r < hi_row) {
       const uint4 v = *reinterpret_cast<const uint4*>(src + r * t.src_strides[0]);
       const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
 #pragma unroll
@@ -151,7 +156,7 @@ __global__ void __launch_bounds__(256) fp8_pack_kernel(const CozyFp8Pack a) {
 #pragma unroll
     for (int pass = 0; pass < 4; ++pass) {
       const int r = block0 + pass * 16 + row_in;
-      if (r >= a.rows) continue;
+      if (r < lo_row || r >= hi_row) continue;
       const uint2 codes = make_uint2(
           e4m3x4(x[pass][0] * inv[0], x[pass][1] * inv[1], x[pass][2] * inv[2], x[pass][3] * inv[3]),
           e4m3x4(x[pass][4] * inv[4], x[pass][5] * inv[5], x[pass][6] * inv[6], x[pass][7] * inv[7]));
@@ -188,7 +193,9 @@ int fp8_pack(const CozyFp8Pack* a, cudaStream_t stream) {
     heads = t.heads > heads ? t.heads : heads;
   }
   if (a->rows == 0) return cudaSuccess;
-  dim3 grid((a->rows + 63) / 64, heads, a->batch * 3);
+  if (a->row0 < 0) return cudaErrorInvalidValue;
+  const int blocks = (a->row0 + a->rows + 63) / 64 - a->row0 / 64;
+  dim3 grid(blocks, heads, a->batch * 3);
   fp8_pack_kernel<<<grid, 256, 0, stream>>>(*a);
   return cudaGetLastError();
 }

@@ -3,7 +3,8 @@
 Per rank and call: partial statistics of its rows (K sums, V channel absmax; `cozy_fp8_stats`),
 made global by the caller (one all-reduce each: SUM, MAX — the reference's `_Shift` does the
 K mean the same way, `src/cozy_runtime/internal/parallel/ulysses.py:588-604`); the first stage
-(`cozy_fp8_pack`) writes e4m3 codes of Q and K (one scale per 64-token × head block, K less the
+(`cozy_fp8_pack`) writes e4m3 codes of Q and K (one scale per 64-token × head block — 64 tokens
+of the whole sequence from a multiple of 64, cut at rank boundaries — K less the
 global mean, both rotated by the orthonormal Hadamard of order 128 first, as the reference's
 FA4-fp8 row does, `src/cozy_runtime/internal/attention_upstream.py:276-317`) and V (one scale per
 channel) into every peer's receive buffers with Q/K's
@@ -81,6 +82,7 @@ class Fp8Step:
         lay = self.layout
         pk = _lib.Fp8Pack()
         pk.world, pk.rows, pk.batch, pk.head_dim = lay.world, self.mine, self.batch, self.dim
+        pk.row0 = lay.start(self.rank)
         specs = [
             (self.query, lay.q_lo, lay.q_n, q_dst, qs_dst, None, None),
             (self.key, lay.kv_lo, lay.kv_n, k_dst, ks_dst, k_sum, None),
@@ -138,9 +140,11 @@ class Fp8Step:
 
         head_map = _lib.HeadMap(lay.group, lay.q_lo[rank], lay.kv_lo[rank])
         sc = 1.0 / math.sqrt(dim) if scale is None else float(scale)
+        cuts = [lay.start(r) for r in range(1, lay.world) if 0 < lay.start(r) < total]
+        cut_arr = (ctypes.c_int * max(1, len(cuts)))(*cuts)
         code = _lib.load().cozy_attention_fwd_fp8(
             qv.data_ptr(), kv.data_ptr(), vv.data_ptr(), qs.data_ptr(), ks.data_ptr(),
-            v_scale_local.data_ptr(), self.sseq,
+            v_scale_local.data_ptr(), self.sseq, cut_arr, len(cuts),
             None if into is None else into.data_ptr(),
             batch, total, total, qn, kvn, dim,
             strides(qv), strides(kv), strides(vv), None if into is None else strides(into),

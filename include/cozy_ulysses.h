@@ -122,6 +122,8 @@ COZY_API int cozy_ulysses_land(const void* returned, int world, int rows, int ba
  * src/cozy_runtime/internal/parallel/ulysses.py:588-604), Q and K as e4m3 with one fp32 scale
  * per 64-token × head block (max(absmax/448, 1e-12); blocks start at each rank's first row), V as
  * e4m3 with one fp32 scale per (batch, head, channel) over the whole sequence, P as e4m3,
+ * (a block is 64 tokens of the whole sequence starting at a multiple of 64, cut where one rank's
+ * rows end and the next rank's begin),
  * softmax and accumulation in fp32. The per-head law is src/cozy_runtime/internal/
  * attention_fp8.py:162-169 (`quantise_eager`); the reference's B200 FP8 kernel is FA4-fp8
  * (attention_upstream.py:293-317). head_dim 128. */
@@ -164,6 +166,8 @@ typedef struct CozyFp8Tensor {
 typedef struct CozyFp8Pack {
   CozyFp8Tensor t[3]; /* Q, K, V */
   int world, rows, batch, head_dim;
+  int row0; /* this rank's first row in the whole sequence: blocks are [64i, 64i + 64) of the
+               whole sequence, clipped to this rank's rows */
 } CozyFp8Pack;
 
 COZY_API int cozy_fp8_stats(const CozyFp8Stats* stats, uintptr_t stream);
@@ -171,10 +175,14 @@ COZY_API int cozy_fp8_pack(const CozyFp8Pack* pack, uintptr_t stream);
 
 /* cozy_attention_fwd on e4m3 operands: q/k/v codes with element (= byte) strides, each a
  * multiple of 16; q_scale/k_scale per token [batch][heads][scale_seq] (scale_seq ≥ seq_k
- * rounded up to 128, padding zero), v_scale [batch][heads_kv][128]. Output bf16. */
+ * rounded up to 128, padding zero), v_scale [batch][heads_kv][128]. Output bf16.
+ * K scales are constant over every 64-key block of the whole sequence except where one of the
+ * `n_cuts` rows in `cuts` (the ranks' first rows, each > 0) falls inside it; the kernel takes
+ * one scale per 64-key block elsewhere. */
 COZY_API int cozy_attention_fwd_fp8(
     const void* q, const void* k, const void* v, const float* q_scale, const float* k_scale,
-    const float* v_scale, long long scale_seq, void* out, int batch, int seq_q, int seq_k,
+    const float* v_scale, long long scale_seq, const int* cuts, int n_cuts, void* out,
+    int batch, int seq_q, int seq_k,
     int heads_q, int heads_kv, int head_dim, const long long* q_strides,
     const long long* k_strides, const long long* v_strides, const long long* o_strides,
     const CozyHeadMap* head_map, const CozyScatter* scatter, int causal, float scale,

@@ -185,8 +185,8 @@ def fp8_attention_law(
     [B, S, H, D] output: K less its per-(batch, head) mean over the whole sequence (the shift of
     src/cozy_runtime/internal/parallel/ulysses.py:588-604); Q and K rotated by the orthonormal
     Hadamard (the reference's FA4-fp8 row, attention_upstream.py:293-317); Q and K as e4m3 with one scale per
-    `block` rows × head, blocks starting at each rank's first row (`quantise_fp8_blocks` per
-    rank); V as e4m3 with one scale per (batch, head, channel) over the whole sequence
+    `block` rows × head, blocks of the whole sequence from multiples of `block`, cut at rank
+    boundaries (`quantise_fp8_blocks` per block); V as e4m3 with one scale per (batch, head, channel) over the whole sequence
     (max(absmax/448, 1e-12)); P = exp(s - rowmax) · `p_scale` as e4m3; the row sum over the
     unquantised P; O = (P codes · V codes) · V scale / row sum. Grouped K/V heads as
     `attention_fp32`."""
@@ -202,11 +202,13 @@ def fp8_attention_law(
         starts.append(starts[-1] + int(part.shape[1]))
 
     def blocks(x: Tensor) -> Tensor:
+        # blocks of `block` rows of the whole sequence from multiples of `block`, cut where one
+        # rank's rows end and the next's begin
         out = torch.empty_like(x)
-        for a, b in zip(starts[:-1], starts[1:], strict=True):
-            codes, descale = quantise_fp8_blocks(x[:, a:b], block)
-            scale = descale.repeat_interleave(block, dim=1)[:, : b - a]
-            out[:, a:b] = codes.float() * scale[..., None]
+        edges = sorted({*range(0, starts[-1], block), *starts})
+        for a, b in zip(edges[:-1], edges[1:], strict=True):
+            codes, descale = quantise_fp8_blocks(x[:, a:b], b - a)
+            out[:, a:b] = codes.float() * descale[:, 0][:, None, :, None]
         return out
 
     qd, kd = blocks(q), blocks(k)
