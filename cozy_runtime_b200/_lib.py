@@ -169,6 +169,11 @@ SIGNATURES = {
          POINTER(Rope), c_int, c_float, c_int, c_float, c_void_p, c_uint64],
         c_int,
     ),
+    "cozy_head_norm_rope": (
+        [c_void_p, c_void_p, c_int, c_int, c_int, c_int, POINTER(c_longlong),
+         POINTER(c_longlong), POINTER(Rope), c_int, c_void_p, c_float, c_float, c_uint64],
+        c_int,
+    ),
     "cozy_fp8_stats": ([POINTER(Fp8Stats), c_uint64], c_int),
     "cozy_fp8_pack": ([POINTER(Fp8Pack), c_uint64], c_int),
     "cozy_attention_fwd_fp8": (

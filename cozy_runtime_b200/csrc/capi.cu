@@ -15,6 +15,10 @@ int attention_forward(const void* q, const void* k, const void* v, void* out, in
                       float scale, int* status, cudaStream_t stream);
 int ulysses_pack(const CozyPackTensor* tensors, int count, int world, int rows, int batch,
                  int head_dim, const CozyRope* rope, cudaStream_t stream);
+int head_norm_rope(const void* x, void* out, int batch, int seq, int heads, int head_dim,
+                   const long long* x_strides, const long long* out_strides,
+                   const CozyRope* rope, int normalize, const float* weight, float offset,
+                   float eps, cudaStream_t stream);
 int ulysses_land(const void* returned, int world, int rows, int batch, int head_dim,
                  const int* head_lo, const int* head_n, void* out, const long long* out_strides,
                  cudaStream_t stream);
@@ -50,6 +54,15 @@ int cozy_ulysses_land(const void* returned, int world, int rows, int batch, int 
   if (!head_lo || !head_n || !out_strides) return cudaErrorInvalidValue;
   return cozy::ulysses_land(returned, world, rows, batch, head_dim, head_lo, head_n, out,
                             out_strides, as_stream(stream));
+}
+
+int cozy_head_norm_rope(const void* x, void* out, int batch, int seq, int heads, int head_dim,
+                        const long long* x_strides, const long long* out_strides,
+                        const CozyRope* rope, int normalize, const float* weight, float offset,
+                        float eps, uintptr_t stream) {
+  if (!x_strides || !out_strides) return cudaErrorInvalidValue;
+  return cozy::head_norm_rope(x, out, batch, seq, heads, head_dim, x_strides, out_strides, rope,
+                              normalize, weight, offset, eps, as_stream(stream));
 }
 
 const char* cozy_error_name(int code) {

@@ -38,36 +38,14 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
   return v;
 }
 
-// grid: x covers rows × batch × head_n[p] destination rows (CHUNKS threads each), y = peer,
-// z = tensor. One thread = 8 channels of one destination row.
+// Per-head RMSNorm (when `t.normalize`) then RoPE (when `t.rotate`) of one row's 8 channels
+// [d0, d0 + 8) held by this thread; the row's CHUNKS threads are consecutive lanes of one warp
+// (`group_mask`). `token` is the row's RoPE table row. fp32 arithmetic, rounded once by the caller.
 template <int HD>
-__global__ void __launch_bounds__(256) pack_kernel(const PackArgs a) {
+__device__ __forceinline__ void norm_rope_row(float (&x)[8], int d0, int chunk,
+                                              unsigned group_mask, long long token,
+                                              const CozyPackTensor& t, const CozyRope& r) {
   constexpr int CHUNKS = HD / 8;
-  constexpr int ROWS_PER_BLOCK = 256 / CHUNKS;
-  const CozyPackTensor& t = a.t[blockIdx.z];
-  const int peer = blockIdx.y;
-  const int n = t.head_n[peer];
-  const int chunk = threadIdx.x % CHUNKS;
-  const long long row = static_cast<long long>(blockIdx.x) * ROWS_PER_BLOCK + threadIdx.x / CHUNKS;
-  const long long total = static_cast<long long>(a.rows) * a.batch * n;
-  // Whole row groups leave together: every lane of a row's group shares `row`.
-  if (n == 0 || row >= total) return;
-  // destination order [rows][batch][n]
-  const int hh = static_cast<int>(row % n);
-  const long long sb = row / n;
-  const int b = static_cast<int>(sb % a.batch);
-  const int s = static_cast<int>(sb / a.batch);
-  const int head = t.head_lo[peer] + hh;
-  const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(t.src) + s * t.src_strides[0] +
-                             head * t.src_strides[1] + b * t.src_strides[2];
-  const int d0 = chunk * 8;
-  float x[8];
-  unpack8(*reinterpret_cast<const uint4*>(src + d0), x);
-
-  // A row's CHUNKS threads are consecutive lanes of one warp (CHUNKS divides 32).
-  const unsigned group_mask =
-      (CHUNKS == 32) ? 0xffffffffu
-                     : (((1u << CHUNKS) - 1u) << ((threadIdx.x & 31) / CHUNKS * CHUNKS));
   if (t.normalize) {
     float ss = 0.f;
 #pragma unroll
@@ -81,9 +59,7 @@ __global__ void __launch_bounds__(256) pack_kernel(const PackArgs a) {
       x[i] = t.norm_weight ? x[i] * inv * w : x[i] * inv;
     }
   }
-  const CozyRope& r = a.rope;
   if (t.rotate && r.rotary > 0) {
-    const long long token = r.token0 + s;
     const float* cs = r.cos + token * r.stride_token;
     const float* sn = r.sin + token * r.stride_token;
     if (r.interleaved) {
@@ -120,8 +96,118 @@ __global__ void __launch_bounds__(256) pack_kernel(const PackArgs a) {
       }
     }
   }
-  __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(t.dst[peer]) + row * HD + d0;
+}
+
+template <int CHUNKS>
+__device__ __forceinline__ unsigned row_group_mask() {
+  return (CHUNKS == 32) ? 0xffffffffu
+                        : (((1u << CHUNKS) - 1u) << ((threadIdx.x & 31) / CHUNKS * CHUNKS));
+}
+
+// grid: x covers rows × batch × head_n[p] destination rows (CHUNKS threads each), y = peer,
+// z = tensor. One thread = 8 channels of one destination row.
+template <int HD>
+__global__ void __launch_bounds__(256) pack_kernel(const PackArgs a) {
+  constexpr int CHUNKS = HD / 8;
+  constexpr int ROWS_PER_BLOCK = 256 / CHUNKS;
+  const CozyPackTensor& t = a.t[blockIdx.z];
+  const int peer = blockIdx.y;
+  const unsigned n = static_cast<unsigned>(t.head_n[peer]);
+  const int chunk = threadIdx.x % CHUNKS;
+  // destination rows number below 2^31 (checked on the host): 32-bit index arithmetic
+  const unsigned row = blockIdx.x * ROWS_PER_BLOCK + threadIdx.x / CHUNKS;
+  const unsigned total = static_cast<unsigned>(a.rows) * a.batch * n;
+  // Whole row groups leave together: every lane of a row's group shares `row`.
+  if (n == 0 || row >= total) return;
+  // destination order [rows][batch][n]
+  const unsigned hh = row % n;
+  const unsigned sb = row / n;
+  const unsigned b = sb % static_cast<unsigned>(a.batch);
+  const unsigned s = sb / static_cast<unsigned>(a.batch);
+  const int head = t.head_lo[peer] + static_cast<int>(hh);
+  const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(t.src) + s * t.src_strides[0] +
+                             head * t.src_strides[1] + b * t.src_strides[2];
+  const int d0 = chunk * 8;
+  float x[8];
+  unpack8(*reinterpret_cast<const uint4*>(src + d0), x);
+  norm_rope_row<HD>(x, d0, chunk, row_group_mask<CHUNKS>(), a.rope.token0 + s, t, a.rope);
+  __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(t.dst[peer]) + static_cast<long long>(row) * HD + d0;
   *reinterpret_cast<uint4*>(dst) = pack8(x);
+}
+
+// The standalone form: [batch, seq, heads, HD] in, the same shape out, any strides.
+struct NormRopeArgs {
+  CozyPackTensor t;  // src, src_strides, heads, norm fields, rotate; dst[0] = out
+  long long out_strides[3];
+  CozyRope rope;
+  int seq, batch;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(256) head_norm_rope_kernel(const NormRopeArgs a) {
+  constexpr int CHUNKS = HD / 8;
+  constexpr int ROWS_PER_BLOCK = 256 / CHUNKS;
+  const int chunk = threadIdx.x % CHUNKS;
+  const unsigned row = blockIdx.x * ROWS_PER_BLOCK + threadIdx.x / CHUNKS;  // [b][s][h] order
+  const unsigned heads = static_cast<unsigned>(a.t.heads);
+  if (row >= static_cast<unsigned>(a.batch) * a.seq * heads) return;
+  const unsigned h = row % heads;
+  const unsigned bs = row / heads;
+  const unsigned s = bs % static_cast<unsigned>(a.seq);
+  const unsigned b = bs / static_cast<unsigned>(a.seq);
+  const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(a.t.src) + s * a.t.src_strides[0] +
+                             h * a.t.src_strides[1] + b * a.t.src_strides[2];
+  const int d0 = chunk * 8;
+  float x[8];
+  unpack8(*reinterpret_cast<const uint4*>(src + d0), x);
+  norm_rope_row<HD>(x, d0, chunk, row_group_mask<CHUNKS>(), a.rope.token0 + s, a.t, a.rope);
+  __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(a.t.dst[0]) + s * a.out_strides[0] +
+                       h * a.out_strides[1] + b * a.out_strides[2] + d0;
+  *reinterpret_cast<uint4*>(dst) = pack8(x);
+}
+
+int head_norm_rope(const void* x, void* out, int batch, int seq, int heads, int head_dim,
+                   const long long* x_strides, const long long* out_strides,
+                   const CozyRope* rope, int normalize, const float* weight, float offset,
+                   float eps, cudaStream_t stream) {
+  if (head_dim != 64 && head_dim != 128) return cudaErrorNotSupported;
+  if (x == nullptr || out == nullptr || batch < 1 || seq < 0 || heads < 1)
+    return cudaErrorInvalidValue;
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
+    return cudaErrorInvalidValue;
+  for (int k = 0; k < 3; ++k)
+    if (x_strides[k] % 8 || out_strides[k] % 8) return cudaErrorInvalidValue;
+  if (rope != nullptr) {
+    if (rope->cos == nullptr || rope->sin == nullptr) return cudaErrorInvalidValue;
+    if (rope->rotary < 0 || rope->rotary > head_dim || rope->rotary % 2) return cudaErrorInvalidValue;
+    if (!rope->interleaved && rope->rotary % 16) return cudaErrorNotSupported;
+  }
+  const long long rows = static_cast<long long>(batch) * seq * heads;
+  if (rows == 0) return cudaSuccess;
+  if (rows >= (1LL << 31)) return cudaErrorInvalidValue;
+  NormRopeArgs a = {};
+  a.t.src = x;
+  for (int k = 0; k < 3; ++k) {
+    a.t.src_strides[k] = x_strides[k];
+    a.out_strides[k] = out_strides[k];
+  }
+  a.t.heads = heads;
+  a.t.normalize = normalize ? 1 : 0;
+  a.t.norm_weight = weight;
+  a.t.norm_offset = offset;
+  a.t.norm_eps = eps;
+  a.t.rotate = rope != nullptr;
+  a.t.dst[0] = out;
+  if (rope != nullptr) a.rope = *rope;
+  a.seq = seq;
+  a.batch = batch;
+  const int rows_per_block = 256 / (head_dim / 8);
+  const unsigned blocks = static_cast<unsigned>((rows + rows_per_block - 1) / rows_per_block);
+  if (head_dim == 128)
+    head_norm_rope_kernel<128><<<blocks, 256, 0, stream>>>(a);
+  else
+    head_norm_rope_kernel<64><<<blocks, 256, 0, stream>>>(a);
+  return cudaGetLastError();
 }
 
 int ulysses_pack(const CozyPackTensor* tensors, int count, int world, int rows, int batch,
@@ -159,9 +245,9 @@ int ulysses_pack(const CozyPackTensor* tensors, int count, int world, int rows, 
   a.batch = batch;
   const long long dest_rows = static_cast<long long>(rows) * batch * max_n;
   if (dest_rows == 0) return cudaSuccess;
+  if (dest_rows >= (1LL << 31)) return cudaErrorInvalidValue;  // the kernel indexes in 32 bits
   const int rows_per_block = 256 / (head_dim / 8);
   const long long blocks = (dest_rows + rows_per_block - 1) / rows_per_block;
-  if (blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
   dim3 grid(static_cast<unsigned>(blocks), world, count);
   if (head_dim == 128)
     pack_kernel<128><<<grid, 256, 0, stream>>>(a);

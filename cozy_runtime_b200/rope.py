@@ -81,3 +81,50 @@ def llama(seq: int, dim: int, theta: float = 500000.0) -> RopeSpec:
         torch.cos(angles).float().contiguous(), torch.sin(angles).float().contiguous(),
         dim, 1, dim, False,
     )
+
+
+def head_norm_rope(
+    x: Tensor,
+    tables: RopeSpec | None,
+    *,
+    weight: Tensor | None = None,
+    offset: float = 0.0,
+    eps: float = 1e-6,
+    normalize: bool = True,
+    out: Tensor | None = None,
+) -> Tensor:
+    """Per-head RMSNorm then RoPE of [batch, seq, heads, head_dim] bf16 `x` (one launch of
+    `cozy_head_norm_rope`): the drop-in for src/cozy_runtime/accel/fusion/_kernels.py:459
+    (`head_norm_rope(launch, entry, x, weight, eps, tables, dtype)`, law :177-240) with the
+    tables as `rope_tables` lays them out (`RopeSpec`; row = token of `x`'s sequence).
+    `weight`: fp32 [head_dim] or None (unit); `normalize=False` rotates only."""
+    import ctypes
+
+    import torch
+
+    from cozy_runtime_b200 import _lib
+
+    if x.dtype != torch.bfloat16 or not x.is_cuda:
+        raise ValueError("head_norm_rope serves bf16 CUDA tensors")
+    batch, seq, heads, dim = x.shape
+    out = torch.empty_like(x) if out is None else out
+    rope_arg = None
+    if tables is not None:
+        rope_arg = _lib.Rope()
+        rope_arg.cos, rope_arg.sin = tables.cos.data_ptr(), tables.sin.data_ptr()
+        rope_arg.stride_token, rope_arg.stride_channel = tables.stride_token, tables.stride_channel
+        rope_arg.token0, rope_arg.rotary = 0, tables.rotary
+        rope_arg.interleaved = int(tables.interleaved)
+    w = None
+    if weight is not None:
+        w = weight.to(device=x.device, dtype=torch.float32).contiguous()
+    code = _lib.load().cozy_head_norm_rope(
+        x.data_ptr(), out.data_ptr(), batch, seq, heads, dim,
+        _lib.strides3((x.stride(1), x.stride(2), x.stride(0))),
+        _lib.strides3((out.stride(1), out.stride(2), out.stride(0))),
+        None if rope_arg is None else ctypes.byref(rope_arg), int(normalize),
+        None if w is None else w.data_ptr(), float(offset), float(eps),
+        torch.cuda.current_stream(x.device).cuda_stream,
+    )
+    _lib.check("cozy_head_norm_rope", code)
+    return out

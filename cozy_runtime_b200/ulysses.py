@@ -502,7 +502,8 @@ def exchange(
     if fp8:
         if compute is not None or rope is not None or norm_q is not None or norm_k is not None:
             raise NotImplementedError("the FP8 path serves native attention without RoPE/RMSNorm")
-        if world > 1 and _transport(handle, transport) != "peer":
+        if world > 1 and (_transport(handle, transport) != "peer"
+                          or not _peer_ready(handle, query.device)):
             raise NotImplementedError("the FP8 path crosses over the peer transport only")
         return _exchange_fp8(query, key, value, handle, layout, rank, began, causal, scale)
     if world == 1 and rope is None and norm_q is None and norm_k is None and compute is None:
@@ -512,7 +513,8 @@ def exchange(
         _CLOCK.add((began, first, _Clock.mark(query), _Clock.mark(query)), 0)
         return out
 
-    if world > 1 and compute is None and _transport(handle, transport) == "peer":
+    if (world > 1 and compute is None and _transport(handle, transport) == "peer"
+            and _peer_ready(handle, query.device)):
         return _exchange_peer(
             query, key, value, handle, layout, rank, began, causal, scale, rope, norm_q, norm_k
         )
@@ -546,6 +548,46 @@ def exchange(
         raise
     _CLOCK.add((began, first, last, _Clock.mark(query)), step.moved())
     return out
+
+
+_FORMED: weakref.WeakKeyDictionary = weakref.WeakKeyDictionary()
+
+
+def _peer_ready(handle, device: torch.device) -> bool:
+    """Whether the group's NVLink transport passed its formation check (run once per group, on
+    every rank together): one small exchange over the peer transport and over NCCL must give the
+    same bytes on every rank, as the reference checks its copy-engine exchange against NCCL
+    before using it (src/cozy_runtime/internal/parallel/copy_engine.py:408-449). A failed check
+    leaves the group on NCCL."""
+    state = _FORMED.get(handle)
+    if state is None:
+        _FORMED[handle] = "checking"  # the check's own exchanges take the peer path
+        state = _FORMED[handle] = _form_check(handle, device)
+    return state is not False
+
+
+def _form_check(handle, device: torch.device) -> bool:
+    world, rank = dist.get_world_size(handle), dist.get_rank(handle)
+    gen = torch.Generator(device=device).manual_seed(977 + rank)
+    rows = tensor_split_rows(64 * world + 3, world)
+    heads = 2 * world
+    q, k, v = (
+        torch.randn(1, rows[rank], heads, 128, generator=gen, device=device).to(torch.bfloat16)
+        for _ in range(3)
+    )
+    ok = True
+    try:
+        over_peer = exchange(q, k, v, handle, None, rows=rows, transport="peer")
+        over_nccl = exchange(q, k, v, handle, None, rows=rows, transport="nccl")
+        torch.cuda.synchronize(device)
+        ok = bool(torch.equal(over_peer, over_nccl)) and not int(
+            attention.status_word(device).item()
+        )
+    except RuntimeError:
+        ok = False
+    agreed = torch.tensor([1 if ok else 0], dtype=torch.int32, device=device)
+    dist.all_reduce(agreed, op=dist.ReduceOp.MIN, group=handle)
+    return bool(agreed.item())
 
 
 def _transport(handle, asked: str | None) -> str:

@@ -108,6 +108,18 @@ typedef struct CozyRope {
 COZY_API int cozy_ulysses_pack(const CozyPackTensor* tensors, int count, int world, int rows, int batch,
                       int head_dim, const CozyRope* rope, uintptr_t stream);
 
+/* Per-head RMSNorm (when `normalize`; weight NULL = unit, else weight + offset) then RoPE
+ * (when `rope` is non-NULL) of x [batch, seq, heads, head_dim] into out of the same shape, any
+ * strides ({seq, head, batch}, elements); fp32 arithmetic rounded once. The standalone form of
+ * the first stage's law: a drop-in for src/cozy_runtime/accel/fusion/_kernels.py:459
+ * (`head_norm_rope`, the Triton kernel at :177-240) and kernels/csrc/norm.cpp:41-107
+ * (`rms_rope_split_half`). */
+COZY_API int cozy_head_norm_rope(const void* x, void* out, int batch, int seq, int heads,
+                                 int head_dim, const long long* x_strides,
+                                 const long long* out_strides, const CozyRope* rope,
+                                 int normalize, const float* weight, float offset, float eps,
+                                 uintptr_t stream);
+
 /* The last stage of the exchange: the attended rows returned by every rank, stacked by source
  * rank in `returned` ([world][rows][batch][head_n[p]][head_dim]), landed in this rank's output
  * `out` [batch, rows, heads, head_dim] (element strides {seq, head, batch}) at heads
