@@ -147,6 +147,10 @@ SIGNATURES = {
          POINTER(HeadMap), POINTER(Scatter), c_int, c_float, c_void_p, c_uint64],
         c_int,
     ),
+    "cozy_attention_split_plan": (
+        [c_int, c_int, c_int, c_int, c_int, c_int, POINTER(c_longlong), POINTER(c_int)],
+        c_int,
+    ),
     "cozy_ulysses_pack": (
         [POINTER(PackTensor), c_int, c_int, c_int, c_int, c_int, POINTER(Rope), c_uint64],
         c_int,

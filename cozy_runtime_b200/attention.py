@@ -121,3 +121,22 @@ def forward(
 def implementation(query: Tensor, key: Tensor, value: Tensor, options: dict) -> str:
     """The reference's `Local.impl`: the concrete implementation serving these operands."""
     return "cozy-b200-tcgen05"
+
+
+def split_plan(
+    batch: int, seq_q: int, seq_k: int, heads_q: int, head_dim: int, causal: bool
+) -> tuple[int, int]:
+    """(whole tiles, parts): how a call of this shape is scheduled on the current CUDA device
+    (`cozy_attention_split_plan`). Past the first `whole` 256-row tiles, each tile runs as
+    `parts` CTAs over shares of the keys, merged by the last to finish; parts 1 = no split."""
+    import ctypes
+
+    from cozy_runtime_b200 import _lib
+
+    whole, parts = ctypes.c_longlong(0), ctypes.c_int(0)
+    code = _lib.load().cozy_attention_split_plan(
+        batch, seq_q, seq_k, heads_q, head_dim, int(causal), ctypes.byref(whole),
+        ctypes.byref(parts),
+    )
+    _lib.check("cozy_attention_split_plan", code)
+    return whole.value, parts.value

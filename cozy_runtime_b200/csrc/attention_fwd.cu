@@ -28,6 +28,12 @@
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
+#include <stdlib.h>
+
+#include <algorithm>
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include "../../include/cozy_ulysses.h"
 #include "sm100.cuh"
@@ -72,6 +78,14 @@ struct AttentionParams {
   // K scales can change inside a 64-key half of a tile
   int n_cuts;
   int cuts[COZY_MAX_PEERS];
+  // Split key ranges (the last partial wave of tiles): tiles [0, n_full) run whole, one CTA
+  // each; every later tile runs as `parts` CTAs over consecutive key-block ranges. A part leaves
+  // its unnormalised O rows and (max, sum) in `ws_o`/`ws_ml`; the part that arrives last at the
+  // tile's counter (an atomic, no waiting) merges them and writes the output.
+  int n_full, parts;
+  float* ws_o;     // [split tile][part][query tile][HD / 4][128 rows] float4
+  float2* ws_ml;   // [split tile][part][query tile][128 rows]
+  int* counters;   // [split tile][query tile], zero at launch
 };
 
 template <int HD, bool FP8>
@@ -110,6 +124,54 @@ __device__ __forceinline__ bool elect_one() {
       "{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\tselp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(pred));
   return pred != 0;
+}
+
+// Named barrier `kId` over `kCount` threads (a multiple of 32) that also returns whether
+// `pred` held in every one of them.
+template <int kId, int kCount>
+__device__ __forceinline__ bool named_bar_and(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred)), "n"(kId), "n"(kCount)
+      : "memory");
+  return r != 0;
+}
+
+template <int kId, int kCount>
+__device__ __forceinline__ void named_bar_sync() {
+  asm volatile("bar.sync %0, %1;" ::"n"(kId), "n"(kCount) : "memory");
+}
+
+// This CTA's tile, and for a split tile its part and its index among the split tiles (part -1
+// for a whole tile). Cheap enough to recompute where it is needed, rather than hold in registers.
+__device__ __forceinline__ int unit_tile(const AttentionParams& p, int u, int* part,
+                                         int* split_tile) {
+  if (u < p.n_full) {
+    *part = -1;
+    *split_tile = 0;
+    return u;
+  }
+  const int v = u - p.n_full;
+  *split_tile = v / p.parts;
+  *part = v - *split_tile * p.parts;
+  return p.n_full + *split_tile;
+}
+
+// Thread and block index read anew (volatile: never merged with an earlier read), so values
+// derived from them after a long loop are recomputed there instead of held through it.
+__device__ __forceinline__ int fresh_tid() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%tid.x;" : "=r"(r));
+  return static_cast<int>(r);
+}
+
+__device__ __forceinline__ int fresh_ctaid() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%ctaid.x;" : "=r"(r));
+  return static_cast<int>(r);
 }
 
 // mbar_wait by every lane of a warp, with one answer for the whole warp.
@@ -251,7 +313,7 @@ __device__ __forceinline__ void exp_chunk_fp8(const uint32_t (&r)[32], float2 sc
   }
 }
 
-template <int HD, bool FP8>
+template <int HD, bool FP8, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                          const __grid_constant__ CUtensorMap tm_k,
@@ -276,15 +338,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // Heaviest causal blocks first: block x takes query block (q_blocks - 1 - x).
-  const int qb = p.q_blocks - 1 - static_cast<int>(blockIdx.x);
-  const int head = blockIdx.y;
-  const int b = blockIdx.z;
+  // Work unit -> tile (query block x, head, batch), x fastest. Heaviest causal blocks first:
+  // block x takes query block (q_blocks - 1 - x).
+  int part = -1, split_tile = 0;
+  const int tile = SPLIT ? unit_tile(p, static_cast<int>(blockIdx.x), &part, &split_tile)
+                         : static_cast<int>(blockIdx.x);
+  const int qb = p.q_blocks - 1 - tile % p.q_blocks;
+  const int head = (tile / p.q_blocks) % p.heads_q;
+  const int b = tile / (p.q_blocks * p.heads_q);
   const int kv_head = (head + p.q_base) / p.group - p.kv_base;
   const int q0 = qb * (kQTiles * kBlockM);
   int kv_end = p.seq_k;
   if (p.causal) kv_end = min(p.seq_k, max(0, q0 + kQTiles * kBlockM + p.causal_offset));
-  const int n_kv = (kv_end + kBlockN - 1) / kBlockN;
+  const int n_blocks = (kv_end + kBlockN - 1) / kBlockN;
+  // this unit's key blocks: [kv_first, kv_first + n_kv), kv_first even (the softmax loop runs
+  // over absolute block numbers and takes its barrier parity from them)
+  int kv_first = 0, n_kv = n_blocks;
+  if (SPLIT && part >= 0) {
+    const int pairs = n_blocks / 2;
+    kv_first = 2 * (part * pairs / p.parts);
+    n_kv = (part + 1 == p.parts ? n_blocks : 2 * ((part + 1) * pairs / p.parts)) - kv_first;
+  }
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -336,7 +410,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m = -INFINITY;  // running max, log2 domain, of the probabilities' reference point
     float l = 0.f;        // running row sum against m
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
+    // j: absolute key block; kv_first is even, so j & 1 is also the parity of the local count
+    const int kv_stop = kv_first + n_kv;
+    for (int j = kv_first; j < kv_stop; ++j) {
       if (!mbar_wait(&s_full[s], j & 1, abort, p.status)) {
         ok = false;
         break;
@@ -390,9 +466,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float mt = fmaxf(mlo == -INFINITY ? -INFINITY : mlo * sc_lo,
                              mhi == -INFINITY ? -INFINITY : mhi * sc_hi);
       const float m_new = fmaxf(m, mt);
-      if (j == 0) {
+      // Split kernel: a row whose max is still -inf has seen only masked keys or none yet (its
+      // part's first block), its O is zero or not yet written (the first PV overwrites it), so
+      // it takes the new max without a rescale. Whole-tile kernel: the first block sets the max.
+      if (!SPLIT && j == 0) {
         m = m_new;
-      } else if (__any_sync(0xffffffffu, m_new > m + (FP8 ? kRescaleLog2Fp8 : kRescaleLog2))) {
+      } else if (__any_sync(0xffffffffu, (!SPLIT || m != -INFINITY) &&
+                                             m_new > m + (FP8 ? kRescaleLog2Fp8 : kRescaleLog2))) {
         // O row rescale: this warp's rows, once PV of the previous tile completed (the commit
         // behind s_full covers every earlier MMA of the issuing thread).
         const float factor = (m == -INFINITY) ? 0.f : ex2_approx(m - m_new);
@@ -409,6 +489,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         m = m_new;
       }
+      if (SPLIT && m == -INFINITY) m = m_new;
       const float mu = (m == -INFINITY) ? 0.f : m;
       const float2 scale_lo = make_float2(sc_lo, sc_lo), scale_hi = make_float2(sc_hi, sc_hi);
       float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
@@ -448,59 +529,159 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(&p_ready[2 * s + 1]);
     }
     // ------------------------------------------------------------------------- epilogue
+    // Everything the epilogue needs beyond (m, l, ok, n_kv) is derived again here, from fresh
+    // index reads, so that it holds no register through the loop above.
+    {
+    const int e_tid = fresh_tid();
+    const int e_s = e_tid >> 7;
+    const int quarter = (e_tid >> 5) & 3;
+    const int e_lane = e_tid & 31;
+    int part = -1, split_tile = 0;
+    const int e_tile =
+        SPLIT ? unit_tile(p, fresh_ctaid(), &part, &split_tile) : fresh_ctaid();
+    const int head = (e_tile / p.q_blocks) % p.heads_q;
+    const int b = e_tile / (p.q_blocks * p.heads_q);
+    const int kv_head = (head + p.q_base) / p.group - p.kv_base;
+    const int q_row = (p.q_blocks - 1 - e_tile % p.q_blocks) * (kQTiles * kBlockM) +
+                      e_s * kBlockM + quarter * 32 + e_lane;
+    const uint32_t e_tO = *reinterpret_cast<volatile uint32_t*>(tmem_slot) +
+                          (static_cast<uint32_t>(quarter * 32) << 16) + 256u +
+                          static_cast<uint32_t>(e_s * HD);
     if (ok && n_kv > 0) {
-      ok = mbar_wait(&o_final[s], 0, abort, p.status);
+      ok = mbar_wait(&o_final[e_s], 0, abort, p.status);
       tc_fence_after();
     }
-    if (ok) {
+    const bool valid = q_row < p.seq_q;
+    __nv_bfloat16* dst;
+    if (p.scatter) {
+      // the row's owner: the rank whose sequence rows contain it (rows are contiguous per rank)
+      int owner = 0;
+      while (owner + 1 < p.world && q_row >= p.row_start[owner + 1]) ++owner;
+      dst = p.outs[owner] + static_cast<long long>(b) * p.outs_strides[owner][2] +
+            static_cast<long long>(q_row - p.row_start[owner]) * p.outs_strides[owner][0] +
+            static_cast<long long>(head + p.head_offset) * p.outs_strides[owner][1];
+    } else {
+      dst = p.out + static_cast<long long>(b) * p.out_b +
+            static_cast<long long>(q_row) * p.out_s + static_cast<long long>(head) * p.out_h;
+    }
+    // 32 fp32 columns of the row's O (against its row sum's reference) -> bf16 output
+    auto emit = [&](int c, const uint32_t (&o)[32], float inv) {
+      uint32_t packed[16];
+      if constexpr (FP8) {  // V's per-channel scales
+        const float* vs = p.v_scale +
+                          (static_cast<long long>(b) * p.heads_kv + kv_head) * HD + c * 32;
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          packed[i] = pack_bf16x2(__uint_as_float(o[2 * i]) * inv * vs[2 * i],
+                                  __uint_as_float(o[2 * i + 1]) * inv * vs[2 * i + 1]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          packed[i] = pack_bf16x2(__uint_as_float(o[2 * i]) * inv,
+                                  __uint_as_float(o[2 * i + 1]) * inv);
+      }
+      if (valid) {
+        uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          d4[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2],
+                             packed[4 * i + 3]);
+      }
+    };
+    if (SPLIT && part >= 0) {
+      // ------------------------------------------------- one part of a split tile
+      // Leave this part's rows, then count in; the last part of the tile merges every part's
+      // rows (each against the largest max) and writes the output. Every thread of the
+      // warpgroup reaches both barriers, so none waits on a thread that gave up.
+      const int row = quarter * 32 + e_lane;
+      const long long slot0 = static_cast<long long>(split_tile) * p.parts * 2 + e_s;  // part 0
+      if (ok) {
+        const long long slot = slot0 + 2LL * part;
+        // [HD/4 float4 columns][128 rows]: a warp's 32 rows are 512 contiguous bytes per access
+        float4* wo = reinterpret_cast<float4*>(p.ws_o) + slot * (HD / 4) * kBlockM + row;
+#pragma unroll
+        for (int c = 0; c < HD / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(e_tO + c * 32, o);
+          tmem_wait_ld();
+          reg_fence(o);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            wo[(c * 8 + i) * kBlockM] = make_float4(__uint_as_float(o[4 * i]), __uint_as_float(o[4 * i + 1]),
+                                        __uint_as_float(o[4 * i + 2]),
+                                        __uint_as_float(o[4 * i + 3]));
+        }
+        p.ws_ml[slot * kBlockM + row] = make_float2(m, l);
+        __threadfence();
+      }
+      // barriers 1 and 2: the warpgroups of query tiles 0 and 1
+      const bool all_ok = e_s == 0 ? named_bar_and<1, kBlockM>(ok) : named_bar_and<2, kBlockM>(ok);
+      volatile int* last_flag = reinterpret_cast<volatile int*>(smem + L::kMiscOffset + 8) + e_s;
+      if (quarter == 0 && e_lane == 0) {
+        int last = 0;
+        if (all_ok) {
+          int* counter = p.counters + split_tile * 2 + e_s;
+          last = atomicAdd(counter, 1) == p.parts - 1;
+          if (last) atomicExch(counter, 0);
+        }
+        *last_flag = last;
+      }
+      if (e_s == 0) named_bar_sync<1, kBlockM>();
+      else named_bar_sync<2, kBlockM>();
+      if (*last_flag) {
+        __threadfence();
+        float mx = -INFINITY;
+        for (int q = 0; q < p.parts; ++q)
+          mx = fmaxf(mx, __ldcg(&p.ws_ml[(slot0 + 2LL * q) * kBlockM + row]).x);
+        float sum = 0.f;
+        for (int q = 0; q < p.parts; ++q) {
+          const float2 ml = __ldcg(&p.ws_ml[(slot0 + 2LL * q) * kBlockM + row]);
+          if (ml.x != -INFINITY) sum += ml.y * ex2_approx(ml.x - mx);
+        }
+        const float inv = (sum > 0.f && mx != -INFINITY) ? 1.f / sum : 0.f;
+#pragma unroll 1
+        for (int c = 0; c < HD / 32; ++c) {
+          float acc[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+          for (int q = 0; q < p.parts; ++q) {
+            const long long slot = slot0 + 2LL * q;
+            const float2 ml = __ldcg(&p.ws_ml[slot * kBlockM + row]);
+            const float w = ml.x == -INFINITY ? 0.f : ex2_approx(ml.x - mx);
+            const float4* src = reinterpret_cast<const float4*>(p.ws_o) +
+                                (slot * (HD / 4) + c * 8) * kBlockM + row;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float4 x = __ldcg(src + i * kBlockM);
+              acc[4 * i] = fmaf(w, x.x, acc[4 * i]);
+              acc[4 * i + 1] = fmaf(w, x.y, acc[4 * i + 1]);
+              acc[4 * i + 2] = fmaf(w, x.z, acc[4 * i + 2]);
+              acc[4 * i + 3] = fmaf(w, x.w, acc[4 * i + 3]);
+            }
+          }
+          uint32_t o[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(acc[i]);
+          emit(c, o, inv);
+        }
+      }
+    } else if (ok) {
       // rows that saw no key (bottom-right causal with seq_q > seq_k) are written as zeros
       const float inv = (l > 0.f && m != -INFINITY) ? 1.f / l : 0.f;
-      const bool valid = q_row < p.seq_q;
-      __nv_bfloat16* dst;
-      if (p.scatter) {
-        // the row's owner: the rank whose sequence rows contain it (rows are contiguous per rank)
-        int owner = 0;
-        while (owner + 1 < p.world && q_row >= p.row_start[owner + 1]) ++owner;
-        dst = p.outs[owner] + static_cast<long long>(b) * p.outs_strides[owner][2] +
-              static_cast<long long>(q_row - p.row_start[owner]) * p.outs_strides[owner][0] +
-              static_cast<long long>(head + p.head_offset) * p.outs_strides[owner][1];
-      } else {
-        dst = p.out + static_cast<long long>(b) * p.out_b +
-              static_cast<long long>(q_row) * p.out_s + static_cast<long long>(head) * p.out_h;
-      }
 #pragma unroll
       for (int c = 0; c < HD / 32; ++c) {
         uint32_t o[32];
         if (n_kv > 0) {
-          tmem_ld32(tO + c * 32, o);
+          tmem_ld32(e_tO + c * 32, o);
           tmem_wait_ld();
           reg_fence(o);
         } else {
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] = 0u;
         }
-        uint32_t packed[16];
-        if constexpr (FP8) {  // V's per-channel scales
-          const float* vs = p.v_scale +
-                            (static_cast<long long>(b) * p.heads_kv + kv_head) * HD + c * 32;
-#pragma unroll
-          for (int i = 0; i < 16; ++i)
-            packed[i] = pack_bf16x2(__uint_as_float(o[2 * i]) * inv * vs[2 * i],
-                                    __uint_as_float(o[2 * i + 1]) * inv * vs[2 * i + 1]);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 16; ++i)
-            packed[i] = pack_bf16x2(__uint_as_float(o[2 * i]) * inv,
-                                    __uint_as_float(o[2 * i + 1]) * inv);
-        }
-        if (valid) {
-          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            d4[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2],
-                               packed[4 * i + 3]);
-        }
+        emit(c, o, inv);
       }
+    }
     }
   } else if (warp == 8) {
     // ------------------------------------------------------------------------ TMA producer
@@ -525,7 +706,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_expect_tx(&kv_full[stage], L::kTileBytes);
         for (int box = 0; box < L::kBoxes; ++box)
           tma_load_4d(sKV + stage * L::kTileBytes + box * L::kBoxBytes, map, &kv_full[stage],
-                      box * 64, j * kBlockN, kv_head, b);
+                      box * 64, (kv_first + j) * kBlockN, kv_head, b);
       }
       __syncwarp();
       issued = i + 1;
@@ -700,21 +881,161 @@ static int make_map(CUtensorMap* map, const void* base, int elem_bytes, int head
   return r == CUDA_SUCCESS ? 0 : cudaErrorInvalidValue;
 }
 
+// ------------------------------------------------------------------ split of the last wave
+// A CTA owns a tile for its whole key range, so when the tiles are not a whole number of waves
+// of one CTA per SM, the last wave leaves SMs idle (C2 at Ulysses degree 8: 390 tiles on 148
+// SMs = 2.64 waves, the third 64 % full). The tiles past the last whole wave can instead run
+// as `parts` CTAs each over a share of the keys, merged by the last one to finish. The plan
+// minimises a wave count model in units of one key block's time per CTA, with a fixed cost per
+// CTA (start-up, pipeline fill, epilogue) and per merged part.
+constexpr double kUnitCost = 4.0;    // key blocks' worth of time a CTA spends outside its loop
+constexpr double kMergeCost = 0.5;   // per part read back by the merging CTA
+constexpr int kMaxParts = 16;
+constexpr long long kMaxWholeWaves = 16;
+constexpr size_t kMaxWorkspace = size_t(1) << 30;
+
+struct SplitPlan {
+  long long n_full;
+  int parts;
+  long long n_split;
+};
+
+static size_t split_bytes(long long n_split, int parts, int head_dim) {
+  const size_t rows = static_cast<size_t>(n_split) * parts * kQTiles * kBlockM;
+  const size_t counters = (static_cast<size_t>(n_split) * kQTiles * sizeof(int) + 255) & ~size_t(255);
+  return counters + rows * sizeof(float2) + rows * head_dim * sizeof(float);
+}
+
+static SplitPlan plan_split(long long tiles, int n_blocks, int sms, int head_dim) {
+  SplitPlan best = {tiles, 1, 0};
+  const char* env = getenv("COZY_ATTENTION_SPLIT");
+  if (env != nullptr && env[0] == '0' && env[1] == '\0') return best;
+  if (sms <= 0 || n_blocks < 2 || tiles <= 0) return best;
+  // Past many whole waves the SMs' finishing times have drifted apart by more than a tile, and
+  // the ones that finish early absorb the partial wave: measured on B200 at the C2 shape, 21.08
+  // waves gain nothing from a split (1185 vs 1191 TFLOP/s), 10.5 waves gain 2.8 %, 2.6 waves 12 %.
+  if (tiles / sms >= kMaxWholeWaves) return best;
+  const double unsplit = static_cast<double>((tiles + sms - 1) / sms) * (n_blocks + kUnitCost);
+  // a clear gain only: a split costs workspace traffic the model leaves out
+  double best_time = 0.97 * unsplit;
+  const long long whole = tiles / sms;
+  for (long long waves = whole; waves >= 0 && waves >= whole - 1; --waves) {
+    const long long tail = tiles - waves * sms;
+    if (tail <= 0) continue;
+    // parts start on even key blocks: at least two blocks each
+    for (int parts = 2; parts <= kMaxParts && parts <= n_blocks / 2; ++parts) {
+      const long long units = tail * parts;
+      const long long split_waves = (units + sms - 1) / sms;
+      const int longest = 2 * ((n_blocks / 2 + parts - 1) / parts) + (n_blocks & 1);
+      const double t = waves * (n_blocks + kUnitCost) +
+                       split_waves * (longest + kUnitCost + kMergeCost * parts);
+      if (t < best_time && split_bytes(tail, parts, head_dim) <= kMaxWorkspace) {
+        best_time = t;
+        best = {tiles - tail, parts, tail};
+      }
+    }
+  }
+  return best;
+}
+
+// Split workspace, one per (device, stream): launches on one stream run in order, so they can
+// share it; launches on different streams may overlap and must not. Grows, never shrinks; not
+// allocated while the stream is being captured (the launch then runs unsplit).
+struct Workspace {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+};
+
+static void* split_workspace(int device, cudaStream_t stream, size_t bytes) {
+  static std::mutex mutex;
+  static std::map<std::pair<int, uintptr_t>, Workspace> spaces;
+  std::lock_guard<std::mutex> lock(mutex);
+  Workspace& w = spaces[{device, reinterpret_cast<uintptr_t>(stream)}];
+  if (w.bytes >= bytes) return w.ptr;
+  cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &capture) != cudaSuccess ||
+      capture != cudaStreamCaptureStatusNone) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  if (w.ptr != nullptr) {
+    // earlier launches on this stream may still read the old buffer
+    if (cudaStreamSynchronize(stream) != cudaSuccess || cudaFree(w.ptr) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    w = Workspace{};
+  }
+  const size_t want = std::max(bytes, size_t(64) << 20);
+  if (cudaMalloc(&w.ptr, want) != cudaSuccess) {
+    cudaGetLastError();
+    w = Workspace{};
+    return nullptr;
+  }
+  w.bytes = want;
+  return w.ptr;
+}
+
+static int sm_count(int device) {
+  static int counts[64] = {};
+  if (device >= 64) return 0;
+  if (counts[device] == 0)
+    cudaDeviceGetAttribute(&counts[device], cudaDevAttrMultiProcessorCount, device);
+  return counts[device];
+}
+
 template <int HD, bool FP8>
 static int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
-                  const AttentionParams& p, cudaStream_t stream) {
+                  AttentionParams& p, bool allow_split, cudaStream_t stream) {
   using L = AttentionSmem<HD, FP8>;
   static bool configured[64] = {};
   int device = 0;
   cudaGetDevice(&device);
   if (device < 64 && !configured[device]) {
-    cudaError_t e = cudaFuncSetAttribute(attention_fwd_kernel<HD, FP8>,
+    cudaError_t e = cudaFuncSetAttribute(attention_fwd_kernel<HD, FP8, false>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(attention_fwd_kernel<HD, FP8, true>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
     if (e != cudaSuccess) return e;
     configured[device] = true;
   }
-  dim3 grid(p.q_blocks, p.heads_q, p.batch);
-  attention_fwd_kernel<HD, FP8><<<grid, kThreads, L::kAlloc, stream>>>(mq, mk, mv, p);
+  const long long tiles = static_cast<long long>(p.q_blocks) * p.heads_q * p.batch;
+  SplitPlan plan = {tiles, 1, 0};
+  // causal tiles differ in length and are ordered heaviest first: they are not split
+  if (allow_split && !p.causal)
+    plan = plan_split(tiles, (p.seq_k + kBlockN - 1) / kBlockN, sm_count(device), HD);
+  p.n_full = static_cast<int>(plan.n_full);
+  p.parts = plan.parts;
+  p.ws_o = nullptr;
+  p.ws_ml = nullptr;
+  p.counters = nullptr;
+  if (plan.n_split > 0) {
+    uint8_t* ws = static_cast<uint8_t*>(
+        split_workspace(device, stream, split_bytes(plan.n_split, plan.parts, HD)));
+    if (ws == nullptr) {
+      p.n_full = static_cast<int>(tiles);
+      p.parts = 1;
+      plan.n_split = 0;
+    } else {
+      const size_t rows = static_cast<size_t>(plan.n_split) * plan.parts * kQTiles * kBlockM;
+      const size_t counter_bytes =
+          (static_cast<size_t>(plan.n_split) * kQTiles * sizeof(int) + 255) & ~size_t(255);
+      p.counters = reinterpret_cast<int*>(ws);
+      p.ws_ml = reinterpret_cast<float2*>(ws + counter_bytes);
+      p.ws_o = reinterpret_cast<float*>(ws + counter_bytes + rows * sizeof(float2));
+      cudaError_t e = cudaMemsetAsync(p.counters, 0, counter_bytes, stream);
+      if (e != cudaSuccess) return e;
+    }
+  }
+  const long long units = p.n_full + plan.n_split * plan.parts;
+  if (units > 0x7fffffffLL) return cudaErrorInvalidValue;
+  if (plan.n_split > 0)
+    attention_fwd_kernel<HD, FP8, true>
+        <<<static_cast<unsigned>(units), kThreads, L::kAlloc, stream>>>(mq, mk, mv, p);
+  else
+    attention_fwd_kernel<HD, FP8, false>
+        <<<static_cast<unsigned>(units), kThreads, L::kAlloc, stream>>>(mq, mk, mv, p);
   return cudaGetLastError();
 }
 
@@ -732,7 +1053,7 @@ static int attention_launch(const void* q, const void* k, const void* v, void* o
                             const long long* q_strides, const long long* k_strides,
                             const long long* v_strides, const long long* o_strides,
                             const CozyHeadMap* head_map, const CozyScatter* scatter, int causal,
-                            float scale, int* status, const Fp8Operands* fp8,
+                            float scale, int* status, const Fp8Operands* fp8, bool allow_split,
                             cudaStream_t stream) {
   if (head_dim != 64 && head_dim != 128) return cudaErrorNotSupported;
   if (fp8 != nullptr && head_dim != 128) return cudaErrorNotSupported;
@@ -750,6 +1071,8 @@ static int attention_launch(const void* q, const void* k, const void* v, void* o
   const int kv_last = (heads_q - 1 + map.q_base) / map.group - map.kv_base;
   if (kv_first < 0 || kv_last >= heads_kv) return cudaErrorInvalidValue;
   if (batch > 65535 || heads_q > 65535) return cudaErrorInvalidValue;
+  if (static_cast<long long>(batch) * heads_q * ((seq_q + 255) / 256) > 0x7fffffffLL)
+    return cudaErrorInvalidValue;
   const void* ptrs[4] = {q, k, v, scatter ? q : out};
   for (const void* ptr : ptrs)
     if (ptr == nullptr || reinterpret_cast<uintptr_t>(ptr) % 16 != 0) return cudaErrorInvalidValue;
@@ -838,10 +1161,10 @@ static int attention_launch(const void* q, const void* k, const void* v, void* o
     p.scale_seq = fp8->scale_seq;
     p.n_cuts = fp8->n_cuts;
     for (int c = 0; c < fp8->n_cuts; ++c) p.cuts[c] = fp8->cuts[c];
-    return launch<128, true>(mq, mk, mv, p, stream);
+    return launch<128, true>(mq, mk, mv, p, allow_split, stream);
   }
-  if (head_dim == 128) return launch<128, false>(mq, mk, mv, p, stream);
-  return launch<64, false>(mq, mk, mv, p, stream);
+  if (head_dim == 128) return launch<128, false>(mq, mk, mv, p, allow_split, stream);
+  return launch<64, false>(mq, mk, mv, p, allow_split, stream);
 }
 
 int attention_forward(const void* q, const void* k, const void* v, void* out, int batch,
@@ -852,7 +1175,40 @@ int attention_forward(const void* q, const void* k, const void* v, void* out, in
                       float scale, int* status, cudaStream_t stream) {
   return attention_launch(q, k, v, out, batch, seq_q, seq_k, heads_q, heads_kv, head_dim,
                           q_strides, k_strides, v_strides, o_strides, head_map, scatter, causal,
-                          scale, status, nullptr, stream);
+                          scale, status, nullptr, true, stream);
+}
+
+// The split plan attention_forward takes on the current device for a non-FP8 call of this shape
+// (FP8 calls take the same plan): `whole` tiles of 256 query rows run in one CTA each, the
+// remaining tiles in `parts` CTAs each (parts = 1: nothing is split).
+int attention_split_plan(int batch, int seq_q, int seq_k, int heads_q, int head_dim, int causal,
+                         long long* whole, int* parts) {
+  if (whole == nullptr || parts == nullptr || batch <= 0 || seq_q <= 0 || seq_k <= 0 ||
+      heads_q <= 0 || (head_dim != 64 && head_dim != 128))
+    return cudaErrorInvalidValue;
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return e;
+  const long long tiles =
+      static_cast<long long>(batch) * heads_q * ((seq_q + kQTiles * kBlockM - 1) / (kQTiles * kBlockM));
+  SplitPlan plan = {tiles, 1, 0};
+  if (!causal) plan = plan_split(tiles, (seq_k + kBlockN - 1) / kBlockN, sm_count(device), head_dim);
+  *whole = plan.n_full;
+  *parts = plan.parts;
+  return cudaSuccess;
+}
+
+// As attention_forward, without the split of the last wave (which needs a workspace this
+// library allocates): allocates nothing.
+int attention_forward_unsplit(const void* q, const void* k, const void* v, void* out, int batch,
+                              int seq_q, int seq_k, int heads_q, int heads_kv, int head_dim,
+                              const long long* q_strides, const long long* k_strides,
+                              const long long* v_strides, const long long* o_strides,
+                              const CozyHeadMap* head_map, const CozyScatter* scatter,
+                              int causal, float scale, int* status, cudaStream_t stream) {
+  return attention_launch(q, k, v, out, batch, seq_q, seq_k, heads_q, heads_kv, head_dim,
+                          q_strides, k_strides, v_strides, o_strides, head_map, scatter, causal,
+                          scale, status, nullptr, false, stream);
 }
 
 int attention_forward_fp8(const void* q, const void* k, const void* v, const float* q_scale,
@@ -865,7 +1221,7 @@ int attention_forward_fp8(const void* q, const void* k, const void* v, const flo
   const Fp8Operands fp8 = {q_scale, k_scale, v_scale, scale_seq, cuts, n_cuts};
   return attention_launch(q, k, v, out, batch, seq_q, seq_k, heads_q, heads_kv, head_dim,
                           q_strides, k_strides, v_strides, o_strides, head_map, scatter, causal,
-                          scale, status, &fp8, stream);
+                          scale, status, &fp8, true, stream);
 }
 
 }  // namespace cozy

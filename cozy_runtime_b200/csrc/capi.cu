@@ -13,6 +13,8 @@ int attention_forward(const void* q, const void* k, const void* v, void* out, in
                       const long long* v_strides, const long long* o_strides,
                       const CozyHeadMap* head_map, const CozyScatter* scatter, int causal,
                       float scale, int* status, cudaStream_t stream);
+int attention_split_plan(int batch, int seq_q, int seq_k, int heads_q, int head_dim, int causal,
+                         long long* whole, int* parts);
 int ulysses_pack(const CozyPackTensor* tensors, int count, int world, int rows, int batch,
                  int head_dim, const CozyRope* rope, cudaStream_t stream);
 int head_norm_rope(const void* x, void* out, int batch, int seq, int heads, int head_dim,
@@ -39,6 +41,12 @@ int cozy_attention_fwd(const void* q, const void* k, const void* v, void* out, i
   return cozy::attention_forward(q, k, v, out, batch, seq_q, seq_k, heads_q, heads_kv, head_dim,
                                  q_strides, k_strides, v_strides, o_strides, head_map, scatter, causal, scale,
                                  status, as_stream(stream));
+}
+
+int cozy_attention_split_plan(int batch, int seq_q, int seq_k, int heads_q, int head_dim,
+                              int causal, long long* whole_tiles, int* parts) {
+  return cozy::attention_split_plan(batch, seq_q, seq_k, heads_q, head_dim, causal, whole_tiles,
+                                    parts);
 }
 
 int cozy_ulysses_pack(const CozyPackTensor* tensors, int count, int world, int rows, int batch,
@@ -69,7 +77,7 @@ const char* cozy_error_name(int code) {
   return cudaGetErrorName(static_cast<cudaError_t>(code));
 }
 
-int cozy_abi_version(void) { return 100; }
+int cozy_abi_version(void) { return 101; }
 
 }  // extern "C"
 

@@ -22,7 +22,7 @@
 #include "../../include/cozy_ulysses.h"
 
 namespace cozy {
-int attention_forward(const void* q, const void* k, const void* v, void* out, int batch,
+int attention_forward_unsplit(const void* q, const void* k, const void* v, void* out, int batch,
                       int seq_q, int seq_k, int heads_q, int heads_kv, int head_dim,
                       const long long* q_strides, const long long* k_strides,
                       const long long* v_strides, const long long* o_strides,
@@ -102,7 +102,7 @@ extern "C" int cozy_rope_attention_fwd_noalloc(
   const long long qs[3] = {1LL * batch * heads_q * head_dim, head_dim, 1LL * heads_q * head_dim};
   const long long ks[3] = {1LL * batch * heads_kv * head_dim, head_dim,
                            1LL * heads_kv * head_dim};
-  return cozy::attention_forward(q_rot, k_rot, v, out, batch, seq, seq, heads_q, heads_kv,
+  return cozy::attention_forward_unsplit(q_rot, k_rot, v, out, batch, seq, seq, heads_q, heads_kv,
                                  head_dim, qs, ks, v_strides, o_strides, nullptr, nullptr, causal,
                                  scale, status, s);
 }

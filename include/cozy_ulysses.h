@@ -66,6 +66,18 @@ COZY_API int cozy_attention_fwd(const void* q, const void* k, const void* v, voi
                        const CozyHeadMap* head_map, const CozyScatter* scatter, int causal,
                        float scale, int* status, uintptr_t stream);
 
+/* How cozy_attention_fwd (and cozy_attention_fwd_fp8) schedule a call of this shape on the
+ * current device. A CTA owns 256 query rows of one (batch, head) for the whole key range, so
+ * tiles that fill no whole wave of one CTA per SM would leave SMs idle; instead, past the first
+ * `*whole_tiles` tiles, each tile runs as `*parts` CTAs over consecutive shares of the keys,
+ * whose partial rows the last CTA to finish merges (an atomic count, no waiting). `*parts` = 1
+ * when nothing is split (always for causal calls). The split needs a workspace the library
+ * allocates once per (device, stream) and keeps; launches on one stream share it in order, and
+ * launches made while the stream is being captured into a graph run unsplit unless it exists.
+ * COZY_ATTENTION_SPLIT=0 in the environment turns the split off. */
+COZY_API int cozy_attention_split_plan(int batch, int seq_q, int seq_k, int heads_q, int head_dim,
+                                       int causal, long long* whole_tiles, int* parts);
+
 /* One tensor of the seq->head exchange's first stage (Q, K or V): this rank's rows
  * [batch, rows, heads, head_dim] (`src`, element strides {seq, head, batch}), optionally
  * RMS-normalised per head and rotated, written as the block each peer receives:
