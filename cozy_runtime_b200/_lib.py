@@ -128,6 +128,36 @@ class Fp8Pack(Structure):
     ]
 
 
+class NarrowTensor(Structure):
+    """`CozyNarrowTensor`."""
+
+    _fields_ = [
+        ("src", c_void_p),
+        ("src_strides", c_longlong * 3),
+        ("heads", c_int),
+        ("shift", c_void_p),
+        ("dst", c_void_p * MAX_PEERS),
+        ("scale_dst", c_void_p * MAX_PEERS),
+        ("head_lo", c_int * MAX_PEERS),
+        ("head_n", c_int * MAX_PEERS),
+        ("row_lo", c_int * MAX_PEERS),
+        ("row_n", c_int * MAX_PEERS),
+    ]
+
+
+class WidenSource(Structure):
+    """`CozyWidenSource`."""
+
+    _fields_ = [
+        ("codes", c_void_p),
+        ("scales", c_void_p),
+        ("row_lo", c_int),
+        ("rows", c_int),
+        ("head_lo", c_int),
+        ("head_n", c_int),
+    ]
+
+
 class CudaCallError(RuntimeError):
     """A library entry point returned a non-zero cudaError_t."""
 
@@ -149,6 +179,19 @@ SIGNATURES = {
     ),
     "cozy_attention_split_plan": (
         [c_int, c_int, c_int, c_int, c_int, c_int, POINTER(c_longlong), POINTER(c_int)],
+        c_int,
+    ),
+    "cozy_key_sum": (
+        [c_void_p, POINTER(c_longlong), c_int, c_int, c_int, c_int, c_void_p, c_uint64], c_int,
+    ),
+    "cozy_narrow_shift": (
+        [c_void_p, c_longlong, c_int, c_int, c_int, c_void_p, c_uint64], c_int,
+    ),
+    "cozy_narrow_pack": (
+        [POINTER(NarrowTensor), c_int, c_int, c_int, c_int, c_int, c_uint64], c_int,
+    ),
+    "cozy_narrow_widen": (
+        [POINTER(WidenSource), c_int, c_int, c_int, c_void_p, POINTER(c_longlong), c_uint64],
         c_int,
     ),
     "cozy_ulysses_pack": (

@@ -17,7 +17,7 @@ PACKAGE = Path(__file__).resolve().parent
 ROOT = PACKAGE.parent
 CSRC = PACKAGE / "csrc"
 LIBRARY = PACKAGE / "libcozy_ulysses.so"
-SOURCES = ["attention_fwd.cu", "stage.cu", "fp8.cu", "peer.cu", "noalloc.cu", "capi.cu"]
+SOURCES = ["attention_fwd.cu", "stage.cu", "fp8.cu", "peer.cu", "noalloc.cu", "narrow.cu", "capi.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

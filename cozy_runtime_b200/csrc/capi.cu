@@ -15,6 +15,14 @@ int attention_forward(const void* q, const void* k, const void* v, void* out, in
                       float scale, int* status, cudaStream_t stream);
 int attention_split_plan(int batch, int seq_q, int seq_k, int heads_q, int head_dim, int causal,
                          long long* whole, int* parts);
+int key_sum(const void* key, const long long* strides, int rows, int batch, int heads,
+            int head_dim, float* sum, cudaStream_t stream);
+int narrow_shift(const float* sum, long long count, int batch, int heads, int head_dim,
+                 float* shift, cudaStream_t stream);
+int narrow_pack(const CozyNarrowTensor* tensors, int count, int world, int rows, int batch,
+                int head_dim, cudaStream_t stream);
+int narrow_widen(const CozyWidenSource* sources, int count, int batch, int head_dim, void* out,
+                 const long long* out_strides, cudaStream_t stream);
 int ulysses_pack(const CozyPackTensor* tensors, int count, int world, int rows, int batch,
                  int head_dim, const CozyRope* rope, cudaStream_t stream);
 int head_norm_rope(const void* x, void* out, int batch, int seq, int heads, int head_dim,
@@ -49,6 +57,26 @@ int cozy_attention_split_plan(int batch, int seq_q, int seq_k, int heads_q, int 
                                     parts);
 }
 
+int cozy_key_sum(const void* key, const long long* strides, int rows, int batch, int heads,
+                 int head_dim, float* sum, uintptr_t stream) {
+  return cozy::key_sum(key, strides, rows, batch, heads, head_dim, sum, as_stream(stream));
+}
+
+int cozy_narrow_shift(const float* sum, long long count, int batch, int heads, int head_dim,
+                      float* shift, uintptr_t stream) {
+  return cozy::narrow_shift(sum, count, batch, heads, head_dim, shift, as_stream(stream));
+}
+
+int cozy_narrow_pack(const CozyNarrowTensor* tensors, int count, int world, int rows, int batch,
+                     int head_dim, uintptr_t stream) {
+  return cozy::narrow_pack(tensors, count, world, rows, batch, head_dim, as_stream(stream));
+}
+
+int cozy_narrow_widen(const CozyWidenSource* sources, int count, int batch, int head_dim,
+                      void* out, const long long* out_strides, uintptr_t stream) {
+  return cozy::narrow_widen(sources, count, batch, head_dim, out, out_strides, as_stream(stream));
+}
+
 int cozy_ulysses_pack(const CozyPackTensor* tensors, int count, int world, int rows, int batch,
                       int head_dim, const CozyRope* rope, uintptr_t stream) {
   if (!tensors) return cudaErrorInvalidValue;
@@ -77,7 +105,7 @@ const char* cozy_error_name(int code) {
   return cudaGetErrorName(static_cast<cudaError_t>(code));
 }
 
-int cozy_abi_version(void) { return 101; }
+int cozy_abi_version(void) { return 102; }
 
 }  // extern "C"
 

@@ -1,0 +1,322 @@
+// The int8 wire of the exchange ("narrow"): rows of Q, K and V (K less a shift every GPU
+// shares) and of the attention's output cross as int8 with one bf16 scale per row, after a turn
+// by the orthonormal Hadamard matrix of the head dimension; the receiver turns them back.
+//
+// Law (src/cozy_runtime/internal/parallel/turn.py:60-82, `law` and `law_back`), per row x of
+// D = 64 or 128 bf16 values:
+//   t     = (x · H) · D^-½ − shift                  H: Sylvester ±1 matrix of order D
+//   scale = bf16(max(max|t| · (1/127), 2^-126))     round to nearest even
+//   code  = sign(q) · ⌊|q| + ½⌋,  q = clamp(t / scale, −127, 127)   (IEEE division)
+//   back  = bf16((code · H) · (scale · D^-½))
+// The turn is a fast Walsh-Hadamard transform across the warp that holds the row (the same
+// matrix: H of order 2n is [[H, H], [H, −H]], one butterfly per index bit). Back, the codes'
+// transform is exact in fp32 (|sum| ≤ 127·128), so `back` equals law_back bit for bit; forward,
+// the fp32 sums of the turn may round in another order than the reference's matrix product.
+//
+// key_sum_kernel:     this rank's fp32 column sums of K (the all-reduced sum / total is the
+//                     shift's source, as src/cozy_runtime/internal/parallel/ulysses.py:588-604).
+// narrow_shift_kernel: shift = turned(sum / total), per (batch, head).
+// narrow_pack_kernel: one warp per row (token, head, batch) of a tensor, its codes and scale
+//                     written to every destination whose rows and heads contain it: by head for
+//                     the first stage (every peer takes its heads of all this rank's rows), by
+//                     row for the output's return (every owner takes its rows of all heads).
+// narrow_widen_kernel: one warp per received row, back to bf16 at any strides.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/cozy_ulysses.h"
+
+namespace cozy {
+
+constexpr float kTiny = 1.17549435e-38f;  // 2^-126, bf16's smallest normal
+
+template <int D>
+struct Turn {
+  static constexpr int kPer = D / 32;  // values a lane holds: lane L has [L·kPer, L·kPer + kPer)
+  static constexpr float kNorm = D == 128 ? 0.08838834764831845f : 0.125f;  // D^-1/2
+};
+
+// x·H for a row spread over the warp (unnormalised).
+template <int D>
+__device__ __forceinline__ void fwht(float (&x)[D / 32], int lane) {
+  constexpr int kPer = D / 32;
+#pragma unroll
+  for (int bit = 1; bit < kPer; bit <<= 1)
+#pragma unroll
+    for (int i = 0; i < kPer; ++i)
+      if (!(i & bit)) {
+        const float u = x[i], w = x[i | bit];
+        x[i] = u + w;
+        x[i | bit] = u - w;
+      }
+#pragma unroll
+  for (int lanes = 1; lanes < 32; lanes <<= 1) {
+    const bool high = (lane & lanes) != 0;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const float other = __shfl_xor_sync(0xffffffffu, x[i], lanes);
+      x[i] = high ? other - x[i] : x[i] + other;
+    }
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(D) key_sum_kernel(const __nv_bfloat16* key, long long s_seq,
+                                                   long long s_head, long long s_batch, int rows,
+                                                   int heads, float* sum) {
+  const int d = threadIdx.x;
+  const int head = blockIdx.y, b = blockIdx.z;
+  const int r0 = blockIdx.x * 256;
+  const int r1 = min(rows, r0 + 256);
+  const __nv_bfloat16* k = key + b * s_batch + head * s_head + d;
+  float acc = 0.f;
+  for (int r = r0; r < r1; ++r) acc += __bfloat162float(k[r * s_seq]);
+  atomicAdd(sum + (static_cast<long long>(b) * heads + head) * D + d, acc);
+}
+
+// One warp per (batch, head): shift = ((sum / count) · H) · D^-½.
+template <int D>
+__global__ void narrow_shift_kernel(const float* sum, float count, int rows_total, float* shift) {
+  constexpr int kPer = D / 32;
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows_total) return;
+  float x[kPer];
+#pragma unroll
+  for (int i = 0; i < kPer; ++i)
+    x[i] = __fdiv_rn(sum[static_cast<long long>(row) * D + lane * kPer + i], count);
+  fwht<D>(x, lane);
+#pragma unroll
+  for (int i = 0; i < kPer; ++i)
+    shift[static_cast<long long>(row) * D + lane * kPer + i] = __fmul_rn(x[i], Turn<D>::kNorm);
+}
+
+struct NarrowArgs {
+  CozyNarrowTensor t[3];
+  int count, world, rows, batch;
+};
+
+template <int D>
+__global__ void __launch_bounds__(256) narrow_pack_kernel(const NarrowArgs a) {
+  constexpr int kPer = D / 32;
+  const CozyNarrowTensor& t = a.t[blockIdx.y];
+  const int lane = threadIdx.x & 31;
+  const long long items = static_cast<long long>(a.rows) * a.batch * t.heads;
+  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  for (long long it = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+       it < items; it += warps) {
+    // head fastest, then batch, then row: consecutive warps fill consecutive destination rows
+    const int h = static_cast<int>(it % t.heads);
+    const long long rb = it / t.heads;
+    const int b = static_cast<int>(rb % a.batch);
+    const int r = static_cast<int>(rb / a.batch);
+    const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(t.src) + b * t.src_strides[2] +
+                               static_cast<long long>(r) * t.src_strides[0] +
+                               h * t.src_strides[1] + lane * kPer;
+    float x[kPer];
+    if constexpr (kPer == 4) {
+      const uint2 v = *reinterpret_cast<const uint2*>(src);
+      const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.x));
+      const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.y));
+      x[0] = lo.x, x[1] = lo.y, x[2] = hi.x, x[3] = hi.y;
+    } else {
+      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src));
+      x[0] = f.x, x[1] = f.y;
+    }
+    fwht<D>(x, lane);
+    const float* shift =
+        t.shift ? t.shift + (static_cast<long long>(b) * t.heads + h) * D + lane * kPer : nullptr;
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      x[i] = __fmul_rn(x[i], Turn<D>::kNorm);
+      if (shift) x[i] = __fsub_rn(x[i], shift[i]);
+      amax = fmaxf(amax, fabsf(x[i]));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const __nv_bfloat16 scale = __float2bfloat16_rn(fmaxf(__fmul_rn(amax, 1.0f / 127.0f), kTiny));
+    const float sf = __bfloat162float(scale);
+    uint32_t word = 0;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const float q = fminf(fmaxf(__fdiv_rn(x[i], sf), -127.f), 127.f);
+      const float mag = floorf(__fadd_rn(fabsf(q), 0.5f));
+      const int code = static_cast<int>(q < 0.f ? -mag : mag);
+      word |= (static_cast<uint32_t>(code) & 0xffu) << (8 * i);
+    }
+    for (int p = 0; p < a.world; ++p) {
+      if (r < t.row_lo[p] || r >= t.row_lo[p] + t.row_n[p]) continue;
+      if (h < t.head_lo[p] || h >= t.head_lo[p] + t.head_n[p]) continue;
+      const long long at = (static_cast<long long>(r - t.row_lo[p]) * a.batch + b) * t.head_n[p] +
+                           (h - t.head_lo[p]);
+      int8_t* dst = static_cast<int8_t*>(t.dst[p]) + at * D + lane * kPer;
+      if constexpr (kPer == 4) *reinterpret_cast<uint32_t*>(dst) = word;
+      else *reinterpret_cast<uint16_t*>(dst) = static_cast<uint16_t>(word);
+      if (lane == 0) static_cast<__nv_bfloat16*>(t.scale_dst[p])[at] = scale;
+    }
+  }
+}
+
+struct WidenArgs {
+  CozyWidenSource s[COZY_MAX_PEERS];
+  int count, batch;
+  __nv_bfloat16* out;
+  long long s_seq, s_head, s_batch;
+};
+
+template <int D>
+__global__ void __launch_bounds__(256) narrow_widen_kernel(const WidenArgs a) {
+  constexpr int kPer = D / 32;
+  const CozyWidenSource& s = a.s[blockIdx.y];
+  const int lane = threadIdx.x & 31;
+  const long long items = static_cast<long long>(s.rows) * a.batch * s.head_n;
+  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  for (long long it = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+       it < items; it += warps) {
+    // items in the codes' own order: [rows][batch][head_n]
+    const int h = static_cast<int>(it % s.head_n);
+    const long long rb = it / s.head_n;
+    const int b = static_cast<int>(rb % a.batch);
+    const int r = static_cast<int>(rb / a.batch);
+    const int8_t* codes = static_cast<const int8_t*>(s.codes) + it * D + lane * kPer;
+    float x[kPer];
+    if constexpr (kPer == 4) {
+      const char4 c = *reinterpret_cast<const char4*>(codes);
+      x[0] = c.x, x[1] = c.y, x[2] = c.z, x[3] = c.w;
+    } else {
+      const char2 c = *reinterpret_cast<const char2*>(codes);
+      x[0] = c.x, x[1] = c.y;
+    }
+    fwht<D>(x, lane);  // integers: exact
+    const float factor =
+        __fmul_rn(__bfloat162float(static_cast<const __nv_bfloat16*>(s.scales)[it]), Turn<D>::kNorm);
+    __nv_bfloat16* dst = a.out + b * a.s_batch + static_cast<long long>(s.row_lo + r) * a.s_seq +
+                         static_cast<long long>(s.head_lo + h) * a.s_head + lane * kPer;
+    if constexpr (kPer == 4) {
+      __nv_bfloat162 lo = __floats2bfloat162_rn(__fmul_rn(x[0], factor), __fmul_rn(x[1], factor));
+      __nv_bfloat162 hi = __floats2bfloat162_rn(__fmul_rn(x[2], factor), __fmul_rn(x[3], factor));
+      uint2 v;
+      v.x = *reinterpret_cast<uint32_t*>(&lo);
+      v.y = *reinterpret_cast<uint32_t*>(&hi);
+      *reinterpret_cast<uint2*>(dst) = v;
+    } else {
+      *reinterpret_cast<__nv_bfloat162*>(dst) =
+          __floats2bfloat162_rn(__fmul_rn(x[0], factor), __fmul_rn(x[1], factor));
+    }
+  }
+}
+
+static int grid_for(long long items) {
+  const long long blocks = (items + 7) / 8;  // 8 warps a block, one item each at first
+  return static_cast<int>(blocks < 148 * 16 ? (blocks > 0 ? blocks : 1) : 148 * 16);
+}
+
+int key_sum(const void* key, const long long* strides, int rows, int batch, int heads,
+            int head_dim, float* sum, cudaStream_t stream) {
+  if (head_dim != 64 && head_dim != 128) return cudaErrorNotSupported;
+  if (key == nullptr || strides == nullptr || sum == nullptr || rows < 0 || batch < 1 || heads < 1)
+    return cudaErrorInvalidValue;
+  if (rows == 0) return cudaSuccess;
+  dim3 grid((rows + 255) / 256, heads, batch);
+  const __nv_bfloat16* k = static_cast<const __nv_bfloat16*>(key);
+  if (head_dim == 128)
+    key_sum_kernel<128><<<grid, 128, 0, stream>>>(k, strides[0], strides[1], strides[2], rows, heads, sum);
+  else
+    key_sum_kernel<64><<<grid, 64, 0, stream>>>(k, strides[0], strides[1], strides[2], rows, heads, sum);
+  return cudaGetLastError();
+}
+
+int narrow_shift(const float* sum, long long count, int batch, int heads, int head_dim,
+                 float* shift, cudaStream_t stream) {
+  if (head_dim != 64 && head_dim != 128) return cudaErrorNotSupported;
+  if (sum == nullptr || shift == nullptr || count <= 0 || count > (1LL << 24) || batch < 1 ||
+      heads < 1)
+    return cudaErrorInvalidValue;
+  const int rows = batch * heads;
+  const int blocks = (rows + 7) / 8;
+  const float c = static_cast<float>(count);  // exact: count ≤ 2^24
+  if (head_dim == 128) narrow_shift_kernel<128><<<blocks, 256, 0, stream>>>(sum, c, rows, shift);
+  else narrow_shift_kernel<64><<<blocks, 256, 0, stream>>>(sum, c, rows, shift);
+  return cudaGetLastError();
+}
+
+int narrow_pack(const CozyNarrowTensor* tensors, int count, int world, int rows, int batch,
+                int head_dim, cudaStream_t stream) {
+  if (head_dim != 64 && head_dim != 128) return cudaErrorNotSupported;
+  if (tensors == nullptr || count < 1 || count > 3 || world < 1 || world > COZY_MAX_PEERS ||
+      rows < 0 || batch < 1)
+    return cudaErrorInvalidValue;
+  NarrowArgs a;
+  a.count = count;
+  a.world = world;
+  a.rows = rows;
+  a.batch = batch;
+  long long most = 0;
+  const int vec = head_dim / 32;  // elements a lane loads: 4 (8 bytes) or 2 (4 bytes)
+  for (int i = 0; i < count; ++i) {
+    const CozyNarrowTensor& t = tensors[i];
+    if (t.src == nullptr || t.heads < 1 || reinterpret_cast<uintptr_t>(t.src) % (2 * vec))
+      return cudaErrorInvalidValue;
+    for (int k = 0; k < 3; ++k)
+      if (t.src_strides[k] <= 0 || t.src_strides[k] % vec) return cudaErrorInvalidValue;
+    if (t.shift != nullptr && reinterpret_cast<uintptr_t>(t.shift) % 4) return cudaErrorInvalidValue;
+    for (int p = 0; p < world; ++p) {
+      if (t.head_n[p] < 0 || t.row_n[p] < 0 || t.head_lo[p] < 0 || t.row_lo[p] < 0 ||
+          t.head_lo[p] + t.head_n[p] > t.heads || t.row_lo[p] + t.row_n[p] > rows)
+        return cudaErrorInvalidValue;
+      if (t.head_n[p] > 0 && t.row_n[p] > 0 &&
+          (t.dst[p] == nullptr || t.scale_dst[p] == nullptr ||
+           reinterpret_cast<uintptr_t>(t.dst[p]) % vec ||
+           reinterpret_cast<uintptr_t>(t.scale_dst[p]) % 2))
+        return cudaErrorInvalidValue;
+    }
+    a.t[i] = t;
+    const long long items = static_cast<long long>(rows) * batch * t.heads;
+    most = items > most ? items : most;
+  }
+  if (most == 0) return cudaSuccess;
+  dim3 grid(grid_for(most), count);
+  if (head_dim == 128) narrow_pack_kernel<128><<<grid, 256, 0, stream>>>(a);
+  else narrow_pack_kernel<64><<<grid, 256, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+int narrow_widen(const CozyWidenSource* sources, int count, int batch, int head_dim, void* out,
+                 const long long* out_strides, cudaStream_t stream) {
+  if (head_dim != 64 && head_dim != 128) return cudaErrorNotSupported;
+  if (sources == nullptr || count < 1 || count > COZY_MAX_PEERS || batch < 1 || out == nullptr ||
+      out_strides == nullptr)
+    return cudaErrorInvalidValue;
+  const int vec = head_dim / 32;
+  if (reinterpret_cast<uintptr_t>(out) % (2 * vec)) return cudaErrorInvalidValue;
+  for (int k = 0; k < 3; ++k)
+    if (out_strides[k] <= 0 || out_strides[k] % vec) return cudaErrorInvalidValue;
+  WidenArgs a;
+  a.count = count;
+  a.batch = batch;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.s_seq = out_strides[0];
+  a.s_head = out_strides[1];
+  a.s_batch = out_strides[2];
+  long long most = 0;
+  for (int i = 0; i < count; ++i) {
+    const CozyWidenSource& s = sources[i];
+    if (s.rows < 0 || s.head_n < 0 || s.row_lo < 0 || s.head_lo < 0) return cudaErrorInvalidValue;
+    if (s.rows > 0 && s.head_n > 0 &&
+        (s.codes == nullptr || s.scales == nullptr ||
+         reinterpret_cast<uintptr_t>(s.codes) % vec || reinterpret_cast<uintptr_t>(s.scales) % 2))
+      return cudaErrorInvalidValue;
+    a.s[i] = s;
+    const long long items = static_cast<long long>(s.rows) * batch * s.head_n;
+    most = items > most ? items : most;
+  }
+  if (most == 0) return cudaSuccess;
+  dim3 grid(grid_for(most), count);
+  if (head_dim == 128) narrow_widen_kernel<128><<<grid, 256, 0, stream>>>(a);
+  else narrow_widen_kernel<64><<<grid, 256, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace cozy

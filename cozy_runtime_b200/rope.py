@@ -92,12 +92,14 @@ def head_norm_rope(
     eps: float = 1e-6,
     normalize: bool = True,
     out: Tensor | None = None,
+    token0: int = 0,
 ) -> Tensor:
     """Per-head RMSNorm then RoPE of [batch, seq, heads, head_dim] bf16 `x` (one launch of
     `cozy_head_norm_rope`): the drop-in for src/cozy_runtime/accel/fusion/_kernels.py:459
     (`head_norm_rope(launch, entry, x, weight, eps, tables, dtype)`, law :177-240) with the
     tables as `rope_tables` lays them out (`RopeSpec`; row = token of `x`'s sequence).
-    `weight`: fp32 [head_dim] or None (unit); `normalize=False` rotates only."""
+    `weight`: fp32 [head_dim] or None (unit); `normalize=False` rotates only; `token0`: the
+    table row of `x`'s first token (a rank's rows of a longer sequence)."""
     import ctypes
 
     import torch
@@ -113,7 +115,7 @@ def head_norm_rope(
         rope_arg = _lib.Rope()
         rope_arg.cos, rope_arg.sin = tables.cos.data_ptr(), tables.sin.data_ptr()
         rope_arg.stride_token, rope_arg.stride_channel = tables.stride_token, tables.stride_channel
-        rope_arg.token0, rope_arg.rotary = 0, tables.rotary
+        rope_arg.token0, rope_arg.rotary = token0, tables.rotary
         rope_arg.interleaved = int(tables.interleaved)
     w = None
     if weight is not None:

@@ -7,7 +7,11 @@ its rows of the attention over the whole sequence, for every head. Differences o
 
 * The first stage is one fused kernel (`cozy_ulysses_pack`): RoPE and per-head RMSNorm (when
   asked), the transpose into per-peer head blocks, for Q, K and V in one launch.
-* Q, K and V cross with NCCL all-to-all (the reference's default wire, ulysses.py:207-246).
+* Q, K and V cross by the kernels' own stores into the peers' receive buffers over NVLink
+  (`peer.PeerGroup`, the default on one node once its formation check passes), or with NCCL
+  all-to-all (the reference's default wire, ulysses.py:207-246).
+* `narrow=True` takes the reference's int8 wire (turn.py): one warp per row turns, scales and
+  quantizes it into every destination, and one widens it back (`narrow.NarrowStep`).
 * With `compute=None` the native sm_100a attention reads the receive buffers in place
   ([S, B, h, D], no unpack) and writes its output straight into the return send buffer; a
   callable `compute` gets [B, S, h, D] views and is served the reference's way.
@@ -37,6 +41,8 @@ from torch import Tensor
 
 from cozy_runtime_b200 import _lib, attention, peer
 from cozy_runtime_b200 import fp8 as fp8_mod
+from cozy_runtime_b200 import narrow as narrow_mod
+from cozy_runtime_b200 import rope as rope_mod
 from cozy_runtime_b200.rope import RopeSpec
 
 Compute = Callable[[Tensor, Tensor, Tensor], Tensor]
@@ -467,12 +473,12 @@ def exchange(
     (NCCL all-to-all); default `COZY_ULYSSES_TRANSPORT`, else "peer" for native attention on a
     CUDA group of one node. `fp8`: Q, K and V cross and multiply as e4m3 (`fp8.Fp8Step`: K less
     its global mean, Q/K Hadamard-rotated with 64-token block scales, V per-channel scales, P as
-    e4m3; head_dim 128, native attention, degree 1 or the peer transport). Returns
-    [B, S_r, H, D] in the query's dtype.
+    e4m3; head_dim 128, native attention, degree 1 or the peer transport). `narrow` (or
+    `narrow(total)`): Q, K less its turned global mean, V and the output cross as int8 with a
+    bf16 scale per row after a Hadamard turn (`narrow.NarrowStep`, the reference's wire; head
+    dims 64 and 128; any dimension that is not a power of two stays wide, as in the reference).
+    Returns [B, S_r, H, D] in the query's dtype.
     """
-    wide = narrow(0) if callable(narrow) else narrow
-    if wide:
-        raise NotImplementedError("the int8 narrow wire is not built on this path")
     if not query.is_cuda:
         raise ValueError("cozy-b200 exchange serves CUDA tensors only")
     if query.dtype != torch.bfloat16:
@@ -498,6 +504,18 @@ def exchange(
         raise ValueError(f"rows {rows} do not match rank {rank}'s {mine} rows of {world}")
     layout = plan(rows, heads, heads_kv)
     began = _Clock.mark(query)
+    # The int8 wire, decided on the agreed total as the reference does (ulysses.py:691): its
+    # Hadamard turn needs a power-of-two head dimension, else the exchange stays wide. The FP8
+    # path's own e4m3 wire is narrower still and takes precedence.
+    total = layout.total
+    wanted = bool(narrow(total) if callable(narrow) else narrow)
+    if wanted and not fp8 and dim & (dim - 1) == 0:
+        if dim not in narrow_mod.ORDERS:
+            raise NotImplementedError(f"the int8 wire serves head_dim {narrow_mod.ORDERS}")
+        return _exchange_narrow(
+            query, key, value, handle, layout, rank, began, compute, causal, scale, rope,
+            norm_q, norm_k, transport,
+        )
 
     if fp8:
         if compute is not None or rope is not None or norm_q is not None or norm_k is not None:
@@ -669,6 +687,193 @@ def _exchange_peer(
         land = pg.view(s, "land", query.dtype)[: batch * mine * heads * dim]
         out.copy_(land.view(batch, mine, heads, dim))
     _CLOCK.add((began, first, last, _Clock.mark(query)), step.moved())
+    return out
+
+
+def _first_law(x: Tensor, rope: RopeSpec | None, norm: Norm | None, token0: int) -> Tensor:
+    """Per-head RMSNorm and RoPE of a rank's rows (global positions from `token0`), as the
+    first stage applies them, into a new tensor: the narrow wire turns the result."""
+    if rope is None and norm is None:
+        return x
+    weight = None if norm is None or norm.weight is None else norm.weight
+    return rope_mod.head_norm_rope(
+        x, rope, weight=weight, offset=0.0 if norm is None else norm.offset,
+        eps=1e-6 if norm is None else norm.eps, normalize=norm is not None, token0=token0,
+    )
+
+
+def _attend_operands(
+    qv: Tensor, kv: Tensor, vv: Tensor, layout: Plan, rank: int, compute: Compute | None,
+    causal: bool, scale: float | None,
+) -> Tensor:
+    """This rank's heads attended over the whole sequence from [B, total, n, D] operands:
+    [B, total, qn, D] rows in a [total][B][qn][D] buffer (the return's source layout)."""
+    batch, total, qn, dim = qv.shape
+    o = torch.empty(total, batch, qn, dim, dtype=qv.dtype, device=qv.device)
+    ov = o.permute(1, 0, 2, 3)
+    if compute is None:
+        head_map = (layout.group, layout.q_lo[rank], layout.kv_lo[rank])
+        attention.attention_into(ov, qv, kv, vv, causal=causal, scale=scale, head_map=head_map)
+        return ov
+    if kv.shape[2] != qn or layout.group != 1:
+        idx = torch.tensor(
+            [(layout.q_lo[rank] + i) // layout.group - layout.kv_lo[rank] for i in range(qn)],
+            device=qv.device,
+        )
+        kv, vv = kv.index_select(2, idx), vv.index_select(2, idx)
+    attended = compute(qv, kv, vv)
+    if attended.shape != (batch, total, qn, dim) or attended.dtype != qv.dtype:
+        raise ValueError("Ulysses attention returned incompatible output")
+    ov.copy_(attended)
+    return ov
+
+
+def _exchange_narrow(
+    query: Tensor,
+    key: Tensor,
+    value: Tensor,
+    handle,
+    layout: Plan,
+    rank: int,
+    began,
+    compute: Compute | None,
+    causal: bool,
+    scale: float | None,
+    rope: RopeSpec | None,
+    norm_q: Norm | None,
+    norm_k: Norm | None,
+    transport: str | None,
+) -> Tensor:
+    """The exchange over the int8 wire (the reference's `narrow=True`, ulysses.py:704-766): K's
+    sums all-reduced and turned into the shift, Q/K/V narrowed into every peer's receive
+    blocks, widened into the operands, attended, the output rows narrowed back to their owners
+    and widened into [B, S_r, H, D]. Crosses over NCCL or the peer transport; at degree 1 the
+    rows still take the wire's law, as the reference's exchange does."""
+    batch, mine, heads, dim = (int(n) for n in query.shape)
+    heads_kv = int(key.shape[2])
+    device = query.device
+    world, total, rows = layout.world, layout.total, layout.rows
+    start = layout.start(rank)
+    query = _first_law(query, rope, norm_q, start)
+    key = _first_law(key, rope, norm_k, start)
+    step = narrow_mod.NarrowStep(query, key, value, layout, rank)
+    k_sum = torch.zeros(batch, heads_kv, dim, dtype=torch.float32, device=device)
+    narrow_mod.key_sum_into(key, k_sum)
+    crossed = False
+    try:
+        if world > 1:
+            crossed = True
+            dist.all_reduce(k_sum, op=dist.ReduceOp.SUM, group=handle)
+        shift = step.shift(k_sum)
+        qn, kvn = layout.q_n[rank], layout.kv_n[rank]
+        i8, bf = torch.int8, torch.bfloat16
+        moved = sum(
+            step.first_block(p, "q") + 2 * step.first_block(p, "kv") + step.return_block(p)
+            for p in range(world) if p != rank
+        ) * (1 + 2 / dim)
+        if (world > 1 and _transport(handle, transport) == "peer"
+                and _peer_ready(handle, device)):
+            pg = peer.group_for(handle, device)
+            status = attention.status_word(device).data_ptr()
+            most_q, most_kv = max(layout.q_n), max(layout.kv_n)
+            sizes = {
+                "nqc": total * batch * most_q * dim, "nqs": total * batch * most_q * 2,
+                "nkc": total * batch * most_kv * dim, "nks": total * batch * most_kv * 2,
+                "nvc": total * batch * most_kv * dim, "nvs": total * batch * most_kv * 2,
+                "nlc": max(rows) * batch * heads * dim, "nls": max(rows) * batch * heads * 2,
+            }
+            with pg.lock:
+                pg.ensure(sizes)
+                seq = pg.next_seq()
+                s = seq & 1
+
+                def first(p: int, kind: str, n: int) -> tuple[int, int]:
+                    at = start * batch * n * dim
+                    return narrow_mod.scale_ptr(
+                        pg.peer(p, s, f"n{kind}c"), pg.peer(p, s, f"n{kind}s"), at, dim
+                    )
+
+                r = range(world)
+                step.pack_to(
+                    shift,
+                    [first(p, "q", layout.q_n[p]) for p in r],
+                    [first(p, "k", layout.kv_n[p]) for p in r],
+                    [first(p, "v", layout.kv_n[p]) for p in r],
+                )
+                pg.signal(peer.QKV, seq)
+                pg.wait(peer.QKV, seq, status)
+                q_op = step.operands(pg.view(s, "nqc", i8), pg.view(s, "nqs", bf), qn)
+                k_op = step.operands(pg.view(s, "nkc", i8), pg.view(s, "nks", bf), kvn)
+                v_op = step.operands(pg.view(s, "nvc", i8), pg.view(s, "nvs", bf), kvn)
+                first_mark = _Clock.mark(query)
+                attended = _attend_operands(q_op, k_op, v_op, layout, rank, compute, causal,
+                                            scale) if qn else None
+                last = _Clock.mark(query)
+                if attended is not None:
+                    # owner p's landing block from this rank: after the blocks of ranks below it
+                    back = []
+                    for p in r:
+                        at = sum(rows[p] * batch * layout.q_n[u] * dim for u in range(rank))
+                        back.append(narrow_mod.scale_ptr(
+                            pg.peer(p, s, "nlc"), pg.peer(p, s, "nls"), at, dim))
+                    step.return_to(attended, back)
+                pg.signal(peer.OUT, seq)
+                pg.wait(peer.OUT, seq, status)
+                out = step.land(pg.view(s, "nlc", i8), pg.view(s, "nls", bf))
+            _CLOCK.add((began, first_mark, last, _Clock.mark(query)), round(moved))
+            return out
+
+        # NCCL crossing (and degree 1: the send blocks are the receive blocks)
+        def blocks(sizes: list[int]) -> tuple[Tensor, Tensor, list[tuple[int, int]]]:
+            codes = torch.empty(sum(sizes), dtype=i8, device=device)
+            scales = torch.empty(sum(sizes) // dim, dtype=bf, device=device)
+            ptrs = [narrow_mod.scale_ptr(codes.data_ptr(), scales.data_ptr(), off, dim)
+                    for off in _offsets(sizes)]
+            return codes, scales, ptrs
+
+        q_sizes = [step.first_block(p, "q") for p in range(world)]
+        kv_sizes = [step.first_block(p, "kv") for p in range(world)]
+        qs, ks, vs = blocks(q_sizes), blocks(kv_sizes), blocks(kv_sizes)
+        step.pack_to(shift, qs[2], ks[2], vs[2])
+        received = []
+        for sent, sizes, n in ((qs, q_sizes, qn), (ks, kv_sizes, kvn), (vs, kv_sizes, kvn)):
+            if world == 1:
+                received.append((sent[0], sent[1]))
+                continue
+            arriving = [rr * batch * n * dim for rr in rows]
+            codes = torch.empty(sum(arriving), dtype=i8, device=device)
+            scales = torch.empty(sum(arriving) // dim, dtype=bf, device=device)
+            dist.all_to_all_single(codes, sent[0], arriving, sizes, group=handle)
+            dist.all_to_all_single(scales, sent[1], [a // dim for a in arriving],
+                                   [z // dim for z in sizes], group=handle)
+            received.append((codes, scales))
+        q_op = step.operands(*received[0], qn)
+        k_op = step.operands(*received[1], kvn)
+        v_op = step.operands(*received[2], kvn)
+        first_mark = _Clock.mark(query)
+        attended = _attend_operands(q_op, k_op, v_op, layout, rank, compute, causal,
+                                    scale) if qn else None
+        last = _Clock.mark(query)
+        back_sizes = [step.return_block(p) for p in range(world)]
+        o_codes, o_scales, o_ptrs = blocks(back_sizes)
+        if attended is not None:
+            step.return_to(attended, o_ptrs)
+        if world == 1:
+            returned = (o_codes, o_scales)
+        else:
+            land_in = [step.landing_block(u) for u in range(world)]
+            codes = torch.empty(sum(land_in), dtype=i8, device=device)
+            scales = torch.empty(sum(land_in) // dim, dtype=bf, device=device)
+            dist.all_to_all_single(codes, o_codes, land_in, back_sizes, group=handle)
+            dist.all_to_all_single(scales, o_scales, [a // dim for a in land_in],
+                                   [z // dim for z in back_sizes], group=handle)
+            returned = (codes, scales)
+        out = step.land(*returned)
+    except BaseException:
+        if crossed:
+            _abort(handle)
+        raise
+    _CLOCK.add((began, first_mark, last, _Clock.mark(query)), round(moved))
     return out
 
 

@@ -233,6 +233,65 @@ COZY_API int cozy_rope_attention_fwd_noalloc(
     const long long* v_strides, const long long* o_strides, const CozyRope* rope, int normalize,
     float norm_eps, int causal, float scale, int* status, uintptr_t stream);
 
+/* --------------------------------------------------------------------- the int8 wire
+ * `exchange(..., narrow=True)`: rows of Q, K (less a shift every GPU shares) and V, and of the
+ * attention's output, cross as int8 with one bf16 scale per row after a turn by the orthonormal
+ * Hadamard matrix of the head dimension (64 or 128), and are turned back on arrival; the law of
+ * src/cozy_runtime/internal/parallel/turn.py:60-82 (`law`, `law_back`):
+ *   t = (x·H)·D^-1/2 - shift;  scale = bf16(max(max|t|·(1/127), 2^-126));
+ *   code = sign(q)·floor(|q| + 1/2) of q = clamp(t / scale, -127, 127);
+ *   back = bf16((code·H)·(scale·D^-1/2)). */
+
+/* Adds this rank's column sums of K [batch, rows, heads, head_dim] (element strides {seq, head,
+ * batch}) into `sum` [batch][heads][head_dim] fp32: the source of the shift after an all-reduce
+ * (replaces `key.sum(1, dtype=torch.float32)` of src/cozy_runtime/internal/parallel/ulysses.py:
+ * 588-604). */
+COZY_API int cozy_key_sum(const void* key, const long long* strides, int rows, int batch,
+                          int heads, int head_dim, float* sum, uintptr_t stream);
+
+/* shift = turned(sum / count) per (batch, head): [batch][heads][head_dim] fp32, K's mean over
+ * `count` rows turned (`_Shift.__call__`, ulysses.py:598-604). */
+COZY_API int cozy_narrow_shift(const float* sum, long long count, int batch, int heads,
+                               int head_dim, float* shift, uintptr_t stream);
+
+/* One tensor of a narrow crossing: bf16 rows [batch, rows, heads, head_dim] (`src`, element
+ * strides {seq, head, batch}), each turned (less `shift` [batch][heads][head_dim] when
+ * non-NULL) and written as codes int8 [row_n[p]][batch][head_n[p]][head_dim] at dst[p] and
+ * scales bf16 [row_n[p]][batch][head_n[p]] at scale_dst[p], for every destination p whose rows
+ * [row_lo[p], +row_n[p]) and heads [head_lo[p], +head_n[p]) hold the row: by head for the first
+ * stage, by row for the output's return. Replaces `turn.narrow` inside `ulysses._pack` (:325-362)
+ * and `_returned` (:459-502). */
+typedef struct CozyNarrowTensor {
+  const void* src;
+  long long src_strides[3];
+  int heads;
+  const float* shift;
+  void* dst[COZY_MAX_PEERS];
+  void* scale_dst[COZY_MAX_PEERS];
+  int head_lo[COZY_MAX_PEERS];
+  int head_n[COZY_MAX_PEERS];
+  int row_lo[COZY_MAX_PEERS];
+  int row_n[COZY_MAX_PEERS];
+} CozyNarrowTensor;
+
+COZY_API int cozy_narrow_pack(const CozyNarrowTensor* tensors, int count, int world, int rows,
+                              int batch, int head_dim, uintptr_t stream);
+
+/* Received codes [rows][batch][head_n][head_dim] int8 and scales [rows][batch][head_n] bf16 of
+ * one source, to rows [row_lo, +rows) and heads [head_lo, +head_n) of `out`. */
+typedef struct CozyWidenSource {
+  const void* codes;
+  const void* scales;
+  int row_lo, rows, head_lo, head_n;
+} CozyWidenSource;
+
+/* `count` sources turned back into bf16 `out` [batch, ·, ·, head_dim] (element strides {seq,
+ * head, batch}), bit for bit `turn.law_back`. Replaces `turn.widen` inside `ulysses._unpack`
+ * (:420-432) and `_land` (:435-457). */
+COZY_API int cozy_narrow_widen(const CozyWidenSource* sources, int count, int batch,
+                               int head_dim, void* out, const long long* out_strides,
+                               uintptr_t stream);
+
 /* ---------------------------------------------------------------- peer memory (one node)
  * The NVLink exchange keeps its receive and landing buffers in memory every GPU of the group
  * maps. These replace the reference's copy-engine exchange buffers

@@ -14,11 +14,15 @@ reference's own code (`tests/golden/make_golden.py`, fixtures `tests/golden/*.np
 from oracle.ulysses_oracle import (  # noqa: F401
     attention_fp32,
     exchange,
+    exchange_narrow,
     fp8_attention_law,
     head_norm_rope,
     heads_padded,
+    narrow_law,
+    narrow_law_back,
     owned_heads,
     quantise_e4m3_per_head,
     quantise_fp8_blocks,
     sequence_rows,
+    turned,
 )

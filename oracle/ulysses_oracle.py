@@ -258,3 +258,74 @@ def quantise_fp8_blocks(x: Tensor, block: int = 64) -> tuple[Tensor, Tensor]:
     scaled = (tiles / descale[:, :, None, :, None]).clamp_(-E4M3_MAX, E4M3_MAX)
     codes = scaled.to(torch.float8_e4m3fn).view(batch, blocks * block, heads, dim)[:, :seq]
     return codes, descale
+
+
+# --------------------------------------------------------------------------- the int8 wire
+def _signs(order: int) -> Tensor:
+    """The ±1 Sylvester matrix of `order` (turn.py:43-52 `signs`): [[H, H], [H, −H]] doubling."""
+    turn = torch.ones(1, 1)
+    while turn.shape[0] < order:
+        turn = torch.cat([torch.cat([turn, turn], 1), torch.cat([turn, -turn], 1)])
+    return turn
+
+
+def turned(rows: Tensor) -> Tensor:
+    """`rows` (last dimension a power of two) turned by the orthonormal Hadamard matrix, in fp32:
+    (rows · H) · D^-½ with H the ±1 Sylvester matrix
+    (src/cozy_runtime/internal/parallel/turn.py:54-58 `turned`)."""
+    order = rows.shape[-1]
+    return (rows.float() @ _signs(order)) * order**-0.5
+
+
+def narrow_law(x: Tensor, shift: Tensor | None = None) -> tuple[Tensor, Tensor]:
+    """Rows of `x` less the turned `shift`, turned, as int8 scaled to each row's absmax/127
+    (floor 2^-126 = bf16's smallest normal, rounded half away from zero), and those scales in
+    `x`'s dtype (turn.py:60-70 `law`)."""
+    t = turned(x)
+    if shift is not None:
+        t = t - shift
+    tiny = torch.finfo(x.dtype).tiny
+    scale = (t.abs().amax(-1, keepdim=True) * (1.0 / 127)).clamp(min=tiny).to(x.dtype)
+    q = (t / scale.float()).clamp(-127, 127)
+    return (q.sign() * (q.abs() + 0.5).floor()).to(torch.int8), scale
+
+
+def narrow_law_back(values: Tensor, scale: Tensor) -> Tensor:
+    """`narrow_law`'s rows back, in `scale`'s dtype (turn.py:73-77 `law_back`)."""
+    order = values.shape[-1]
+    summed = values.float() @ _signs(order)
+    return (summed * (scale.float() * order**-0.5)).to(scale.dtype)
+
+
+def _narrowed(x: Tensor, shift: Tensor | None = None) -> Tensor:
+    """One crossing of the int8 wire: law there, law_back here."""
+    return narrow_law_back(*narrow_law(x, shift))
+
+
+def exchange_narrow(
+    queries: Sequence[Tensor],
+    keys: Sequence[Tensor],
+    values: Sequence[Tensor],
+    compute: Callable[[Tensor, Tensor, Tensor], Tensor],
+) -> list[Tensor]:
+    """`exchange` with the int8 wire (`narrow=True`), simulated in one process. Restates
+    ulysses.py:588-604 and :704-766: K's sum over every rank's rows (fp32), divided by the total
+    and turned, is the shift every rank takes off its K rows (`_Shift`); Q, K and V cross
+    narrowed (`_pack` :353-362) and widen into the operands (`_unpack` :428-429); `compute`
+    runs on them; its output (query dtype) crosses back narrowed (`_returned` :481-482) and
+    widens into its owner's rows (`_land` :451-453). The law is row-local, so narrowing each
+    rank's rows before the crossing equals narrowing them after it, as done here. bf16 rows
+    throughout (the scales take the rows' dtype)."""
+    world = len(queries)
+    total = sum(int(t.shape[1]) for t in queries)
+    summed = sum(k.sum(1, dtype=torch.float32) for k in keys)
+    shift = turned(summed / total)  # [B, Hkv, D]
+    qn = [_narrowed(q) for q in queries]
+    kn = [_narrowed(k, shift[:, None]) for k in keys]
+    vn = [_narrowed(v) for v in values]
+
+    def narrow_out(a: Tensor, b: Tensor, c: Tensor) -> Tensor:
+        return compute(a, b, c)
+
+    outs = exchange(qn, kn, vn, narrow_out)
+    return [_narrowed(o.to(queries[0].dtype)) for o in outs[:world]]

@@ -25,3 +25,7 @@ def ulysses_cases() -> list[str]:
 
 def rope_cases() -> list[str]:
     return sorted(p.name for p in GOLDEN.glob("rope_*.npz"))
+
+
+def narrow_cases() -> list[str]:
+    return sorted(p.name for p in GOLDEN.glob("narrow_*.npz"))

@@ -18,8 +18,13 @@ What it records, each as an `.npz` in this directory:
   `src/cozy_runtime/internal/bench/kernels.py:819` `_fused_rope`, executed with the Triton
   launch replaced by a recorder, so the recorded `want` is the reference code's output.
 * ``fp8_quantise.npz``: `src/cozy_runtime/internal/attention_fp8.py:162` `quantise_eager`.
+* ``turn_*.npz``: the int8 wire's law, `src/cozy_runtime/internal/parallel/turn.py:60`
+  `law` (with and without a shift, which is `turned` of a mean as `_Shift` makes it) and `:73`
+  `law_back`, on bf16 rows.
+* ``narrow_*.npz``: the reference's exchange with `narrow=True` (Q, K less its turned mean, V
+  and the output crossing as int8), bf16 inputs and `sdpa` in bf16, over gloo as above.
 
-Run:  python tests/golden/make_golden.py
+Run:  python tests/golden/make_golden.py [ulysses] [rope] [fp8] [turn] [narrow]  (default: all)
 Third-party pins the reference declares but this container lacks (`tensorfs` 0.27.0,
 `diffusers` 0.40.0) are replaced by import stubs: neither is on the computed path.
 """
@@ -102,7 +107,7 @@ def _inputs(batch, seq, hq, hkv, dim, dtype, seed):
     return q, k, v
 
 
-def _rank(rank, world, port, case, outdir):
+def _rank(rank, world, port, case, outdir, narrow=False):
     import torch.distributed as dist
 
     import_reference()
@@ -124,6 +129,7 @@ def _rank(rank, world, port, case, outdir):
         dist.group.WORLD,
         lambda a, b, c: attention_upstream.sdpa(a, b, c, is_causal=causal),
         site="golden",
+        narrow=narrow,
     )
     torch.save(out, os.path.join(outdir, f"{name}.{rank}.pt"))
     dist.barrier()
@@ -220,7 +226,68 @@ def fp8_golden() -> None:
     print("fp8_quantise:", tuple(codes.shape), tuple(descale.shape))
 
 
+# (name, world, batch, seq, heads_q, heads_kv, dim, causal): bf16 inputs and compute
+NARROW_CASES = [
+    ("w1", 1, 1, 48, 2, 2, 64, False),
+    ("w2_batch2", 2, 2, 37, 4, 4, 128, False),
+    ("w3_padheads", 3, 1, 40, 4, 4, 64, False),
+    ("w2_causal_gqa", 2, 1, 33, 4, 2, 128, True),
+]
+
+
+def narrow_goldens() -> None:
+    import torch.multiprocessing as mp
+
+    for index, (name, world, batch, seq, hq, hkv, dim, causal) in enumerate(NARROW_CASES):
+        case = (name, world, batch, seq, hq, hkv, dim, torch.bfloat16, causal)
+        with tempfile.TemporaryDirectory() as tmp:
+            mp.spawn(_rank, args=(world, 29700 + index, case, tmp, True), nprocs=world, join=True)
+            outs = [torch.load(os.path.join(tmp, f"{name}.{r}.pt")) for r in range(world)]
+        out = torch.cat(outs, dim=1)
+        q, k, v = _inputs(batch, seq, hq, hkv, dim, torch.bfloat16, SEED)
+        rows = [int(o.shape[1]) for o in outs]
+        np.savez_compressed(
+            HERE / f"narrow_{name}.npz",
+            q=to_np(q), k=to_np(k), v=to_np(v), out=to_np(out), heads_kv=hkv, world=world,
+            causal=int(causal), rows=np.array(rows),
+        )
+        print(f"narrow_{name}: rows {rows} out {tuple(out.shape)} {out.dtype}")
+
+
+def turn_goldens() -> None:
+    import_reference()
+    from cozy_runtime.internal.parallel import turn
+
+    for dim in (64, 128):
+        g = torch.Generator().manual_seed(SEED + dim)
+        x = torch.randn(2, 40, 3, dim, generator=g).to(torch.bfloat16)
+        x[0, 3, 1] = 0  # an all-zero row takes the scale floor
+        x[1, 7, 2, 5] = 60.0  # an outlier
+        key = (torch.randn(2, 40, 3, dim, generator=g) + 0.7).to(torch.bfloat16)
+        summed = key.sum(1, dtype=torch.float32)
+        shift = turn.turned(summed / key.shape[1])  # as `_Shift` makes it
+        codes, scale = turn.law(x)
+        kcodes, kscale = turn.law(key, shift[:, None])
+        np.savez_compressed(
+            HERE / f"turn_d{dim}.npz",
+            x=to_np(x), codes=codes.numpy(), scale=to_np(scale), back=to_np(turn.law_back(codes, scale)),
+            key=to_np(key), shift=shift.numpy(), kcodes=kcodes.numpy(), kscale=to_np(kscale),
+            kback=to_np(turn.law_back(kcodes, kscale)),
+        )
+        print(f"turn_d{dim}: codes {tuple(codes.shape)} scale {tuple(scale.shape)}")
+
+
 if __name__ == "__main__":
-    ulysses_goldens()
-    rope_goldens()
-    fp8_golden()
+    import sys as _sys
+
+    parts = set(_sys.argv[1:]) or {"ulysses", "rope", "fp8", "turn", "narrow"}
+    if "ulysses" in parts:
+        ulysses_goldens()
+    if "rope" in parts:
+        rope_goldens()
+    if "fp8" in parts:
+        fp8_golden()
+    if "turn" in parts:
+        turn_goldens()
+    if "narrow" in parts:
+        narrow_goldens()

@@ -103,7 +103,7 @@ def test_library_exports_header_symbols():
     assert declared == set(_lib.SIGNATURES), "the ctypes binding covers the header"
     for name in declared:
         assert hasattr(lib, name), name
-    assert lib.cozy_abi_version() == 101
+    assert lib.cozy_abi_version() == 102
 
 
 def test_error_name_without_gpu():
@@ -128,11 +128,12 @@ def test_product_does_not_import_oracle():
         assert "import oracle" not in text and "from oracle" not in text, path
 
 
-def test_exchange_refuses_cpu_and_narrow():
+def test_exchange_refuses_cpu():
+    """No CPU fallback: host tensors are refused, on the int8 wire too."""
     from cozy_runtime_b200 import ulysses
 
     x = torch.zeros(1, 4, 2, 64, dtype=torch.bfloat16)
-    with pytest.raises(NotImplementedError):
+    with pytest.raises(ValueError):
         ulysses.exchange(x, x, x, None, None, narrow=True)
     with pytest.raises(ValueError):
         ulysses.exchange(x, x, x, None, None)

@@ -5,7 +5,7 @@ import pytest
 import torch
 
 import oracle
-from tests._golden import load, rope_cases, tensor, ulysses_cases
+from tests._golden import load, narrow_cases, rope_cases, tensor, ulysses_cases
 
 
 @pytest.mark.parametrize("name", ulysses_cases())
@@ -79,3 +79,43 @@ def test_fp8_block_law_is_per_head_law_at_whole_sequence():
     assert torch.allclose(descale[:, 0], amax / 448.0)
     back = codes.float() * descale[:, 0][:, None, :, None]
     assert (back - x).abs().max() <= amax.max() / 448.0 * 16
+
+
+@pytest.mark.parametrize("dim", [64, 128])
+def test_turn_law_matches_reference(dim):
+    """The int8 wire's law, bit for bit: codes, bf16 scales and the rows back, without and with
+    K's turned mean as the shift."""
+    case = load(f"turn_d{dim}.npz")
+    x, key = tensor(case["x"]), tensor(case["key"])
+    codes, scale = oracle.narrow_law(x)
+    assert np.array_equal(codes.numpy(), case["codes"])
+    assert torch.equal(scale, tensor(case["scale"]))
+    assert torch.equal(oracle.narrow_law_back(codes, scale), tensor(case["back"]))
+    shift = oracle.turned(key.sum(1, dtype=torch.float32) / key.shape[1])
+    assert torch.equal(shift, torch.from_numpy(case["shift"]))
+    kcodes, kscale = oracle.narrow_law(key, shift[:, None])
+    assert np.array_equal(kcodes.numpy(), case["kcodes"])
+    assert torch.equal(kscale, tensor(case["kscale"]))
+    assert torch.equal(oracle.narrow_law_back(kcodes, kscale), tensor(case["kback"]))
+
+
+@pytest.mark.parametrize("name", narrow_cases())
+def test_narrow_exchange_matches_reference(name):
+    """The whole narrow exchange against the reference's, bit for bit, both running torch SDPA on
+    the bf16 operands as the compute (the reference's CPU `sdpa` calls it)."""
+    case = load(name)
+    q, k, v = (tensor(case[key]) for key in ("q", "k", "v"))
+    world, causal = int(case["world"]), bool(case["causal"])
+    assert oracle.sequence_rows(q.shape[1], world) == [int(r) for r in case["rows"]]
+    parts = [torch.tensor_split(t, world, dim=1) for t in (q, k, v)]
+
+    def sdpa_bf16(a, b, c):  # the reference's compute here: torch SDPA on the bf16 operands
+        out = torch.nn.functional.scaled_dot_product_attention(
+            a.transpose(1, 2), b.transpose(1, 2), c.transpose(1, 2), is_causal=causal
+        )
+        return out.transpose(1, 2)
+
+    outs = oracle.exchange_narrow(*parts, sdpa_bf16)
+    got = torch.cat(outs, dim=1).float()
+    want = tensor(case["out"]).float()
+    assert torch.equal(got, want)
