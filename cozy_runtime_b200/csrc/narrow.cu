@@ -13,8 +13,9 @@
 // transform is exact in fp32 (|sum| ≤ 127·128), so `back` equals law_back bit for bit; forward,
 // the fp32 sums of the turn may round in another order than the reference's matrix product.
 //
-// key_sum_kernel:     this rank's fp32 column sums of K (the all-reduced sum / total is the
-//                     shift's source, as src/cozy_runtime/internal/parallel/ulysses.py:588-604).
+// key_sum_kernel:     this rank's fp32 column sums of K in a fixed order (the all-reduced sum /
+//                     total is the shift's source, as src/cozy_runtime/internal/parallel/
+//                     ulysses.py:588-604).
 // narrow_shift_kernel: shift = turned(sum / total), per (batch, head).
 // narrow_pack_kernel: one warp per row (token, head, batch) of a tensor, its codes and scale
 //                     written to every destination whose rows and heads contain it: by head for
@@ -61,18 +62,43 @@ __device__ __forceinline__ void fwht(float (&x)[D / 32], int lane) {
   }
 }
 
+// One CTA per (batch, head): warp w sums rows w, w + 8, ... (lane L: channels [L·kPer, +kPer)),
+// then the eight partial sums are added in warp order: the same order every call, so the
+// shift, and every code narrowed against it, repeat bit for bit.
 template <int D>
-__global__ void __launch_bounds__(D) key_sum_kernel(const __nv_bfloat16* key, long long s_seq,
-                                                   long long s_head, long long s_batch, int rows,
-                                                   int heads, float* sum) {
-  const int d = threadIdx.x;
-  const int head = blockIdx.y, b = blockIdx.z;
-  const int r0 = blockIdx.x * 256;
-  const int r1 = min(rows, r0 + 256);
-  const __nv_bfloat16* k = key + b * s_batch + head * s_head + d;
-  float acc = 0.f;
-  for (int r = r0; r < r1; ++r) acc += __bfloat162float(k[r * s_seq]);
-  atomicAdd(sum + (static_cast<long long>(b) * heads + head) * D + d, acc);
+__global__ void __launch_bounds__(256) key_sum_kernel(const __nv_bfloat16* key, long long s_seq,
+                                                     long long s_head, long long s_batch,
+                                                     int rows, int heads, float* sum) {
+  constexpr int kPer = D / 32;
+  __shared__ float part[8][D];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int head = blockIdx.x, b = blockIdx.y;
+  const __nv_bfloat16* k = key + b * s_batch + head * s_head + lane * kPer;
+  float acc[kPer];
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) acc[i] = 0.f;
+  for (int r = warp; r < rows; r += 8) {
+    const __nv_bfloat16* row = k + static_cast<long long>(r) * s_seq;
+    if constexpr (kPer == 4) {
+      const uint2 v = *reinterpret_cast<const uint2*>(row);
+      const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.x));
+      const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.y));
+      acc[0] += lo.x, acc[1] += lo.y, acc[2] += hi.x, acc[3] += hi.y;
+    } else {
+      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(row));
+      acc[0] += f.x, acc[1] += f.y;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) part[warp][lane * kPer + i] = acc[i];
+  __syncthreads();
+  if (threadIdx.x < D) {
+    float total = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) total += part[w][threadIdx.x];
+    float* out = sum + (static_cast<long long>(b) * heads + head) * D + threadIdx.x;
+    *out += total;
+  }
 }
 
 // One warp per (batch, head): shift = ((sum / count) · H) · D^-½.
@@ -219,12 +245,17 @@ int key_sum(const void* key, const long long* strides, int rows, int batch, int 
   if (key == nullptr || strides == nullptr || sum == nullptr || rows < 0 || batch < 1 || heads < 1)
     return cudaErrorInvalidValue;
   if (rows == 0) return cudaSuccess;
-  dim3 grid((rows + 255) / 256, heads, batch);
+  const int vec = head_dim / 32;
+  if (reinterpret_cast<uintptr_t>(key) % (2 * vec)) return cudaErrorInvalidValue;
+  for (int i = 0; i < 3; ++i)
+    if (strides[i] <= 0 || strides[i] % vec) return cudaErrorInvalidValue;
+  if (batch > 65535) return cudaErrorInvalidValue;
+  dim3 grid(heads, batch);
   const __nv_bfloat16* k = static_cast<const __nv_bfloat16*>(key);
   if (head_dim == 128)
-    key_sum_kernel<128><<<grid, 128, 0, stream>>>(k, strides[0], strides[1], strides[2], rows, heads, sum);
+    key_sum_kernel<128><<<grid, 256, 0, stream>>>(k, strides[0], strides[1], strides[2], rows, heads, sum);
   else
-    key_sum_kernel<64><<<grid, 64, 0, stream>>>(k, strides[0], strides[1], strides[2], rows, heads, sum);
+    key_sum_kernel<64><<<grid, 256, 0, stream>>>(k, strides[0], strides[1], strides[2], rows, heads, sum);
   return cudaGetLastError();
 }
 

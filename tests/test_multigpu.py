@@ -15,7 +15,7 @@ import pytest
 import torch
 
 import oracle
-from tests._golden import load, tensor, ulysses_cases
+from tests._golden import load, narrow_cases, tensor, ulysses_cases
 
 pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
 
@@ -32,7 +32,8 @@ def _port() -> int:
         return s.getsockname()[1]
 
 
-def _rank(rank, world, port, inputs, causal, outdir, rope_args, transport, fp8=False):
+def _rank(rank, world, port, inputs, causal, outdir, rope_args, transport, fp8=False,
+          narrow=False):
     import torch.distributed as dist
 
     from cozy_runtime_b200 import rope as rope_mod
@@ -51,7 +52,7 @@ def _rank(rank, world, port, inputs, causal, outdir, rope_args, transport, fp8=F
         spec = rope_mod.axial(rope_args[0], (44, 42, 42), after=rope_args[1]).to(device)
     outs = [
         ulysses.exchange(q, k, v, dist.group.WORLD, None, causal=causal, rope=spec,
-                         transport=transport, fp8=fp8)
+                         transport=transport, fp8=fp8, narrow=narrow)
         for _ in range(3)
     ]
     torch.cuda.synchronize()
@@ -65,11 +66,13 @@ def _rank(rank, world, port, inputs, causal, outdir, rope_args, transport, fp8=F
     dist.destroy_process_group()
 
 
-def _run(inputs, world, causal=False, rope_args=None, transport="peer", fp8=False):
+def _run(inputs, world, causal=False, rope_args=None, transport="peer", fp8=False,
+         narrow=False):
     import torch.multiprocessing as mp
 
     with tempfile.TemporaryDirectory() as tmp:
-        mp.spawn(_rank, args=(world, _port(), inputs, causal, tmp, rope_args, transport, fp8),
+        mp.spawn(_rank, args=(world, _port(), inputs, causal, tmp, rope_args, transport, fp8,
+                              narrow),
                  nprocs=world, join=True)
         return torch.cat([torch.load(os.path.join(tmp, f"{r}.pt")) for r in range(world)], dim=1)
 
@@ -142,3 +145,33 @@ def test_fp8_exchange_peer_against_law(world, hq, hkv, causal):
 
     assert cos(got, law) >= 0.999
     assert cos(got, oracle.attention_fp32(q, k, v, causal=causal)) >= 0.995
+
+
+@pytest.mark.parametrize("transport", ["peer", "nccl"])
+@pytest.mark.parametrize("name", narrow_cases())
+def test_narrow_exchange_matches_reference_golden(name, transport):
+    """The int8 wire between GPU processes against the reference's own narrow exchange."""
+    case = load(name)
+    world = int(case["world"])
+    if world < 2 or world > _gpus():
+        pytest.skip(f"needs {world} GPUs")
+    inputs = tuple(tensor(case[key]) for key in ("q", "k", "v"))
+    got = _run(inputs, world, causal=bool(case["causal"]), transport=transport, narrow=True)
+    _check(got, tensor(case["out"]).float())
+
+
+@pytest.mark.parametrize("world,hq,hkv,causal", [(2, 4, 4, False), (4, 8, 2, True), (8, 16, 16, False)])
+@pytest.mark.parametrize("transport", ["peer", "nccl"])
+def test_narrow_exchange_against_oracle(world, hq, hkv, causal, transport):
+    if world > _gpus():
+        pytest.skip(f"needs {world} GPUs")
+    g = torch.Generator().manual_seed(world * 31 + hq)
+    seq = 1000 + world
+    q = torch.randn(1, seq, hq, 128, generator=g).to(torch.bfloat16)
+    k = torch.randn(1, seq, hkv, 128, generator=g).to(torch.bfloat16)
+    v = torch.randn(1, seq, hkv, 128, generator=g).to(torch.bfloat16)
+    got = _run((q, k, v), world, causal=causal, transport=transport, narrow=True)
+    parts = [torch.tensor_split(t, world, dim=1) for t in (q, k, v)]
+    want = torch.cat(oracle.exchange_narrow(
+        *parts, lambda a, b, c: oracle.attention_fp32(a, b, c, causal=causal)), dim=1)
+    _check(got, want.float())
