@@ -104,35 +104,59 @@ __device__ __forceinline__ unsigned row_group_mask() {
                         : (((1u << CHUNKS) - 1u) << ((threadIdx.x & 31) / CHUNKS * CHUNKS));
 }
 
-// grid: x covers rows × batch × head_n[p] destination rows (CHUNKS threads each), y = peer,
-// z = tensor. One thread = 8 channels of one destination row.
+// Destination rows a thread carries: their loads are issued before the first row's math. Two
+// rows at 8 CTAs an SM (32 registers) measured best on B200 (C2 first stage: 291 µs at one row,
+// 268 µs at two, 301 µs at two without the register cap, 335 µs at four); the limit is the
+// 16-byte reads an SM keeps in flight.
+constexpr int kPackRows = 2;
+
+// grid: x covers rows × batch × head_n[p] destination rows (CHUNKS threads each, kPackRows
+// passes of 256 / CHUNKS rows per CTA), y = peer, z = tensor. One thread = 8 channels of one
+// destination row per pass.
 template <int HD>
-__global__ void __launch_bounds__(256) pack_kernel(const PackArgs a) {
+__global__ void __launch_bounds__(256, 8) pack_kernel(const PackArgs a) {
   constexpr int CHUNKS = HD / 8;
-  constexpr int ROWS_PER_BLOCK = 256 / CHUNKS;
+  constexpr int ROWS_PER_PASS = 256 / CHUNKS;
   const CozyPackTensor& t = a.t[blockIdx.z];
   const int peer = blockIdx.y;
   const unsigned n = static_cast<unsigned>(t.head_n[peer]);
   const int chunk = threadIdx.x % CHUNKS;
   // destination rows number below 2^31 (checked on the host): 32-bit index arithmetic
-  const unsigned row = blockIdx.x * ROWS_PER_BLOCK + threadIdx.x / CHUNKS;
   const unsigned total = static_cast<unsigned>(a.rows) * a.batch * n;
-  // Whole row groups leave together: every lane of a row's group shares `row`.
-  if (n == 0 || row >= total) return;
-  // destination order [rows][batch][n]
-  const unsigned hh = row % n;
-  const unsigned sb = row / n;
-  const unsigned b = sb % static_cast<unsigned>(a.batch);
-  const unsigned s = sb / static_cast<unsigned>(a.batch);
-  const int head = t.head_lo[peer] + static_cast<int>(hh);
-  const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(t.src) + s * t.src_strides[0] +
-                             head * t.src_strides[1] + b * t.src_strides[2];
+  const unsigned first = blockIdx.x * (kPackRows * ROWS_PER_PASS) + threadIdx.x / CHUNKS;
+  // Whole row groups leave together: every lane of a row's group shares its rows.
+  if (n == 0 || first >= total) return;
   const int d0 = chunk * 8;
-  float x[8];
-  unpack8(*reinterpret_cast<const uint4*>(src + d0), x);
-  norm_rope_row<HD>(x, d0, chunk, row_group_mask<CHUNKS>(), a.rope.token0 + s, t, a.rope);
-  __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(t.dst[peer]) + static_cast<long long>(row) * HD + d0;
-  *reinterpret_cast<uint4*>(dst) = pack8(x);
+  float x[kPackRows][8];
+  unsigned token[kPackRows];
+#pragma unroll
+  for (int k = 0; k < kPackRows; ++k) {
+    const unsigned row = first + k * ROWS_PER_PASS;
+    token[k] = 0;
+    if (row < total) {
+      // destination order [rows][batch][n]
+      const unsigned hh = row % n;
+      const unsigned sb = row / n;
+      const unsigned b = sb % static_cast<unsigned>(a.batch);
+      const unsigned s = sb / static_cast<unsigned>(a.batch);
+      token[k] = s;
+      const int head = t.head_lo[peer] + static_cast<int>(hh);
+      const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(t.src) +
+                                 s * t.src_strides[0] + head * t.src_strides[1] +
+                                 b * t.src_strides[2];
+      unpack8(*reinterpret_cast<const uint4*>(src + d0), x[k]);
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kPackRows; ++k) {
+    const unsigned row = first + k * ROWS_PER_PASS;
+    if (row >= total) break;
+    norm_rope_row<HD>(x[k], d0, chunk, row_group_mask<CHUNKS>(), a.rope.token0 + token[k], t,
+                      a.rope);
+    __nv_bfloat16* dst =
+        static_cast<__nv_bfloat16*>(t.dst[peer]) + static_cast<long long>(row) * HD + d0;
+    *reinterpret_cast<uint4*>(dst) = pack8(x[k]);
+  }
 }
 
 // The standalone form: [batch, seq, heads, HD] in, the same shape out, any strides.
@@ -246,7 +270,7 @@ int ulysses_pack(const CozyPackTensor* tensors, int count, int world, int rows, 
   const long long dest_rows = static_cast<long long>(rows) * batch * max_n;
   if (dest_rows == 0) return cudaSuccess;
   if (dest_rows >= (1LL << 31)) return cudaErrorInvalidValue;  // the kernel indexes in 32 bits
-  const int rows_per_block = 256 / (head_dim / 8);
+  const int rows_per_block = kPackRows * 256 / (head_dim / 8);
   const long long blocks = (dest_rows + rows_per_block - 1) / rows_per_block;
   dim3 grid(static_cast<unsigned>(blocks), world, count);
   if (head_dim == 128)
