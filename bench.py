@@ -312,6 +312,8 @@ def main() -> None:
     parser.add_argument("--impl", default="cozy", choices=["cozy", "reference"])
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
+    parser.add_argument("--narrow", action="store_true",
+                        help="the int8 wire (exchange(..., narrow=True)); not the headline")
     parser.add_argument("--heads", type=int, default=0,
                         help="profiling only: fewer heads (same sequence and layout)")
     args = parser.parse_args()
@@ -363,7 +365,8 @@ def main() -> None:
 
     def step(qq, kk, vv):
         return ulysses.exchange(qq, kk, vv, group, None, rows=rows, causal=cfg["causal"],
-                                rope=spec, norm_q=norm, norm_k=norm, fp8=fp8)
+                                rope=spec, norm_q=norm, norm_k=norm, fp8=fp8,
+                                narrow=args.narrow)
 
     for _ in range(args.warmup):
         step(q, k, v)
@@ -467,6 +470,9 @@ def main() -> None:
         # two signal and two wait kernels (peer); FP8 adds the statistics kernel
         transport = os.environ.get("COZY_ULYSSES_TRANSPORT", "peer")
         per_step = 2 + (0 if world == 1 else (1 if transport == "nccl" else 4)) + (1 if fp8 else 0)
+        if args.narrow:  # key sums, shift, pack, 3 widens, attention, return pack, land widen
+            per_step = 9 + (2 if cfg["rope"] or cfg["norm"] else 0) + (
+                4 if world > 1 and transport == "peer" else 0)
         profile = ROOT / "profiles" / f"attention_fwd_{args.config}_traffic.json"
         traffic = None
         if profile.exists():
@@ -495,6 +501,7 @@ def main() -> None:
                 "causal": cfg["causal"],
                 "parallelism": f"ulysses{world}",
                 "rows_per_rank": rows,
+                "wire": "int8 (narrow)" if args.narrow else ("e4m3" if fp8 else "bf16"),
                 "l2": "inputs larger than L2 (no flush)",
             },
             "layer": {

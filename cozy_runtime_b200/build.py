@@ -19,6 +19,9 @@ CSRC = PACKAGE / "csrc"
 LIBRARY = PACKAGE / "libcozy_ulysses.so"
 SOURCES = ["attention_fwd.cu", "stage.cu", "fp8.cu", "peer.cu", "noalloc.cu", "narrow.cu", "capi.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+#: Sources compiled with IEEE fp32 semantics (denormals kept, exact division and square root):
+#: the int8 wire's law must round as the reference's CPU arithmetic does.
+EXACT = {"narrow.cu"}
 
 
 def nvcc() -> str:
@@ -28,13 +31,13 @@ def nvcc() -> str:
     return found
 
 
-def flags(verbose: bool = False) -> list[str]:
+def flags(verbose: bool = False, exact: bool = False) -> list[str]:
     out = [
         *ARCH,
         "-O3",
         "-std=c++17",
         "-lineinfo",
-        "--use_fast_math",
+        *(["-ftz=false", "-prec-div=true", "-prec-sqrt=true"] if exact else ["--use_fast_math"]),
         "-Xcompiler",
         "-fPIC,-fvisibility=hidden",
         "-I",
@@ -61,7 +64,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     objects = []
     for source in SOURCES:
         obj = out_dir / (Path(source).stem + ".o")
-        cmd = [nvcc(), *flags(verbose), "-c", str(CSRC / source), "-o", str(obj)]
+        cmd = [nvcc(), *flags(verbose, source in EXACT), "-c", str(CSRC / source), "-o", str(obj)]
         subprocess.run(cmd, check=True)
         objects.append(str(obj))
     tmp = LIBRARY.with_suffix(".so.tmp")

@@ -13,7 +13,8 @@
 // transform is exact in fp32 (|sum| ≤ 127·128), so `back` equals law_back bit for bit; forward,
 // the fp32 sums of the turn may round in another order than the reference's matrix product.
 //
-// key_sum_kernel:     this rank's fp32 column sums of K in a fixed order (the all-reduced sum /
+// key_sum_kernel:     this rank's fp32 column sums of K in a fixed order, one 8-CTA cluster per
+//                     (batch, head) (the all-reduced sum /
 //                     total is the shift's source, as src/cozy_runtime/internal/parallel/
 //                     ulysses.py:588-604).
 // narrow_shift_kernel: shift = turned(sum / total), per (batch, head).
@@ -22,6 +23,7 @@
 //                     the first stage (every peer takes its heads of all this rank's rows), by
 //                     row for the output's return (every owner takes its rows of all heads).
 // narrow_widen_kernel: one warp per received row, back to bf16 at any strides.
+#include <cooperative_groups.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -29,6 +31,8 @@
 #include "../../include/cozy_ulysses.h"
 
 namespace cozy {
+
+namespace cg = cooperative_groups;
 
 constexpr float kTiny = 1.17549435e-38f;  // 2^-126, bf16's smallest normal
 
@@ -53,52 +57,81 @@ __device__ __forceinline__ void fwht(float (&x)[D / 32], int lane) {
       }
 #pragma unroll
   for (int lanes = 1; lanes < 32; lanes <<= 1) {
-    const bool high = (lane & lanes) != 0;
+    // the lane holding the butterfly's upper half keeps (other - x), the lower (x + other):
+    // other + sign·x, one FMA (exact: sign is ±1)
+    const float sign = (lane & lanes) ? -1.f : 1.f;
 #pragma unroll
     for (int i = 0; i < kPer; ++i) {
       const float other = __shfl_xor_sync(0xffffffffu, x[i], lanes);
-      x[i] = high ? other - x[i] : x[i] + other;
+      x[i] = __fmaf_rn(sign, x[i], other);
     }
   }
 }
 
-// One CTA per (batch, head): warp w sums rows w, w + 8, ... (lane L: channels [L·kPer, +kPer)),
-// then the eight partial sums are added in warp order: the same order every call, so the
-// shift, and every code narrowed against it, repeat bit for bit.
+// One 8-CTA cluster per (batch, head): CTA c of the cluster sums rows [c·rows/8, (c+1)·rows/8),
+// its warp w rows w, w + 32, ... of that share (lane L: channels [L·kPer, +kPer)); the warps'
+// sums are added in warp order, then CTA 0 adds the eight CTAs' sums in rank order through
+// distributed shared memory. The same order every call, so the shift, and every code narrowed
+// against it, repeat bit for bit.
+constexpr int kSumCluster = 8;
+
+constexpr int kSumWarps = 32;
+
 template <int D>
-__global__ void __launch_bounds__(256) key_sum_kernel(const __nv_bfloat16* key, long long s_seq,
-                                                     long long s_head, long long s_batch,
-                                                     int rows, int heads, float* sum) {
+__global__ void __cluster_dims__(kSumCluster, 1, 1) __launch_bounds__(kSumWarps * 32)
+    key_sum_kernel(const __nv_bfloat16* key, long long s_seq, long long s_head, long long s_batch,
+                   int rows, int heads, float* sum) {
   constexpr int kPer = D / 32;
-  __shared__ float part[8][D];
+  __shared__ float part[kSumWarps][D];
+  __shared__ float cta_total[D];
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = static_cast<int>(cluster.block_rank());
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int head = blockIdx.x, b = blockIdx.y;
+  const int head = blockIdx.x / kSumCluster, b = blockIdx.y;
+  const int r0 = static_cast<int>(static_cast<long long>(rows) * rank / kSumCluster);
+  const int r1 = static_cast<int>(static_cast<long long>(rows) * (rank + 1) / kSumCluster);
   const __nv_bfloat16* k = key + b * s_batch + head * s_head + lane * kPer;
-  float acc[kPer];
+  // four rows in flight a warp, four accumulators (rows r + 32u of each pass), added in that
+  // order at the end
+  float acc[4][kPer];
 #pragma unroll
-  for (int i = 0; i < kPer; ++i) acc[i] = 0.f;
-  for (int r = warp; r < rows; r += 8) {
-    const __nv_bfloat16* row = k + static_cast<long long>(r) * s_seq;
-    if constexpr (kPer == 4) {
-      const uint2 v = *reinterpret_cast<const uint2*>(row);
-      const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.x));
-      const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.y));
-      acc[0] += lo.x, acc[1] += lo.y, acc[2] += hi.x, acc[3] += hi.y;
-    } else {
-      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(row));
-      acc[0] += f.x, acc[1] += f.y;
+  for (int u = 0; u < 4; ++u)
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) acc[u][i] = 0.f;
+  for (int r = r0 + warp; r < r1; r += 4 * kSumWarps) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (r + kSumWarps * u >= r1) break;
+      const __nv_bfloat16* row = k + static_cast<long long>(r + kSumWarps * u) * s_seq;
+      if constexpr (kPer == 4) {
+        const uint2 v = *reinterpret_cast<const uint2*>(row);
+        const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.x));
+        const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.y));
+        acc[u][0] += lo.x, acc[u][1] += lo.y, acc[u][2] += hi.x, acc[u][3] += hi.y;
+      } else {
+        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(row));
+        acc[u][0] += f.x, acc[u][1] += f.y;
+      }
     }
   }
 #pragma unroll
-  for (int i = 0; i < kPer; ++i) part[warp][lane * kPer + i] = acc[i];
+  for (int i = 0; i < kPer; ++i)
+    part[warp][lane * kPer + i] = ((acc[0][i] + acc[1][i]) + acc[2][i]) + acc[3][i];
   __syncthreads();
   if (threadIdx.x < D) {
     float total = 0.f;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) total += part[w][threadIdx.x];
-    float* out = sum + (static_cast<long long>(b) * heads + head) * D + threadIdx.x;
-    *out += total;
+    for (int w = 0; w < kSumWarps; ++w) total += part[w][threadIdx.x];
+    cta_total[threadIdx.x] = total;
   }
+  cluster.sync();  // every CTA's share is in its shared memory
+  if (rank == 0 && threadIdx.x < D) {
+    float total = 0.f;
+#pragma unroll
+    for (int c = 0; c < kSumCluster; ++c) total += cluster.map_shared_rank(cta_total, c)[threadIdx.x];
+    sum[(static_cast<long long>(b) * heads + head) * D + threadIdx.x] += total;
+  }
+  cluster.sync();  // no CTA leaves while CTA 0 still reads its shared memory
 }
 
 // One warp per (batch, head): shift = ((sum / count) · H) · D^-½.
@@ -123,64 +156,116 @@ struct NarrowArgs {
   int count, world, rows, batch;
 };
 
+#ifndef COZY_NARROW_PACK_GROUP
+#define COZY_NARROW_PACK_GROUP 1
+#endif
+#ifndef COZY_NARROW_WIDEN_GROUP
+#define COZY_NARROW_WIDEN_GROUP 1
+#endif
+// Heads a warp loads before it turns the first. Measured on B200 at C2 (24 heads × 33272 rows):
+// pack of Q/K/V 555 µs at 1, 588 at 2, 626 at 4; widen 104 µs at 1, 111 at 4, 139 at 8 — the
+// kernels issue ~160 instructions a row (the turn's five shuffle rounds, the quantisation), so
+// extra loads in flight cost occupancy for no gain.
+constexpr int kPackGroup = COZY_NARROW_PACK_GROUP;
+constexpr int kWidenGroup = COZY_NARROW_WIDEN_GROUP;
+// Scales from here up divide by one reciprocal and a correction (below): the residual of the
+// quotient cannot underflow.
+constexpr float kFastDivide = 7.88860905e-31f;  // 2^-100
+
+// One row (token r, batch b, head h) held by the warp: turned, shifted, scaled and quantised,
+// then written to every destination that holds it.
+template <int D>
+__device__ __forceinline__ void narrow_row(float (&x)[D / 32], int lane, const float* shift,
+                                           const NarrowArgs& a, const CozyNarrowTensor& t, int r,
+                                           int b, int h) {
+  constexpr int kPer = D / 32;
+  fwht<D>(x, lane);
+  uint32_t amax_bits = 0;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    x[i] = __fmul_rn(x[i], Turn<D>::kNorm);
+    if (shift) x[i] = __fsub_rn(x[i], shift[i]);
+    amax_bits = max(amax_bits, __float_as_uint(fabsf(x[i])));
+  }
+  // non-negative floats order like their bit patterns: one warp reduction instruction
+  const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, amax_bits));
+  const __nv_bfloat16 scale = __float2bfloat16_rn(fmaxf(__fmul_rn(amax, 1.0f / 127.0f), kTiny));
+  const float sf = __bfloat162float(scale);
+  // q = t / scale rounded to nearest, as IEEE division: q0 = t·(1/scale), then one correction
+  // by the exact residual t − q0·scale (Markstein's step; checked equal to division on 4M
+  // fp32 samples with ties and their neighbours, scales 2^-100 ... 2^100). Smaller scales
+  // (rows of tiny values) divide outright. `sf` is the same in the whole warp.
+  const bool fast = sf >= kFastDivide;
+  const float inv = __frcp_rn(sf);
+  uint32_t word = 0;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    float q;
+    if (fast) {
+      const float q0 = __fmul_rn(x[i], inv);
+      q = __fmaf_rn(__fmaf_rn(-q0, sf, x[i]), inv, q0);
+    } else {
+      q = __fdiv_rn(x[i], sf);
+    }
+    q = fminf(fmaxf(q, -127.f), 127.f);
+    // half away from zero: |q| + 1/2 is exact below 2^23, so truncation rounds it
+    const int code = __float2int_rz(__fadd_rn(q, copysignf(0.5f, q)));
+    word |= (static_cast<uint32_t>(code) & 0xffu) << (8 * i);
+  }
+  for (int p = 0; p < a.world; ++p) {
+    if (r < t.row_lo[p] || r >= t.row_lo[p] + t.row_n[p]) continue;
+    if (h < t.head_lo[p] || h >= t.head_lo[p] + t.head_n[p]) continue;
+    const long long at =
+        (static_cast<long long>(r - t.row_lo[p]) * a.batch + b) * t.head_n[p] + (h - t.head_lo[p]);
+    int8_t* dst = static_cast<int8_t*>(t.dst[p]) + at * D + lane * kPer;
+    if constexpr (kPer == 4) *reinterpret_cast<uint32_t*>(dst) = word;
+    else *reinterpret_cast<uint16_t*>(dst) = static_cast<uint16_t>(word);
+    if (lane == 0) static_cast<__nv_bfloat16*>(t.scale_dst[p])[at] = scale;
+  }
+}
+
+// One warp per (row, batch) pair of a tensor, its heads in turn: the pair's index math runs once
+// (32-bit: rows × batch < 2^31, checked on the host), each head's row is one 8- or 4-byte load a
+// lane.
 template <int D>
 __global__ void __launch_bounds__(256) narrow_pack_kernel(const NarrowArgs a) {
   constexpr int kPer = D / 32;
   const CozyNarrowTensor& t = a.t[blockIdx.y];
   const int lane = threadIdx.x & 31;
-  const long long items = static_cast<long long>(a.rows) * a.batch * t.heads;
-  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
-  for (long long it = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-       it < items; it += warps) {
-    // head fastest, then batch, then row: consecutive warps fill consecutive destination rows
-    const int h = static_cast<int>(it % t.heads);
-    const long long rb = it / t.heads;
-    const int b = static_cast<int>(rb % a.batch);
-    const int r = static_cast<int>(rb / a.batch);
-    const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(t.src) + b * t.src_strides[2] +
-                               static_cast<long long>(r) * t.src_strides[0] +
-                               h * t.src_strides[1] + lane * kPer;
-    float x[kPer];
-    if constexpr (kPer == 4) {
-      const uint2 v = *reinterpret_cast<const uint2*>(src);
-      const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.x));
-      const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.y));
-      x[0] = lo.x, x[1] = lo.y, x[2] = hi.x, x[3] = hi.y;
-    } else {
-      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src));
-      x[0] = f.x, x[1] = f.y;
-    }
-    fwht<D>(x, lane);
-    const float* shift =
-        t.shift ? t.shift + (static_cast<long long>(b) * t.heads + h) * D + lane * kPer : nullptr;
-    float amax = 0.f;
+  const unsigned pairs = static_cast<unsigned>(a.rows) * static_cast<unsigned>(a.batch);
+  const unsigned warps = gridDim.x * (blockDim.x >> 5);
+  for (unsigned rb = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); rb < pairs;
+       rb += warps) {
+    const int b = static_cast<int>(rb % static_cast<unsigned>(a.batch));
+    const int r = static_cast<int>(rb / static_cast<unsigned>(a.batch));
+    const __nv_bfloat16* base = static_cast<const __nv_bfloat16*>(t.src) + b * t.src_strides[2] +
+                                static_cast<long long>(r) * t.src_strides[0] + lane * kPer;
+    const float* shift_base =
+        t.shift ? t.shift + static_cast<long long>(b) * t.heads * D + lane * kPer : nullptr;
+    for (int h0 = 0; h0 < t.heads; h0 += kPackGroup) {
+      // the group's rows are loaded before any is turned: kPackGroup reads in flight a lane
+      float x[kPackGroup][kPer];
 #pragma unroll
-    for (int i = 0; i < kPer; ++i) {
-      x[i] = __fmul_rn(x[i], Turn<D>::kNorm);
-      if (shift) x[i] = __fsub_rn(x[i], shift[i]);
-      amax = fmaxf(amax, fabsf(x[i]));
-    }
+      for (int g = 0; g < kPackGroup; ++g) {
+        const int h = h0 + g;
+        if (h >= t.heads) break;
+        const __nv_bfloat16* src = base + h * t.src_strides[1];
+        if constexpr (kPer == 4) {
+          const uint2 v = *reinterpret_cast<const uint2*>(src);
+          const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.x));
+          const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.y));
+          x[g][0] = lo.x, x[g][1] = lo.y, x[g][2] = hi.x, x[g][3] = hi.y;
+        } else {
+          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src));
+          x[g][0] = f.x, x[g][1] = f.y;
+        }
+      }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const __nv_bfloat16 scale = __float2bfloat16_rn(fmaxf(__fmul_rn(amax, 1.0f / 127.0f), kTiny));
-    const float sf = __bfloat162float(scale);
-    uint32_t word = 0;
-#pragma unroll
-    for (int i = 0; i < kPer; ++i) {
-      const float q = fminf(fmaxf(__fdiv_rn(x[i], sf), -127.f), 127.f);
-      const float mag = floorf(__fadd_rn(fabsf(q), 0.5f));
-      const int code = static_cast<int>(q < 0.f ? -mag : mag);
-      word |= (static_cast<uint32_t>(code) & 0xffu) << (8 * i);
-    }
-    for (int p = 0; p < a.world; ++p) {
-      if (r < t.row_lo[p] || r >= t.row_lo[p] + t.row_n[p]) continue;
-      if (h < t.head_lo[p] || h >= t.head_lo[p] + t.head_n[p]) continue;
-      const long long at = (static_cast<long long>(r - t.row_lo[p]) * a.batch + b) * t.head_n[p] +
-                           (h - t.head_lo[p]);
-      int8_t* dst = static_cast<int8_t*>(t.dst[p]) + at * D + lane * kPer;
-      if constexpr (kPer == 4) *reinterpret_cast<uint32_t*>(dst) = word;
-      else *reinterpret_cast<uint16_t*>(dst) = static_cast<uint16_t>(word);
-      if (lane == 0) static_cast<__nv_bfloat16*>(t.scale_dst[p])[at] = scale;
+      for (int g = 0; g < kPackGroup; ++g) {
+        const int h = h0 + g;
+        if (h >= t.heads) break;
+        narrow_row<D>(x[g], lane, shift_base ? shift_base + h * D : nullptr, a, t, r, b, h);
+      }
     }
   }
 }
@@ -192,50 +277,65 @@ struct WidenArgs {
   long long s_seq, s_head, s_batch;
 };
 
+// One warp per (row, batch) pair of a source, its heads in turn (codes are [rows][batch][n]).
 template <int D>
 __global__ void __launch_bounds__(256) narrow_widen_kernel(const WidenArgs a) {
   constexpr int kPer = D / 32;
   const CozyWidenSource& s = a.s[blockIdx.y];
   const int lane = threadIdx.x & 31;
-  const long long items = static_cast<long long>(s.rows) * a.batch * s.head_n;
-  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
-  for (long long it = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-       it < items; it += warps) {
-    // items in the codes' own order: [rows][batch][head_n]
-    const int h = static_cast<int>(it % s.head_n);
-    const long long rb = it / s.head_n;
-    const int b = static_cast<int>(rb % a.batch);
-    const int r = static_cast<int>(rb / a.batch);
-    const int8_t* codes = static_cast<const int8_t*>(s.codes) + it * D + lane * kPer;
-    float x[kPer];
-    if constexpr (kPer == 4) {
-      const char4 c = *reinterpret_cast<const char4*>(codes);
-      x[0] = c.x, x[1] = c.y, x[2] = c.z, x[3] = c.w;
-    } else {
-      const char2 c = *reinterpret_cast<const char2*>(codes);
-      x[0] = c.x, x[1] = c.y;
-    }
-    fwht<D>(x, lane);  // integers: exact
-    const float factor =
-        __fmul_rn(__bfloat162float(static_cast<const __nv_bfloat16*>(s.scales)[it]), Turn<D>::kNorm);
-    __nv_bfloat16* dst = a.out + b * a.s_batch + static_cast<long long>(s.row_lo + r) * a.s_seq +
-                         static_cast<long long>(s.head_lo + h) * a.s_head + lane * kPer;
-    if constexpr (kPer == 4) {
-      __nv_bfloat162 lo = __floats2bfloat162_rn(__fmul_rn(x[0], factor), __fmul_rn(x[1], factor));
-      __nv_bfloat162 hi = __floats2bfloat162_rn(__fmul_rn(x[2], factor), __fmul_rn(x[3], factor));
-      uint2 v;
-      v.x = *reinterpret_cast<uint32_t*>(&lo);
-      v.y = *reinterpret_cast<uint32_t*>(&hi);
-      *reinterpret_cast<uint2*>(dst) = v;
-    } else {
-      *reinterpret_cast<__nv_bfloat162*>(dst) =
-          __floats2bfloat162_rn(__fmul_rn(x[0], factor), __fmul_rn(x[1], factor));
+  const unsigned pairs = static_cast<unsigned>(s.rows) * static_cast<unsigned>(a.batch);
+  const unsigned warps = gridDim.x * (blockDim.x >> 5);
+  for (unsigned rb = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); rb < pairs;
+       rb += warps) {
+    const int b = static_cast<int>(rb % static_cast<unsigned>(a.batch));
+    const int r = static_cast<int>(rb / static_cast<unsigned>(a.batch));
+    const long long first = static_cast<long long>(rb) * s.head_n;  // item of head 0
+    __nv_bfloat16* out = a.out + b * a.s_batch + static_cast<long long>(s.row_lo + r) * a.s_seq +
+                         static_cast<long long>(s.head_lo) * a.s_head + lane * kPer;
+    for (int h0 = 0; h0 < s.head_n; h0 += kWidenGroup) {
+      // the group's codes and scales are loaded before any row is turned back
+      float x[kWidenGroup][kPer];
+      float scale[kWidenGroup];
+#pragma unroll
+      for (int g = 0; g < kWidenGroup; ++g) {
+        const long long it = first + h0 + g;
+        if (h0 + g >= s.head_n) break;
+        const int8_t* codes = static_cast<const int8_t*>(s.codes) + it * D + lane * kPer;
+        if constexpr (kPer == 4) {
+          const char4 c = *reinterpret_cast<const char4*>(codes);
+          x[g][0] = c.x, x[g][1] = c.y, x[g][2] = c.z, x[g][3] = c.w;
+        } else {
+          const char2 c = *reinterpret_cast<const char2*>(codes);
+          x[g][0] = c.x, x[g][1] = c.y;
+        }
+        scale[g] = __bfloat162float(static_cast<const __nv_bfloat16*>(s.scales)[it]);
+      }
+#pragma unroll
+      for (int g = 0; g < kWidenGroup; ++g) {
+        if (h0 + g >= s.head_n) break;
+        fwht<D>(x[g], lane);  // integers: exact
+        const float factor = __fmul_rn(scale[g], Turn<D>::kNorm);
+        __nv_bfloat16* dst = out + (h0 + g) * a.s_head;
+        if constexpr (kPer == 4) {
+          __nv_bfloat162 lo =
+              __floats2bfloat162_rn(__fmul_rn(x[g][0], factor), __fmul_rn(x[g][1], factor));
+          __nv_bfloat162 hi =
+              __floats2bfloat162_rn(__fmul_rn(x[g][2], factor), __fmul_rn(x[g][3], factor));
+          uint2 v;
+          v.x = *reinterpret_cast<uint32_t*>(&lo);
+          v.y = *reinterpret_cast<uint32_t*>(&hi);
+          *reinterpret_cast<uint2*>(dst) = v;
+        } else {
+          *reinterpret_cast<__nv_bfloat162*>(dst) =
+              __floats2bfloat162_rn(__fmul_rn(x[g][0], factor), __fmul_rn(x[g][1], factor));
+        }
+      }
     }
   }
 }
 
 static int grid_for(long long items) {
-  const long long blocks = (items + 7) / 8;  // 8 warps a block, one item each at first
+  const long long blocks = (items + 7) / 8;  // 8 warps a block, one (row, batch) pair each at first
   return static_cast<int>(blocks < 148 * 16 ? (blocks > 0 ? blocks : 1) : 148 * 16);
 }
 
@@ -249,13 +349,15 @@ int key_sum(const void* key, const long long* strides, int rows, int batch, int 
   if (reinterpret_cast<uintptr_t>(key) % (2 * vec)) return cudaErrorInvalidValue;
   for (int i = 0; i < 3; ++i)
     if (strides[i] <= 0 || strides[i] % vec) return cudaErrorInvalidValue;
-  if (batch > 65535) return cudaErrorInvalidValue;
-  dim3 grid(heads, batch);
+  if (batch > 65535 || heads > (1 << 24)) return cudaErrorInvalidValue;
+  dim3 grid(heads * kSumCluster, batch);
   const __nv_bfloat16* k = static_cast<const __nv_bfloat16*>(key);
   if (head_dim == 128)
-    key_sum_kernel<128><<<grid, 256, 0, stream>>>(k, strides[0], strides[1], strides[2], rows, heads, sum);
+    key_sum_kernel<128><<<grid, kSumWarps * 32, 0, stream>>>(k, strides[0], strides[1], strides[2],
+                                                             rows, heads, sum);
   else
-    key_sum_kernel<64><<<grid, 256, 0, stream>>>(k, strides[0], strides[1], strides[2], rows, heads, sum);
+    key_sum_kernel<64><<<grid, kSumWarps * 32, 0, stream>>>(k, strides[0], strides[1], strides[2],
+                                                            rows, heads, sum);
   return cudaGetLastError();
 }
 
@@ -284,7 +386,6 @@ int narrow_pack(const CozyNarrowTensor* tensors, int count, int world, int rows,
   a.world = world;
   a.rows = rows;
   a.batch = batch;
-  long long most = 0;
   const int vec = head_dim / 32;  // elements a lane loads: 4 (8 bytes) or 2 (4 bytes)
   for (int i = 0; i < count; ++i) {
     const CozyNarrowTensor& t = tensors[i];
@@ -304,11 +405,11 @@ int narrow_pack(const CozyNarrowTensor* tensors, int count, int world, int rows,
         return cudaErrorInvalidValue;
     }
     a.t[i] = t;
-    const long long items = static_cast<long long>(rows) * batch * t.heads;
-    most = items > most ? items : most;
   }
-  if (most == 0) return cudaSuccess;
-  dim3 grid(grid_for(most), count);
+  const long long pairs = static_cast<long long>(rows) * batch;
+  if (pairs == 0) return cudaSuccess;
+  if (pairs >= (1LL << 31)) return cudaErrorInvalidValue;  // 32-bit pair index
+  dim3 grid(grid_for(pairs), count);
   if (head_dim == 128) narrow_pack_kernel<128><<<grid, 256, 0, stream>>>(a);
   else narrow_pack_kernel<64><<<grid, 256, 0, stream>>>(a);
   return cudaGetLastError();
@@ -340,8 +441,9 @@ int narrow_widen(const CozyWidenSource* sources, int count, int batch, int head_
          reinterpret_cast<uintptr_t>(s.codes) % vec || reinterpret_cast<uintptr_t>(s.scales) % 2))
       return cudaErrorInvalidValue;
     a.s[i] = s;
-    const long long items = static_cast<long long>(s.rows) * batch * s.head_n;
-    most = items > most ? items : most;
+    const long long pairs = static_cast<long long>(s.rows) * batch;
+    if (pairs >= (1LL << 31)) return cudaErrorInvalidValue;  // 32-bit pair index
+    most = pairs > most ? pairs : most;
   }
   if (most == 0) return cudaSuccess;
   dim3 grid(grid_for(most), count);

@@ -168,26 +168,45 @@ struct NormRopeArgs {
 };
 
 template <int HD>
-__global__ void __launch_bounds__(256) head_norm_rope_kernel(const NormRopeArgs a) {
+__global__ void __launch_bounds__(256, 8) head_norm_rope_kernel(const NormRopeArgs a) {
   constexpr int CHUNKS = HD / 8;
-  constexpr int ROWS_PER_BLOCK = 256 / CHUNKS;
+  constexpr int ROWS_PER_PASS = 256 / CHUNKS;
   const int chunk = threadIdx.x % CHUNKS;
-  const unsigned row = blockIdx.x * ROWS_PER_BLOCK + threadIdx.x / CHUNKS;  // [b][s][h] order
   const unsigned heads = static_cast<unsigned>(a.t.heads);
-  if (row >= static_cast<unsigned>(a.batch) * a.seq * heads) return;
-  const unsigned h = row % heads;
-  const unsigned bs = row / heads;
-  const unsigned s = bs % static_cast<unsigned>(a.seq);
-  const unsigned b = bs / static_cast<unsigned>(a.seq);
-  const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(a.t.src) + s * a.t.src_strides[0] +
-                             h * a.t.src_strides[1] + b * a.t.src_strides[2];
+  const unsigned total = static_cast<unsigned>(a.batch) * a.seq * heads;
+  // rows in [b][s][h] order; kPackRows of them a thread, loads first (as pack_kernel)
+  const unsigned first = blockIdx.x * (kPackRows * ROWS_PER_PASS) + threadIdx.x / CHUNKS;
+  if (first >= total) return;
   const int d0 = chunk * 8;
-  float x[8];
-  unpack8(*reinterpret_cast<const uint4*>(src + d0), x);
-  norm_rope_row<HD>(x, d0, chunk, row_group_mask<CHUNKS>(), a.rope.token0 + s, a.t, a.rope);
-  __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(a.t.dst[0]) + s * a.out_strides[0] +
-                       h * a.out_strides[1] + b * a.out_strides[2] + d0;
-  *reinterpret_cast<uint4*>(dst) = pack8(x);
+  float x[kPackRows][8];
+  unsigned token[kPackRows];
+  __nv_bfloat16* dst[kPackRows];
+#pragma unroll
+  for (int k = 0; k < kPackRows; ++k) {
+    const unsigned row = first + k * ROWS_PER_PASS;
+    token[k] = 0;
+    dst[k] = nullptr;
+    if (row < total) {
+      const unsigned h = row % heads;
+      const unsigned bs = row / heads;
+      const unsigned s = bs % static_cast<unsigned>(a.seq);
+      const unsigned b = bs / static_cast<unsigned>(a.seq);
+      token[k] = s;
+      const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(a.t.src) +
+                                 s * a.t.src_strides[0] + h * a.t.src_strides[1] +
+                                 b * a.t.src_strides[2];
+      unpack8(*reinterpret_cast<const uint4*>(src + d0), x[k]);
+      dst[k] = static_cast<__nv_bfloat16*>(a.t.dst[0]) + s * a.out_strides[0] +
+               h * a.out_strides[1] + b * a.out_strides[2] + d0;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kPackRows; ++k) {
+    if (first + k * ROWS_PER_PASS >= total) break;
+    norm_rope_row<HD>(x[k], d0, chunk, row_group_mask<CHUNKS>(), a.rope.token0 + token[k], a.t,
+                      a.rope);
+    *reinterpret_cast<uint4*>(dst[k]) = pack8(x[k]);
+  }
 }
 
 int head_norm_rope(const void* x, void* out, int batch, int seq, int heads, int head_dim,
@@ -225,7 +244,7 @@ int head_norm_rope(const void* x, void* out, int batch, int seq, int heads, int 
   if (rope != nullptr) a.rope = *rope;
   a.seq = seq;
   a.batch = batch;
-  const int rows_per_block = 256 / (head_dim / 8);
+  const int rows_per_block = kPackRows * 256 / (head_dim / 8);
   const unsigned blocks = static_cast<unsigned>((rows + rows_per_block - 1) / rows_per_block);
   if (head_dim == 128)
     head_norm_rope_kernel<128><<<blocks, 256, 0, stream>>>(a);
