@@ -106,7 +106,7 @@ def peaks(fp8: bool = False, sustained: bool = False) -> tuple[float, float, str
 
 
 class NvmlSampler:
-    """SM clock and clock-event reasons read through NVML every 2 ms during the timed region
+    """SM clock and clock-event reasons read through NVML every 10 ms during the timed region
     (read-only queries; no setting is changed). Falls back to `ClockSampler` without NVML."""
 
     REASONS = (
@@ -138,7 +138,7 @@ class NvmlSampler:
                 self.samples.append((mhz, reasons))
             except n.NVMLError:
                 pass
-            time.sleep(0.002)
+            time.sleep(0.01)
 
     def __enter__(self):
         self.thread.start()
@@ -162,6 +162,19 @@ class NvmlSampler:
             "samples": len(self.samples),
             "source": "nvml",
         }
+
+
+class NullSampler:
+    """The other ranks' stand-in: no sampling."""
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        return None
+
+    def summary(self) -> None:
+        return None
 
 
 def clock_sampler(gpu: int):
@@ -378,7 +391,9 @@ def main() -> None:
     torch.cuda.synchronize()
 
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    sampler = clock_sampler(local_gpu_index(local))
+    # rank 0 samples its GPU's clocks (its line reports them); NVML queries from every rank's
+    # process would take the driver beside the ranks' own launches
+    sampler = clock_sampler(local_gpu_index(local)) if rank == 0 else NullSampler()
     with sampler:
         e0.record()
         for _ in range(args.steps):
@@ -391,14 +406,15 @@ def main() -> None:
     attn_ms = clock["attention_ms"] / max(1, clock["calls"])
     layout = ulysses.plan(rows, heads, hkv)
     my_flops = layer_flops(cfg, heads=layout.q_n[rank])
-    stats = torch.tensor([ms, attn_ms, clock["exposed_ms"] / max(1, clock["calls"])],
-                         dtype=torch.float64, device=device)
+    calls = max(1, clock["calls"])
+    stats = torch.tensor([ms, attn_ms, clock["exposed_ms"] / calls, clock["before_ms"] / calls,
+                          clock["after_ms"] / calls], dtype=torch.float64, device=device)
     achieved = torch.tensor([my_flops / (attn_ms * 1e-3) / 1e12 if attn_ms else 0.0],
                             dtype=torch.float64, device=device)
     if group is not None:
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
         dist.all_reduce(achieved, op=dist.ReduceOp.MIN)
-    ms_max, attn_max, exposed_max = stats.tolist()
+    ms_max, attn_max, exposed_max, before_max, after_max = stats.tolist()
 
     # ---- end to end through the public call, host buffers in and out every step
     e2e_ms = h2d = d2h = None
@@ -508,6 +524,10 @@ def main() -> None:
                 "attention_ms": round(attn_max, 4),
                 "exposed_ms": round(exposed_max, 4),
                 "exposed_frac": round(exposed_max / ms_max, 4) if ms_max else None,
+                # exposed before the attention (first stage, crossing, arrival flags) and after
+                # it (return flags, copy out), each the max over ranks
+                "before_attention_ms": round(before_max, 4),
+                "after_attention_ms": round(after_max, 4),
             },
             "clocks": sampler.summary(),
             "e2e": None if e2e_ms is None else {

@@ -917,7 +917,7 @@ static SplitPlan plan_split(long long tiles, int n_blocks, int sms, int head_dim
   if (tiles / sms >= kMaxWholeWaves) return best;
   const double unsplit = static_cast<double>((tiles + sms - 1) / sms) * (n_blocks + kUnitCost);
   // a clear gain only: a split costs workspace traffic the model leaves out
-  double best_time = 0.97 * unsplit;
+  double best_time = 0.95 * unsplit;
   const long long whole = tiles / sms;
   for (long long waves = whole; waves >= 0 && waves >= whole - 1; --waves) {
     const long long tail = tiles - waves * sms;

@@ -167,8 +167,12 @@ class _Clock:
 
     def __init__(self) -> None:
         self.pending: list[tuple] = []
-        self.totals = {"calls": 0, "exchange": 0.0, "attention": 0.0, "crossed": 0}
+        self.totals = self._zero()
         self.lock = threading.Lock()
+
+    @staticmethod
+    def _zero() -> dict:
+        return {"calls": 0, "exchange": 0.0, "attention": 0.0, "before": 0.0, "crossed": 0}
 
     @staticmethod
     def mark(on: Tensor):
@@ -197,18 +201,22 @@ class _Clock:
             self.totals["calls"] += 1
             self.totals["exchange"] += began.elapsed_time(ended)
             self.totals["attention"] += first.elapsed_time(last)
+            self.totals["before"] += began.elapsed_time(first)
             self.totals["crossed"] += crossed
 
     def take(self) -> dict:
         with self.lock:
             self._fold(wait=True)
-            t, self.totals = self.totals, {"calls": 0, "exchange": 0.0, "attention": 0.0, "crossed": 0}
+            t, self.totals = self.totals, self._zero()
         return {
             "calls": t["calls"],
             "crossed_gb": round(t["crossed"] / 1e9, 3),
             "exchange_ms": round(t["exchange"], 3),
             "attention_ms": round(t["attention"], 3),
             "exposed_ms": round(t["exchange"] - t["attention"], 3),
+            # exposed before the attention (first stage, crossing, arrival) and after it
+            "before_ms": round(t["before"], 3),
+            "after_ms": round(t["exchange"] - t["attention"] - t["before"], 3),
         }
 
 
