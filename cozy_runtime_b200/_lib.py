@@ -125,6 +125,7 @@ class Fp8Pack(Structure):
         ("batch", c_int),
         ("head_dim", c_int),
         ("row0", c_int),
+        ("head_turn", c_int),
     ]
 
 

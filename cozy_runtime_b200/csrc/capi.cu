@@ -105,7 +105,7 @@ const char* cozy_error_name(int code) {
   return cudaGetErrorName(static_cast<cudaError_t>(code));
 }
 
-int cozy_abi_version(void) { return 102; }
+int cozy_abi_version(void) { return 103; }
 
 }  // extern "C"
 

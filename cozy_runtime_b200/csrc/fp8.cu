@@ -57,9 +57,12 @@ __device__ __forceinline__ uint32_t e4m3x4(float a, float b, float c, float d) {
 __global__ void __launch_bounds__(256) fp8_pack_kernel(const CozyFp8Pack a) {
   const int tensor = blockIdx.z % 3;
   const int b = blockIdx.z / 3;
-  const int head = blockIdx.y;
   const CozyFp8Tensor& t = a.t[tensor];
-  if (head >= t.heads) return;
+  if (static_cast<int>(blockIdx.y) >= t.heads) return;
+  // heads from the launch's first head round (the grid's y extent is Q's head count; K/V
+  // start at the same fraction of theirs)
+  const int turn = static_cast<int>(static_cast<long long>(a.head_turn) * t.heads / a.t[0].heads);
+  const int head = (static_cast<int>(blockIdx.y) + turn) % t.heads;
   const int chunk = threadIdx.x & 15;
   const int row_in = threadIdx.x >> 4;
   const int d0 = chunk * 8;
@@ -194,6 +197,9 @@ int fp8_pack(const CozyFp8Pack* a, cudaStream_t stream) {
   }
   if (a->rows == 0) return cudaSuccess;
   if (a->row0 < 0) return cudaErrorInvalidValue;
+  if (a->head_turn < 0 || (a->t[0].heads > 0 && a->head_turn >= a->t[0].heads) ||
+      a->t[0].heads != heads)  // the grid walks Q's heads; K/V have as many or fewer
+    return cudaErrorInvalidValue;
   const int blocks = (a->row0 + a->rows + 63) / 64 - a->row0 / 64;
   dim3 grid(blocks, heads, a->batch * 3);
   fp8_pack_kernel<<<grid, 256, 0, stream>>>(*a);

@@ -83,6 +83,8 @@ class Fp8Step:
         pk = _lib.Fp8Pack()
         pk.world, pk.rows, pk.batch, pk.head_dim = lay.world, self.mine, self.batch, self.dim
         pk.row0 = lay.start(self.rank)
+        # start at this rank's own heads: the ranks then write to different peers at a time
+        pk.head_turn = lay.q_lo[self.rank] if lay.q_n[self.rank] else 0
         specs = [
             (self.query, lay.q_lo, lay.q_n, q_dst, qs_dst, None, None),
             (self.key, lay.kv_lo, lay.kv_n, k_dst, ks_dst, k_sum, None),

@@ -374,11 +374,22 @@ class RankStep:
         """Stage 1 into the given per-peer block addresses (local, or in the peers' own receive
         buffers over NVLink): one launch for Q, K and V."""
         lay, rotate = self.layout, self.rope is not None
+        # The kernel fills its destinations in list order (one grid row of CTAs per peer).
+        # Listed from this rank onwards, the ranks write to a different peer each at any moment
+        # (a permutation), instead of all into peer 0's memory first, then peer 1's, ... which
+        # would put every sender behind one receiver's NVLink ingress at a time.
+        order = [(self.rank + i) % lay.world for i in range(lay.world)]
+
+        def turned(seq):
+            return [seq[p] for p in order]
+
         pack(
             [
-                (self.query, q_dst, lay.q_lo, lay.q_n, rotate, self.norm_q),
-                (self.key, k_dst, lay.kv_lo, lay.kv_n, rotate, self.norm_k),
-                (self.value, v_dst, lay.kv_lo, lay.kv_n, False, None),
+                (self.query, turned(q_dst), turned(lay.q_lo), turned(lay.q_n), rotate,
+                 self.norm_q),
+                (self.key, turned(k_dst), turned(lay.kv_lo), turned(lay.kv_n), rotate,
+                 self.norm_k),
+                (self.value, turned(v_dst), turned(lay.kv_lo), turned(lay.kv_n), False, None),
             ],
             self.mine,
             self.rope,

@@ -192,6 +192,9 @@ typedef struct CozyFp8Pack {
   int world, rows, batch, head_dim;
   int row0; /* this rank's first row in the whole sequence: blocks are [64i, 64i + 64) of the
                whole sequence, clipped to this rank's rows */
+  int head_turn; /* the first head (of Q; K/V: the same fraction of theirs) the launch packs,
+                    then the next ones round: a rank starting at its own heads writes to a
+                    different peer than the other ranks at any moment */
 } CozyFp8Pack;
 
 COZY_API int cozy_fp8_stats(const CozyFp8Stats* stats, uintptr_t stream);

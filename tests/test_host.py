@@ -103,7 +103,7 @@ def test_library_exports_header_symbols():
     assert declared == set(_lib.SIGNATURES), "the ctypes binding covers the header"
     for name in declared:
         assert hasattr(lib, name), name
-    assert lib.cozy_abi_version() == 102
+    assert lib.cozy_abi_version() == 103
 
 
 def test_error_name_without_gpu():
