@@ -16,7 +16,6 @@ from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
 import statistics
 import subprocess
@@ -283,9 +282,8 @@ def cpu_baseline(cfg: dict, budget_s: float = 12.0) -> dict:
     q = torch.randn(1, rows, 1, d, generator=g).to(torch.bfloat16)
     k = torch.randn(1, s, 1, d, generator=g).to(torch.bfloat16)
     v = torch.randn(1, s, 1, d, generator=g).to(torch.bfloat16)
+    # (causal: a block of rows at the sequence's end sees every key, so the same cost)
     flops_call = 4.0 * rows * s * d
-    if cfg["causal"]:  # a causal block at the sequence's end sees every key: same cost
-        pass
     calls, start = 0, time.perf_counter()
     while True:
         oracle.attention_fp32(q, k, v)

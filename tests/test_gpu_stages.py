@@ -1,8 +1,6 @@
 """The stages on their own: the standalone RMSNorm + RoPE entry point against the reference's
 law (golden vectors of the reference's own checker), and the bounded peer wait running out."""
 
-import ctypes
-
 import pytest
 import torch
 
