@@ -247,6 +247,29 @@ __device__ __forceinline__ float2 exp2_poly2(float2 t) {
                      __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(r.y) << 23)));
 }
 
+// 2^f on [0, 1) by a degree-2 polynomial for the FP8 kernel, whose P is rounded to e4m3 (3
+// mantissa bits: steps of up to 6 %): fitted like the cubic above, max relative error 1.7e-3.
+// Its value at f = 0 is above 1, so the exponent add needs no margin; the clamp stays. Measured
+// on B200 (C4's per-GPU shape at degree 8, 5 heads × 75600): 2 pairs of 8 on it 1240 TFLOP/s
+// against 1226 with the cubic; 4, 6, 8 pairs of 8: 1163, 1004, 917 (the FMA pipe, not the MUFU,
+// limits there).
+constexpr float kExp2Q0 = 1.00171638f;
+constexpr float kExp2Q1 = 0.65764964f;
+constexpr float kExp2Q2 = 0.33720079f;
+
+__device__ __forceinline__ float2 exp2_poly2_quadratic(float2 t) {
+  const float2 magic = make_float2(12582912.0f, 12582912.0f);
+  t.x = fmaxf(t.x, -120.0f);
+  t.y = fmaxf(t.y, -120.0f);
+  const float2 r = __fadd2_rd(t, magic);
+  const float2 fl = __fadd2_rn(r, make_float2(-12582912.0f, -12582912.0f));
+  const float2 f = __ffma2_rn(fl, make_float2(-1.0f, -1.0f), t);
+  float2 p = __ffma2_rn(make_float2(kExp2Q2, kExp2Q2), f, make_float2(kExp2Q1, kExp2Q1));
+  p = __ffma2_rn(p, f, make_float2(kExp2Q0, kExp2Q0));
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(r.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(r.y) << 23)));
+}
+
 // 32 scores -> 32 probabilities 2^(s·scale - m) as 16 packed bf16 pairs, summed into `acc`.
 __device__ __forceinline__ void exp_chunk(const uint32_t (&r)[32], float2 scale2, float2 negm2,
                                           float2& acc, uint32_t (&pk)[16]) {
@@ -300,7 +323,7 @@ __device__ __forceinline__ void exp_chunk_fp8(const uint32_t (&r)[32], float2 sc
       const float2 sv = make_float2(__uint_as_float(r[k]), __uint_as_float(r[k + 1]));
       const float2 t = __ffma2_rn(sv, scale2, bias2);
       if (((2 * i + h) & 7) < kPolyPerEight) {
-        e[h] = exp2_poly2(t);
+        e[h] = exp2_poly2_quadratic(t);
       } else {
         e[h] = make_float2(ex2_approx(t.x), ex2_approx(t.y));
       }

@@ -109,6 +109,15 @@ def plan(rows: Sequence[int], heads: int, heads_kv: int) -> Plan:
     return Plan(tuple(rows), heads, heads_kv, tuple(q_lo), tuple(q_n), tuple(kv_lo), tuple(kv_n))
 
 
+def destination_order(rank: int, world: int) -> list[int]:
+    """The order a rank's first stage fills its peers' blocks in: from itself onwards. The
+    kernel fills destinations in list order (one grid row of CTAs per peer); so ordered, the
+    ranks write to a different peer each at any moment (a permutation), instead of all into peer
+    0's memory first, then peer 1's, which would put every sender behind one receiver's NVLink
+    ingress at a time."""
+    return [(rank + i) % world for i in range(world)]
+
+
 def tensor_split_rows(total: int, world: int) -> list[int]:
     """`torch.tensor_split` row counts (cp.py:166-174)."""
     base, extra = divmod(total, world)
@@ -374,11 +383,7 @@ class RankStep:
         """Stage 1 into the given per-peer block addresses (local, or in the peers' own receive
         buffers over NVLink): one launch for Q, K and V."""
         lay, rotate = self.layout, self.rope is not None
-        # The kernel fills its destinations in list order (one grid row of CTAs per peer).
-        # Listed from this rank onwards, the ranks write to a different peer each at any moment
-        # (a permutation), instead of all into peer 0's memory first, then peer 1's, ... which
-        # would put every sender behind one receiver's NVLink ingress at a time.
-        order = [(self.rank + i) % lay.world for i in range(lay.world)]
+        order = destination_order(self.rank, lay.world)
 
         def turned(seq):
             return [seq[p] for p in order]

@@ -137,3 +137,52 @@ def test_exchange_refuses_cpu():
         ulysses.exchange(x, x, x, None, None, narrow=True)
     with pytest.raises(ValueError):
         ulysses.exchange(x, x, x, None, None)
+
+
+def test_destination_order_is_a_permutation_at_every_step():
+    """At every position of the first stage's destination lists the ranks target distinct
+    peers, and each rank's list covers every peer once."""
+    from cozy_runtime_b200 import ulysses
+
+    for world in (1, 2, 3, 4, 7, 8):
+        orders = [ulysses.destination_order(r, world) for r in range(world)]
+        for r in range(world):
+            assert sorted(orders[r]) == list(range(world)) and orders[r][0] == r
+        for i in range(world):
+            assert sorted(o[i] for o in orders) == list(range(world))
+
+
+def test_narrow_block_sizes_cover_the_exchange():
+    """The int8 wire's per-peer blocks add up to the whole exchange in both directions: what
+    every rank sends for Q equals what the rank holding those heads receives, and the return
+    blocks of every source fill each rank's output rows of every head."""
+    from cozy_runtime_b200 import narrow, ulysses
+
+    batch, dim = 2, 64
+    for total, world, heads, hkv in ((100, 3, 5, 5), (37, 8, 16, 4), (50, 4, 6, 2)):
+        rows = ulysses.tensor_split_rows(total, world)
+        lay = ulysses.plan(rows, heads, hkv)
+        steps = []
+        for r in range(world):
+            q = torch.empty(batch, rows[r], heads, dim, dtype=torch.bfloat16)
+            kv = torch.empty(batch, rows[r], hkv, dim, dtype=torch.bfloat16)
+            steps.append(narrow.NarrowStep(q, kv, kv, lay, r))
+        for p in range(world):
+            got_q = sum(st.first_block(p, "q") for st in steps)
+            assert got_q == total * batch * lay.q_n[p] * dim
+            got_kv = sum(st.first_block(p, "kv") for st in steps)
+            assert got_kv == total * batch * lay.kv_n[p] * dim
+        for r, st in enumerate(steps):
+            # a source's return block to owner r is that owner's landing block from the source
+            for s in range(world):
+                assert steps[s].return_block(r) == st.landing_block(s)
+            assert sum(st.landing_block(s) for s in range(world)) == rows[r] * batch * heads * dim
+
+
+def test_scale_pointer_of_a_block():
+    from cozy_runtime_b200 import narrow
+
+    codes, scales = 1 << 20, 1 << 30
+    assert narrow.scale_ptr(codes, scales, 0, 128) == (codes, scales)
+    # 3 rows of 128 codes in: 3 bf16 scales in
+    assert narrow.scale_ptr(codes, scales, 3 * 128, 128) == (codes + 384, scales + 6)
