@@ -105,10 +105,11 @@ def peaks(fp8: bool = False, sustained: bool = False) -> tuple[float, float, str
 
 
 class NvmlSampler:
-    """SM clock and clock-event reasons read through NVML every 10 ms during the timed region, by
-    a child process that streams them back over a pipe (read-only queries; no setting is
-    changed): its driver calls stay out of this process, whose launches the timed steps are.
-    Falls back to `ClockSampler` without NVML."""
+    """SM clock and clock-event reasons read through NVML every 10 ms during the timed region,
+    by a thread of rank 0 (read-only queries; no setting is changed). Falls back to
+    `ClockSampler` without NVML. Measured at degree 2: sampling from a child process instead
+    cost ~3 ms a step (8.9 against 6.0 ms); sampling from every rank's process at degree 8,
+    ~0.4 ms."""
 
     REASONS = (
         ("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
@@ -116,58 +117,38 @@ class NvmlSampler:
         ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
         ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"),
     )
-    SCRIPT = (
-        "import sys, time, pynvml\n"
-        "pynvml.nvmlInit()\n"
-        "h = pynvml.nvmlDeviceGetHandleByIndex(int(sys.argv[1]))\n"
-        "print(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM), flush=True)\n"
-        "while True:\n"
-        "    try:\n"
-        "        print(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),\n"
-        "              pynvml.nvmlDeviceGetCurrentClocksEventReasons(h), flush=True)\n"
-        "    except pynvml.NVMLError:\n"
-        "        pass\n"
-        "    time.sleep(0.01)\n"
-    )
 
     def __init__(self, gpu: int) -> None:
-        import pynvml
-
-        self.nvml = pynvml  # absent NVML fails here: the caller takes ClockSampler
-        self.gpu = gpu
-        self.proc = None
-        self.reader = None
-        self.max_mhz = None
-        self.samples: list[tuple[int, int]] = []
-
-    def _read(self) -> None:
-        for line in self.proc.stdout:
-            parts = line.split()
-            if len(parts) == 2:
-                self.samples.append((int(parts[0]), int(parts[1])))
-
-    def __enter__(self):
-        import subprocess
-        import sys
         import threading
 
-        self.proc = subprocess.Popen([sys.executable, "-c", self.SCRIPT, str(self.gpu)],
-                                     stdout=subprocess.PIPE, text=True)
-        first = self.proc.stdout.readline()  # NVML is up before the timed region starts
-        self.max_mhz = int(first) if first.strip() else None
-        self.reader = threading.Thread(target=self._read, daemon=True)
-        self.reader.start()
+        import pynvml
+
+        self.nvml = pynvml
+        pynvml.nvmlInit()
+        self.handle = pynvml.nvmlDeviceGetHandleByIndex(gpu)
+        self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+        self.samples: list[tuple[int, int]] = []
+        self.stop = threading.Event()
+        self.thread = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self) -> None:
+        n = self.nvml
+        while not self.stop.is_set():
+            try:
+                mhz = n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM)
+                reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                self.samples.append((mhz, reasons))
+            except n.NVMLError:
+                pass
+            time.sleep(0.01)
+
+    def __enter__(self):
+        self.thread.start()
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()  # our own child, by its handle
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:  # noqa: BLE001
-                self.proc.kill()
-        if self.reader is not None:
-            self.reader.join(timeout=5)
+        self.stop.set()
+        self.thread.join(timeout=5)
 
     def summary(self) -> dict | None:
         if not self.samples:
@@ -181,7 +162,7 @@ class NvmlSampler:
             "sm_max_mhz": self.max_mhz,
             "reasons": reasons,
             "samples": len(self.samples),
-            "source": "nvml (child process)",
+            "source": "nvml",
         }
 
 
