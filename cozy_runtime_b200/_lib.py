@@ -182,6 +182,10 @@ SIGNATURES = {
         [c_int, c_int, c_int, c_int, c_int, c_int, POINTER(c_longlong), POINTER(c_int)],
         c_int,
     ),
+    "cozy_attention_split_plan_for": (
+        [c_int, c_int, c_int, c_int, c_int, c_int, c_int, POINTER(c_longlong), POINTER(c_int)],
+        c_int,
+    ),
     "cozy_key_sum": (
         [c_void_p, POINTER(c_longlong), c_int, c_int, c_int, c_int, c_void_p, c_uint64], c_int,
     ),

@@ -1204,21 +1204,28 @@ int attention_forward(const void* q, const void* k, const void* v, void* out, in
 // The split plan attention_forward takes on the current device for a non-FP8 call of this shape
 // (FP8 calls take the same plan): `whole` tiles of 256 query rows run in one CTA each, the
 // remaining tiles in `parts` CTAs each (parts = 1: nothing is split).
-int attention_split_plan(int batch, int seq_q, int seq_k, int heads_q, int head_dim, int causal,
-                         long long* whole, int* parts) {
+// As attention_split_plan, for a GPU of `sms` SMs (host arithmetic only: no device is needed).
+int attention_split_plan_for(int batch, int seq_q, int seq_k, int heads_q, int head_dim,
+                             int causal, int sms, long long* whole, int* parts) {
   if (whole == nullptr || parts == nullptr || batch <= 0 || seq_q <= 0 || seq_k <= 0 ||
-      heads_q <= 0 || (head_dim != 64 && head_dim != 128))
+      heads_q <= 0 || sms <= 0 || (head_dim != 64 && head_dim != 128))
     return cudaErrorInvalidValue;
-  int device = 0;
-  cudaError_t e = cudaGetDevice(&device);
-  if (e != cudaSuccess) return e;
   const long long tiles =
       static_cast<long long>(batch) * heads_q * ((seq_q + kQTiles * kBlockM - 1) / (kQTiles * kBlockM));
   SplitPlan plan = {tiles, 1, 0};
-  if (!causal) plan = plan_split(tiles, (seq_k + kBlockN - 1) / kBlockN, sm_count(device), head_dim);
+  if (!causal) plan = plan_split(tiles, (seq_k + kBlockN - 1) / kBlockN, sms, head_dim);
   *whole = plan.n_full;
   *parts = plan.parts;
   return cudaSuccess;
+}
+
+int attention_split_plan(int batch, int seq_q, int seq_k, int heads_q, int head_dim, int causal,
+                         long long* whole, int* parts) {
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return e;
+  return attention_split_plan_for(batch, seq_q, seq_k, heads_q, head_dim, causal,
+                                  sm_count(device), whole, parts);
 }
 
 // As attention_forward, without the split of the last wave (which needs a workspace this

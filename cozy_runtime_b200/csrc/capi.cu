@@ -15,6 +15,8 @@ int attention_forward(const void* q, const void* k, const void* v, void* out, in
                       float scale, int* status, cudaStream_t stream);
 int attention_split_plan(int batch, int seq_q, int seq_k, int heads_q, int head_dim, int causal,
                          long long* whole, int* parts);
+int attention_split_plan_for(int batch, int seq_q, int seq_k, int heads_q, int head_dim,
+                             int causal, int sms, long long* whole, int* parts);
 int key_sum(const void* key, const long long* strides, int rows, int batch, int heads,
             int head_dim, float* sum, cudaStream_t stream);
 int narrow_shift(const float* sum, long long count, int batch, int heads, int head_dim,
@@ -77,6 +79,12 @@ int cozy_narrow_widen(const CozyWidenSource* sources, int count, int batch, int 
   return cozy::narrow_widen(sources, count, batch, head_dim, out, out_strides, as_stream(stream));
 }
 
+int cozy_attention_split_plan_for(int batch, int seq_q, int seq_k, int heads_q, int head_dim,
+                                  int causal, int sms, long long* whole_tiles, int* parts) {
+  return cozy::attention_split_plan_for(batch, seq_q, seq_k, heads_q, head_dim, causal, sms,
+                                        whole_tiles, parts);
+}
+
 int cozy_ulysses_pack(const CozyPackTensor* tensors, int count, int world, int rows, int batch,
                       int head_dim, const CozyRope* rope, uintptr_t stream) {
   if (!tensors) return cudaErrorInvalidValue;
@@ -105,7 +113,7 @@ const char* cozy_error_name(int code) {
   return cudaGetErrorName(static_cast<cudaError_t>(code));
 }
 
-int cozy_abi_version(void) { return 103; }
+int cozy_abi_version(void) { return 104; }
 
 }  // extern "C"
 

@@ -78,6 +78,11 @@ COZY_API int cozy_attention_fwd(const void* q, const void* k, const void* v, voi
 COZY_API int cozy_attention_split_plan(int batch, int seq_q, int seq_k, int heads_q, int head_dim,
                                        int causal, long long* whole_tiles, int* parts);
 
+/* The same plan for a GPU of `sms` SMs: host arithmetic only, no device needed. */
+COZY_API int cozy_attention_split_plan_for(int batch, int seq_q, int seq_k, int heads_q,
+                                           int head_dim, int causal, int sms,
+                                           long long* whole_tiles, int* parts);
+
 /* One tensor of the seq->head exchange's first stage (Q, K or V): this rank's rows
  * [batch, rows, heads, head_dim] (`src`, element strides {seq, head, batch}), optionally
  * RMS-normalised per head and rotated, written as the block each peer receives:

@@ -103,7 +103,7 @@ def test_library_exports_header_symbols():
     assert declared == set(_lib.SIGNATURES), "the ctypes binding covers the header"
     for name in declared:
         assert hasattr(lib, name), name
-    assert lib.cozy_abi_version() == 103
+    assert lib.cozy_abi_version() == 104
 
 
 def test_error_name_without_gpu():
@@ -186,3 +186,41 @@ def test_scale_pointer_of_a_block():
     assert narrow.scale_ptr(codes, scales, 0, 128) == (codes, scales)
     # 3 rows of 128 codes in: 3 bf16 scales in
     assert narrow.scale_ptr(codes, scales, 3 * 128, 128) == (codes + 384, scales + 6)
+
+
+def _plan(batch, seq, heads, causal=False, sms=148, dim=128):
+    from cozy_runtime_b200 import _lib
+
+    whole, parts = ctypes.c_longlong(), ctypes.c_int()
+    code = _lib.load().cozy_attention_split_plan_for(
+        batch, seq, seq, heads, dim, int(causal), sms, ctypes.byref(whole), ctypes.byref(parts))
+    assert code == 0
+    return whole.value, parts.value
+
+
+def test_split_plan_for_the_benchmark_shapes():
+    """The attention's schedule on 148 SMs (host arithmetic, no GPU): C2 splits its last
+    partial wave at degrees 4 and 8 (5.27 and 2.64 waves), not at 1 (21 waves: the SMs' drift
+    absorbs it) nor at 2 (a predicted 3 %, under the 5 % bar); causal calls never split."""
+    c2 = 33272
+    assert _plan(1, c2, 24) == (3120, 1)
+    assert _plan(1, c2, 12) == (1560, 1)
+    assert _plan(1, c2, 6) == (740, 7)
+    assert _plan(1, c2, 3) == (296, 3)
+    assert _plan(1, 131071, 32, causal=True) == (16384, 1)
+    whole, parts = _plan(2, 4608, 6)  # C3 at degree 4: one whole wave, the rest split
+    assert whole == 148 and parts > 1
+    whole, parts = _plan(1, 4000, 2)  # fewer tiles than SMs: all split
+    assert whole == 0 and parts > 1
+    assert _plan(1, 256 * 148, 1)[1] == 1  # exactly one wave
+
+
+def test_split_plan_refuses_bad_arguments():
+    from cozy_runtime_b200 import _lib
+
+    whole, parts = ctypes.c_longlong(), ctypes.c_int()
+    lib = _lib.load()
+    assert lib.cozy_attention_split_plan_for(1, 100, 100, 2, 96, 0, 148, ctypes.byref(whole),
+                                             ctypes.byref(parts)) != 0
+    assert lib.cozy_attention_split_plan_for(1, 100, 100, 2, 128, 0, 0, ctypes.byref(whole),
+                                             ctypes.byref(parts)) != 0
