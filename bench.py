@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Benchmark of the Ulysses context-parallel attention layer (BASELINE.json's metric).
+"""Benchmark of the Ulysses context-parallel attention layer (the path's headline metric).
 
 A step is one layer: the fused first stage (RoPE/RMSNorm + transposition into per-peer blocks),
 the seq->head crossing of Q/K/V (NCCL all-to-all; none at degree 1), the sm_100a attention

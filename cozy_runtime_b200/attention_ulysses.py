@@ -6,7 +6,7 @@ kernel, `function(backend, local)` (:184) makes its Diffusers-style backend call
 (:233-272) through the torch side `serve`d at import (:168). `CANDIDATE` is the selection row a
 B200 (`tcgen05` family) attention table names for this kernel (`internal/attention.py:117-236`).
 
-Relative to the reference, the B200 row serves what BASELINE's configurations need under
+Relative to the reference, the B200 row serves what the benchmark configurations need under
 Ulysses: causal attention (bottom-right) and grouped-query K/V heads, both of which the
 reference's wrapper refuses (:259-262) but its exchange does not depend on.
 """

@@ -4,7 +4,7 @@
 //
 // Both move 16-byte vectors: a row of head_dim bf16 is head_dim/8 consecutive threads, so a
 // warp reads and writes whole 128-byte lines. These kernels are bounded by HBM (or, when the
-// destination is a peer's buffer, by NVLink); see the roofline notes in DESIGN.md.
+// destination is a peer's buffer, by NVLink).
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>

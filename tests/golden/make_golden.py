@@ -1,7 +1,7 @@
 """Generate the golden vectors under tests/golden/ by running the REFERENCE's own code.
 
 Test infrastructure only: this script imports cozy-runtime from a local checkout of the
-reference (default `/root/reference/src`, or `$COZY_REFERENCE_SRC`) and is run by hand in a
+reference (`$COZY_REFERENCE_SRC`, else the checkout's default location below) and is run by hand in a
 container that has it. Nothing else in this repository imports it; the GPU box never runs it.
 
 What it records, each as an `.npz` in this directory:

@@ -1,6 +1,6 @@
 """Parity of the sm_100a attention kernel (cozy_attention_fwd, through the C ABI) with the oracle.
 
-Tolerance (BASELINE's bf16 bar): max-abs ≤ 2e-2 and mean-abs ≤ 2e-3 against the fp32 oracle on
+Tolerance (the path's bf16 bar): max-abs ≤ 2e-2 and mean-abs ≤ 2e-3 against the fp32 oracle on
 the same bf16 inputs.
 """
 

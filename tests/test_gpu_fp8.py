@@ -6,7 +6,7 @@ scatters rows to their owners. Checked two ways: against the oracle's FP8 law (t
 in fp32 arithmetic; per-head cosine ≥ 0.999 and mean-abs ≤ 2.5e-3 — the kernel forms P against a
 running max up to 2^0.5 stale, the law against the exact one, so single e4m3 codes of P can
 differ by a step and a max-abs bar would measure that, not the kernel) and against exact fp32
-attention on the unquantised inputs with BASELINE's FP8 bar: cosine similarity ≥ 0.995 per head.
+attention on the unquantised inputs with the path's FP8 bar: cosine similarity ≥ 0.995 per head.
 """
 
 import numpy as np

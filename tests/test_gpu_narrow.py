@@ -7,7 +7,7 @@ bf16 step or a code by one (at most 0.5 % of codes, none by more than one, here)
 
 Exchange: W ranks run as W `NarrowStep`s on one GPU, each writing into every rank's receive and
 landing blocks at the addresses the NVLink transport would give it; compared with the
-reference's own narrow exchange (golden fixtures: it ran torch SDPA in bf16) under BASELINE's bf16
+reference's own narrow exchange (golden fixtures: it ran torch SDPA in bf16) under the path's bf16
 bar (max-abs ≤ 2e-2, mean-abs ≤ 2e-3), and at larger sizes with the oracle's narrow exchange
 around fp32 attention.
 """

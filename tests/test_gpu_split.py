@@ -1,7 +1,7 @@
 """The split of the last wave: tiles past the last whole wave of one CTA per SM run as several
 CTAs over shares of the keys, and the last one to finish merges their rows.
 
-Checked against the fp32 oracle at sizes it finishes in seconds (BASELINE's bf16 bar: max-abs
+Checked against the fp32 oracle at sizes it finishes in seconds (the path's bf16 bar: max-abs
 ≤ 2e-2, mean-abs ≤ 2e-3), and at the full C2 degree-8 shape (3 heads × 33272 tokens, whose 390
 tiles fill 2.64 waves of 148 SMs) against an fp32 torch reference on the GPU for rows of split
 and of whole tiles, plus split against unsplit (COZY_ATTENTION_SPLIT=0) output: relative L2

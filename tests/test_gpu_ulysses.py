@@ -3,7 +3,7 @@
 W ranks run as W `RankStep`s in one process; the crossings between them are device copies of
 exactly the blocks NCCL's all-to-all moves (the same split sizes and offsets `exchange` hands it).
 The assembled output is compared with the reference's own exchange output (golden vectors from
-`tests/golden/make_golden.py`) at BASELINE's bf16 tolerance: max-abs ≤ 2e-2, mean-abs ≤ 2e-3.
+`tests/golden/make_golden.py`) at the path's bf16 tolerance: max-abs ≤ 2e-2, mean-abs ≤ 2e-3.
 """
 
 import numpy as np
