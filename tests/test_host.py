@@ -224,3 +224,41 @@ def test_split_plan_refuses_bad_arguments():
                                              ctypes.byref(parts)) != 0
     assert lib.cozy_attention_split_plan_for(1, 100, 100, 2, 128, 0, 0, ctypes.byref(whole),
                                              ctypes.byref(parts)) != 0
+
+
+def test_backend_call_refusals_without_gpu():
+    """The backend call's refusals, which come before any device work, as the reference's
+    (attention_ulysses.py:246-262): log-sum-exp, masks under Ulysses, a kernel that is not
+    head-local, ring attention."""
+    from types import SimpleNamespace
+
+    from cozy_runtime_b200 import attention_ulysses as au
+
+    x = torch.zeros(1, 4, 2, 64, dtype=torch.bfloat16)
+    call = au._dispatch("cozy_b200_test", au.COZY_B200)
+    with pytest.raises(ValueError, match="log-sum-exp"):
+        call(x, x, x, return_lse=True)
+    config = SimpleNamespace(context_parallel_config=SimpleNamespace(ring_degree=1, group=None))
+    with pytest.raises(ValueError, match="unmasked"):
+        call(x, x, x, attn_mask=torch.zeros(4, 4, dtype=torch.bool), _parallel_config=config)
+    # grouped-query heads under Ulysses need enable_gqa
+    kv = torch.zeros(1, 4, 1, 64, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        call(x, kv, kv, _parallel_config=config)
+    reducing = au.Local(forward=lambda *a, **k: None, impl=lambda *a: "", head_local=False)
+    with pytest.raises(ValueError, match="head"):
+        au._dispatch("reducing_test", reducing)(x, x, x, _parallel_config=config)
+    ring = SimpleNamespace(context_parallel_config=SimpleNamespace(ring_degree=2))
+    with pytest.raises(ValueError, match="ring"):
+        au.group(ring)
+    with pytest.raises(ValueError, match="not initialized"):
+        au.group(SimpleNamespace(context_parallel_config=SimpleNamespace(ring_degree=1)))
+
+
+def test_candidate_row_matches_the_kernel():
+    from cozy_runtime_b200 import attention_ulysses as au
+
+    row = au.CANDIDATE
+    assert row.families == frozenset({"tcgen05"}) and row.dtypes == ("bfloat16",)
+    assert row.head_dims == (64, 128) and row.causal and row.gqa and not row.masks
+    assert row.local is au.COZY_B200 and row.local.head_local
