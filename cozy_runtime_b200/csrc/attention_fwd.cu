@@ -962,25 +962,27 @@ static SplitPlan plan_split(long long tiles, int n_blocks, int sms, int head_dim
 }
 
 // Split workspace, one per (device, stream): launches on one stream run in order, so they can
-// share it; launches on different streams may overlap and must not. Grows, never shrinks; not
-// allocated while the stream is being captured (the launch then runs unsplit).
+// share it; launches on different streams may overlap and must not. Grows, never shrinks.
+// A launch made while its stream is being captured into a graph never uses it (it runs
+// unsplit): a graph keeps the address it was captured with and may be replayed on any stream,
+// beside eager launches that share this workspace or after it has grown and been freed.
 struct Workspace {
   void* ptr = nullptr;
   size_t bytes = 0;
 };
 
 static void* split_workspace(int device, cudaStream_t stream, size_t bytes) {
-  static std::mutex mutex;
-  static std::map<std::pair<int, uintptr_t>, Workspace> spaces;
-  std::lock_guard<std::mutex> lock(mutex);
-  Workspace& w = spaces[{device, reinterpret_cast<uintptr_t>(stream)}];
-  if (w.bytes >= bytes) return w.ptr;
   cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
   if (cudaStreamIsCapturing(stream, &capture) != cudaSuccess ||
       capture != cudaStreamCaptureStatusNone) {
     cudaGetLastError();
     return nullptr;
   }
+  static std::mutex mutex;
+  static std::map<std::pair<int, uintptr_t>, Workspace> spaces;
+  std::lock_guard<std::mutex> lock(mutex);
+  Workspace& w = spaces[{device, reinterpret_cast<uintptr_t>(stream)}];
+  if (w.bytes >= bytes) return w.ptr;
   if (w.ptr != nullptr) {
     // earlier launches on this stream may still read the old buffer
     if (cudaStreamSynchronize(stream) != cudaSuccess || cudaFree(w.ptr) != cudaSuccess) {

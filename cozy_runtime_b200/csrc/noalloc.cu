@@ -68,6 +68,21 @@ extern "C" int cozy_rope_attention_fwd_noalloc(
     return cudaErrorInvalidValue;
   if (batch <= 0 || seq <= 0 || heads_q <= 0 || heads_kv <= 0 || head_dim <= 0)
     return cudaErrorInvalidValue;
+  if (head_dim != 64 && head_dim != 128) return cudaErrorNotSupported;
+  // Everything the attention checks is checked here first, so a refused call launches nothing
+  // and leaves the shared array as the last call left it.
+  if (heads_q % heads_kv != 0 || batch > 65535 || heads_q > 65535) return cudaErrorInvalidValue;
+  const void* aligned[4] = {q, k, v, out};
+  for (const void* ptr : aligned)
+    if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0) return cudaErrorInvalidValue;
+  const long long* given[4] = {q_strides, k_strides, v_strides, o_strides};
+  for (const long long* st : given)
+    for (int i = 0; i < 3; ++i)
+      if (st[i] <= 0 || st[i] % 8 != 0) return cudaErrorInvalidValue;
+  if (rope->cos == nullptr || rope->sin == nullptr || rope->rotary < 0 ||
+      rope->rotary > head_dim || rope->rotary % 2 != 0)
+    return cudaErrorInvalidValue;
+  if (!rope->interleaved && rope->rotary % 16 != 0) return cudaErrorNotSupported;
   // Rotated Q and K, [seq][batch][heads][head_dim] bf16 each, must fit the array.
   const unsigned long long q_bytes = 2ull * seq * batch * heads_q * head_dim;
   const unsigned long long k_bytes = 2ull * seq * batch * heads_kv * head_dim;

@@ -2,7 +2,10 @@
  *
  * Conventions (those of the reference's native modules, kernels/csrc/gemm.cpp:1-7 and
  * kernels/csrc/fa3.cpp:1-9 in cozy-runtime): arguments are raw device pointers, sizes, element
- * strides and a cudaStream_t passed as uintptr_t; the caller allocates every buffer; each call
+ * strides and a cudaStream_t passed as uintptr_t; the caller allocates every buffer it passes
+ * (the exceptions, each stated at its entry point: the attention's split workspace, which the
+ * library allocates once per (device, stream) outside stream capture and keeps, and the buffers
+ * a CozyGroup maps when it is formed or reserved, never inside a layer call); each call
  * returns a cudaError_t value as an int (0 = queued on the stream; cudaErrorNotSupported = 801
  * when no kernel serves the shape; cudaErrorInvalidValue = 1 for bad arguments) and never
  * throws. `cozy_error_name` names a code. Kernels that wait report through a caller-owned
@@ -72,9 +75,10 @@ COZY_API int cozy_attention_fwd(const void* q, const void* k, const void* v, voi
  * `*whole_tiles` tiles, each tile runs as `*parts` CTAs over consecutive shares of the keys,
  * whose partial rows the last CTA to finish merges (an atomic count, no waiting). `*parts` = 1
  * when nothing is split (always for causal calls). The split needs a workspace the library
- * allocates once per (device, stream) and keeps; launches on one stream share it in order, and
- * launches made while the stream is being captured into a graph run unsplit unless it exists.
- * COZY_ATTENTION_SPLIT=0 in the environment turns the split off. */
+ * allocates (cudaMalloc) at the first eager launch on a (device, stream) that needs it, and keeps
+ * (it grows, never shrinks); launches on one stream share it in order. Launches made while the
+ * stream is being captured into a graph never use it: they run unsplit, so a graph holds no
+ * address of it. COZY_ATTENTION_SPLIT=0 in the environment turns the split off. */
 COZY_API int cozy_attention_split_plan(int batch, int seq_q, int seq_k, int heads_q, int head_dim,
                                        int causal, long long* whole_tiles, int* parts);
 

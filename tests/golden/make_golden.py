@@ -1,8 +1,8 @@
 """Generate the golden vectors under tests/golden/ by running the REFERENCE's own code.
 
 Test infrastructure only: this script imports cozy-runtime from a local checkout of the
-reference (`$COZY_REFERENCE_SRC`, else the checkout's default location below) and is run by hand in a
-container that has it. Nothing else in this repository imports it; the GPU box never runs it.
+reference named by `$COZY_REFERENCE_SRC` (the checkout's `src` directory; required) and is run
+by hand in a container that has it. Nothing else in this repository imports it; the GPU box never runs it.
 
 What it records, each as an `.npz` in this directory:
 
@@ -24,7 +24,7 @@ What it records, each as an `.npz` in this directory:
 * ``narrow_*.npz``: the reference's exchange with `narrow=True` (Q, K less its turned mean, V
   and the output crossing as int8), bf16 inputs and `sdpa` in bf16, over gloo as above.
 
-Run:  python tests/golden/make_golden.py [ulysses] [rope] [fp8] [turn] [narrow]  (default: all)
+Run:  COZY_REFERENCE_SRC=<checkout>/src python tests/golden/make_golden.py [ulysses] [rope] [fp8] [turn] [narrow]  (default: all)
 Third-party pins the reference declares but this container lacks (`tensorfs` 0.27.0,
 `diffusers` 0.40.0) are replaced by import stubs: neither is on the computed path.
 """
@@ -43,7 +43,7 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-REFERENCE_SRC = os.environ.get("COZY_REFERENCE_SRC", "/root/reference/src")
+REFERENCE_SRC = os.environ.get("COZY_REFERENCE_SRC", "")
 
 
 class _Stub(importlib.abc.MetaPathFinder, importlib.abc.Loader):
@@ -69,6 +69,8 @@ class _Stub(importlib.abc.MetaPathFinder, importlib.abc.Loader):
 def import_reference() -> None:
     if any(isinstance(f, _Stub) for f in sys.meta_path):
         return
+    if not REFERENCE_SRC or not Path(REFERENCE_SRC, "cozy_runtime").is_dir():
+        raise SystemExit("set COZY_REFERENCE_SRC to the reference checkout's src directory")
     sys.meta_path.insert(0, _Stub())
     meta = tempfile.mkdtemp(prefix="cozy-dist-")
     info = Path(meta, "cozy_runtime-0.0.0.dist-info")

@@ -141,3 +141,38 @@ def test_split_fp8():
     assert (got - law).abs().mean().item() <= 2.5e-3
     assert _cosine_per_head(got, law).min().item() >= 0.999
     assert _cosine_per_head(got, oracle.attention_fp32(q, k, v)).min().item() >= 0.995
+
+
+def test_captured_launch_never_uses_the_split_workspace():
+    """A launch captured into a CUDA graph runs unsplit, so the graph holds no workspace
+    address: growing (freeing and reallocating) the stream's workspace with a larger eager call
+    after the capture, then replaying the graph, still gives the unsplit result bit for bit."""
+    from cozy_runtime_b200 import attention
+
+    batch, sq, hq, dim = 1, 4000, 2, 128
+    assert attention.split_plan(batch, sq, sq, hq, dim, False)[1] > 1
+    g = torch.Generator().manual_seed(31)
+    q, k, v = (_randn((batch, sq, hq, dim), g).cuda() for _ in range(3))
+    attention.status_word(q.device)
+    want = _unsplit(lambda: attention.forward(q, k, v))
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        attention.forward(q, k, v)  # eager on this stream: its workspace exists before capture
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            captured = attention.forward(q, k, v)
+        # a larger split call on the capture stream grows its workspace
+        big = 3 * 130 * 256
+        g2 = torch.Generator(device="cuda").manual_seed(5)
+        qb, kb, vb = (torch.randn(1, big // 3, 3, dim, generator=g2, device="cuda")
+                      .to(torch.bfloat16) for _ in range(3))
+        assert attention.split_plan(1, big // 3, big // 3, 3, dim, False)[1] > 1
+        attention.forward(qb, kb, vb)
+        captured.zero_()
+        graph.replay()
+    torch.cuda.synchronize()
+    attention.check_status(q.device)
+    assert torch.equal(captured, want)
+    _check(captured, oracle.attention_fp32(q.cpu(), k.cpu(), v.cpu()))

@@ -6,7 +6,8 @@ latency-bound host thread): it keeps the rotated Q and K in a static device arra
 buffer. Its output must match the ordinary entry points — the first stage `cozy_ulysses_pack`
 into an allocated buffer followed by `cozy_attention_fwd`, which `ulysses.exchange` runs at
 degree 1 — at the bf16 tolerance the other GPU tests use (max-abs 2e-2, mean-abs 2e-3), on two
-calls in a row (the second call reuses the array the first one left behind).
+calls in a row (the second call reuses the array the first one left behind), and against the CPU
+oracle's RMSNorm/RoPE and attention laws on the same inputs.
 
 This file is collected last so a failure here never hides the rest of the suite.
 """
@@ -16,6 +17,8 @@ import math
 
 import pytest
 import torch
+
+import oracle
 
 pytestmark = pytest.mark.gpu
 
@@ -77,6 +80,17 @@ def test_noalloc_matches_ordinary_path(batch, seq, hq, hkv, dim, causal, normali
         err = (got.float() - want.float()).abs()
         assert err.max().item() <= MAX_ABS, f"max-abs {err.max().item():.3e}"
         assert err.mean().item() <= MEAN_ABS, f"mean-abs {err.mean().item():.3e}"
+    # and on its own against the CPU oracle's law: RMSNorm/RoPE, then fp32 attention
+    cos, sin = spec.cos.cpu(), spec.sin.cpu()
+    tables = cos.reshape(-1, spec.stride_token), sin.reshape(-1, spec.stride_token)
+    rot = [oracle.head_norm_rope(t.float().cpu(), *tables, rotary=spec.rotary,
+                                 interleaved=spec.interleaved, normalize=normalize,
+                                 stride_channel=spec.stride_channel).to(torch.bfloat16)
+           for t in (q, k)]
+    law = oracle.attention_fp32(rot[0], rot[1], v.cpu(), causal=causal)
+    err = (got.float().cpu() - law).abs()
+    assert err.max().item() <= MAX_ABS, f"oracle max-abs {err.max().item():.3e}"
+    assert err.mean().item() <= MEAN_ABS, f"oracle mean-abs {err.mean().item():.3e}"
 
 
 def test_noalloc_refuses_more_than_its_array():
@@ -90,3 +104,26 @@ def test_noalloc_refuses_more_than_its_array():
     out = torch.empty_like(x)
     code = _noalloc(lib, x, x, x, out, spec, normalize=False, causal=False)
     assert code == _lib.INVALID_VALUE
+
+
+def test_noalloc_refusal_launches_nothing():
+    """A call the attention would refuse (3 query heads over 2 key/value heads) is refused
+    before the first stage runs: no kernel is launched, so the shared array keeps what the
+    last accepted call left in it."""
+    from torch.profiler import ProfilerActivity, profile
+
+    from cozy_runtime_b200 import _lib, rope
+
+    lib = _lib.load()
+    device = torch.device("cuda", 0)
+    spec = rope.llama(64, 128).to(device)
+    q = torch.zeros(1, 64, 3, 128, dtype=torch.bfloat16, device=device)
+    kv = torch.zeros(1, 64, 2, 128, dtype=torch.bfloat16, device=device)
+    out = torch.empty_like(q)
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        code = _noalloc(lib, q, kv, kv, out, spec, normalize=False, causal=False)
+        torch.cuda.synchronize()
+    assert code == _lib.INVALID_VALUE
+    launched = [e.name for e in prof.events() if "cozy" in e.name]
+    assert not launched, launched
