@@ -6,7 +6,9 @@
 //
 //   warps 0-3   softmax for query tile 0 (thread = one query row = one TMEM lane)
 //   warps 4-7   softmax for query tile 1
-//   warp  8     TMA producer: Q once, then K_j, V_j into a ring of shared-memory slots
+//   warp  8     TMA producer: Q and K_0 once, then V_j with K_{j+1} into a ring of shared-memory
+//               slots; the pair completes one barrier, so the MMA warp waits once per key block
+//               for both (each wait of that warp costs ~150 clocks while its MMAs are in flight)
 //   warp  9     MMA issuer (one elected lane): S = Q·Kᵀ into TMEM, O += P·V, P read from TMEM
 //   warps 10-11 idle (they complete the third warpgroup the register split needs)
 //
@@ -97,9 +99,9 @@ struct AttentionSmem {
   static constexpr int kQOffset = 0;
   static constexpr int kKVOffset = kQTiles * kTileBytes;
   static constexpr int kBarOffset = kKVOffset + kStages * kTileBytes;
-  // barriers: q_full, kv_full[S], kv_empty[S], s_full[2], p_ready[2][2 halves], o_final[2],
-  // drain
-  static constexpr int kBars = 1 + 2 * kStages + 2 + 4 + 2 + 1;
+  // barriers: q_full (Q and K_0), kv_full[2] (the pair V_j, K_{j+1} of block j, alternating),
+  // kv_empty[S], s_full[2], p_ready[2][2 halves], o_final[2], drain
+  static constexpr int kBars = 1 + 2 + kStages + 2 + 4 + 2 + 1;
   static constexpr int kMiscOffset = kBarOffset + kBars * 8;
   static constexpr int kBytes = kMiscOffset + 16;
   static constexpr int kAlloc = kBytes + 1024;  // slack to align the base to 1024 bytes
@@ -349,9 +351,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sKV = smem + L::kKVOffset;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;
-  uint64_t* kv_empty = bars + 1 + kStages;
-  uint64_t* s_full = bars + 1 + 2 * kStages;
+  uint64_t* kv_full = bars + 1;  // [block parity]: V_j and K_{j+1}
+  uint64_t* kv_empty = bars + 3;
+  uint64_t* s_full = bars + 3 + kStages;
   uint64_t* p_ready = s_full + 2;  // [tile][half]
   uint64_t* o_final = s_full + 6;
   uint64_t* drain = s_full + 8;
@@ -385,10 +387,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < kStages; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
-    }
+    mbar_init(&kv_full[0], 1);
+    mbar_init(&kv_full[1], 1);
+    for (int i = 0; i < kStages; ++i) mbar_init(&kv_empty[i], 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
       mbar_init(&p_ready[2 * s], kBlockM);
@@ -710,35 +711,48 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------------------ TMA producer
     // The whole warp walks the schedule (warp-uniform control flow); one elected lane issues.
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
+    // Tiles in order K_0, V_0, K_1, V_1, ...: tile i sits in ring slot i % kStages. Q and K_0
+    // complete q_full; block j's V_j and K_{j+1} complete kv_full[j & 1] together, so the MMA
+    // warp waits once per block for both.
+    auto load_tile = [&](int i, uint64_t* bar) {
+      const int stage = i % kStages;
+      const CUtensorMap* map = (i & 1) ? &tm_v : &tm_k;
+      for (int box = 0; box < L::kBoxes; ++box)
+        tma_load_4d(sKV + stage * L::kTileBytes + box * L::kBoxBytes, map, bar, box * 64,
+                    (kv_first + (i >> 1)) * kBlockN, kv_head, b);
+    };
     if (elect_one()) {
-      mbar_expect_tx(q_full, kQTiles * L::kTileBytes);
+      mbar_expect_tx(q_full, kQTiles * L::kTileBytes + (n_kv > 0 ? L::kTileBytes : 0));
       for (int s = 0; s < kQTiles; ++s)
         for (int box = 0; box < L::kBoxes; ++box)
           tma_load_4d(sQ + s * L::kTileBytes + box * L::kBoxBytes, &tm_q, q_full, box * 64,
                       q0 + s * kBlockM, head, b);
+      if (n_kv > 0) load_tile(0, q_full);
     }
     __syncwarp();
-    int issued = 0;
-    for (int i = 0; i < 2 * n_kv; ++i) {
-      const int stage = i % kStages;
-      if (i >= kStages && !warp_wait(&kv_empty[stage], ((i / kStages) - 1) & 1, abort, p.status))
+    int pairs = 0;
+    for (int j = 0; j < n_kv; ++j) {
+      const int iv = 2 * j + 1, ik = 2 * j + 2;
+      const bool more = j + 1 < n_kv;
+      // both slots free: the MMAs that read their previous tiles have completed
+      if (iv >= kStages &&
+          !warp_wait(&kv_empty[iv % kStages], ((iv / kStages) - 1) & 1, abort, p.status))
         break;
-      const int j = i >> 1;
-      const CUtensorMap* map = (i & 1) ? &tm_v : &tm_k;
+      if (more && ik >= kStages &&
+          !warp_wait(&kv_empty[ik % kStages], ((ik / kStages) - 1) & 1, abort, p.status))
+        break;
       if (elect_one()) {
-        mbar_expect_tx(&kv_full[stage], L::kTileBytes);
-        for (int box = 0; box < L::kBoxes; ++box)
-          tma_load_4d(sKV + stage * L::kTileBytes + box * L::kBoxBytes, map, &kv_full[stage],
-                      box * 64, (kv_first + j) * kBlockN, kv_head, b);
+        mbar_expect_tx(&kv_full[j & 1], (more ? 2 : 1) * L::kTileBytes);
+        load_tile(iv, &kv_full[j & 1]);
+        if (more) load_tile(ik, &kv_full[j & 1]);
       }
       __syncwarp();
-      issued = i + 1;
+      pairs = j + 1;
     }
     // Every copy this CTA issued lands before the CTA unwinds (already true on the normal path,
     // where the MMA warp waited for each one).
     drain_wait(q_full, 0, p.status);
-    for (int i = max(0, issued - kStages); i < issued; ++i)
-      drain_wait(&kv_full[i % kStages], (i / kStages) & 1, p.status);
+    for (int j = max(0, pairs - 2); j < pairs; ++j) drain_wait(&kv_full[j & 1], (j >> 1) & 1, p.status);
     __syncwarp();
   } else if (warp == 9) {
     // ------------------------------------------------------------------------- MMA issuer
@@ -787,8 +801,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                    kk > 0 ? 1u : accumulate);
         }
       };
-      bool ok = warp_wait(q_full, 0, abort, p.status);
-      if (ok) ok = warp_wait(&kv_full[0], 0, abort, p.status);
+      bool ok = warp_wait(q_full, 0, abort, p.status);  // Q and K_0
       if (ok) {
         tc_fence_after();
         if (elect_one()) {
@@ -805,7 +818,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int sv = iv % kStages, sk = ik % kStages;
         const bool more = j + 1 < n_kv;
         const uint32_t acc = j > 0 ? 1u : 0u;
-        if (!(ok = warp_wait(&kv_full[sv], (iv / kStages) & 1, abort, p.status))) break;
+        // V_j and K_{j+1}
+        if (!(ok = warp_wait(&kv_full[j & 1], (j >> 1) & 1, abort, p.status))) break;
         if (!(ok = warp_wait(&p_ready[0], j & 1, abort, p.status))) break;
         tc_fence_after();
         if (elect_one()) issue_pv(0, sv, acc, 0);
@@ -815,17 +829,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (elect_one()) {
           issue_pv(0, sv, acc, 1);
           if (!more) mma_commit(&o_final[0]);
-        }
-        __syncwarp();
-        if (more) {
-          if (!(ok = warp_wait(&kv_full[sk], (ik / kStages) & 1, abort, p.status))) break;
-          tc_fence_after();
-          if (elect_one()) {
+          if (more) {
             issue_qk(0, sk);
             mma_commit(&s_full[0]);
           }
-          __syncwarp();
         }
+        __syncwarp();
         if (!(ok = warp_wait(&p_ready[2], j & 1, abort, p.status))) break;
         tc_fence_after();
         if (elect_one()) issue_pv(1, sv, acc, 0);
