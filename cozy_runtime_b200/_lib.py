@@ -159,6 +159,45 @@ class WidenSource(Structure):
     ]
 
 
+class LayerShape(Structure):
+    """`CozyLayerShape`."""
+
+    _fields_ = [
+        ("world", c_int),
+        ("rows", c_int * MAX_PEERS),
+        ("batch", c_int),
+        ("heads_q", c_int),
+        ("heads_kv", c_int),
+        ("head_dim", c_int),
+        ("causal", c_int),
+    ]
+
+
+class LayerCall(Structure):
+    """`CozyLayerCall`."""
+
+    _fields_ = [
+        ("shape", LayerShape),
+        ("q", c_void_p),
+        ("k", c_void_p),
+        ("v", c_void_p),
+        ("q_strides", c_longlong * 3),
+        ("k_strides", c_longlong * 3),
+        ("v_strides", c_longlong * 3),
+        ("out", c_void_p),
+        ("scale", c_float),
+        ("rope", POINTER(Rope)),
+        ("norm_q", c_int),
+        ("norm_k", c_int),
+        ("norm_q_weight", c_void_p),
+        ("norm_k_weight", c_void_p),
+        ("norm_offset", c_float * 2),
+        ("norm_eps", c_float * 2),
+        ("wait_limit_ns", c_longlong),
+        ("status", c_void_p),
+    ]
+
+
 class CudaCallError(RuntimeError):
     """A library entry point returned a non-zero cudaError_t."""
 
@@ -236,6 +275,20 @@ SIGNATURES = {
          POINTER(HeadMap), POINTER(Scatter), c_int, c_float, c_void_p, c_uint64],
         c_int,
     ),
+    "cozy_group_create": ([c_int, c_int, POINTER(c_void_p)], c_int),
+    "cozy_group_destroy": ([c_void_p], c_int),
+    "cozy_group_blob_bytes": ([], c_int),
+    "cozy_group_needs": ([c_void_p, POINTER(LayerShape), POINTER(c_int)], c_int),
+    "cozy_group_reserve": ([c_void_p, POINTER(LayerShape), c_void_p], c_int),
+    "cozy_group_open": ([c_void_p, c_void_p], c_int),
+    "cozy_group_make_local": ([c_void_p], c_int),
+    "cozy_group_connect_local": ([POINTER(c_void_p), c_int], c_int),
+    "cozy_group_flag_mode": ([c_void_p], c_int),
+    "cozy_group_flag": ([c_void_p, c_int, c_int, POINTER(c_longlong)], c_int),
+    "cozy_ulysses_layer_fwd": ([c_void_p, POINTER(LayerCall), c_uint64], c_int),
+    "cozy_ulysses_layer_begin": ([c_void_p, POINTER(LayerCall), c_uint64], c_int),
+    "cozy_ulysses_layer_attend": ([c_void_p, POINTER(LayerCall), c_uint64], c_int),
+    "cozy_ulysses_layer_end": ([c_void_p, POINTER(LayerCall), c_uint64], c_int),
     "cozy_error_name": ([c_int], c_char_p),
     "cozy_abi_version": ([], c_int),
 }

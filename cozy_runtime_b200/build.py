@@ -17,7 +17,9 @@ PACKAGE = Path(__file__).resolve().parent
 ROOT = PACKAGE.parent
 CSRC = PACKAGE / "csrc"
 LIBRARY = PACKAGE / "libcozy_ulysses.so"
-SOURCES = ["attention_fwd.cu", "stage.cu", "fp8.cu", "peer.cu", "noalloc.cu", "narrow.cu", "capi.cu"]
+SOURCES = [
+    "attention_fwd.cu", "stage.cu", "fp8.cu", "peer.cu", "layer.cu", "noalloc.cu", "narrow.cu", "capi.cu",
+]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 #: Sources compiled with IEEE fp32 semantics (denormals kept, exact division and square root):
 #: the int8 wire's law must round as the reference's CPU arithmetic does.

@@ -38,6 +38,7 @@
 #include <utility>
 
 #include "../../include/cozy_ulysses.h"
+#include "attention.h"
 #include "sm100.cuh"
 
 namespace cozy {
@@ -88,7 +89,60 @@ struct AttentionParams {
   float* ws_o;     // [split tile][part][query tile][HD / 4][128 rows] float4
   float2* ws_ml;   // [split tile][part][query tile][128 rows]
   int* counters;   // [split tile][query tile], zero at launch
+  // Walk orders. Query blocks run from q_turn downwards, cyclically (q_turn = q_blocks - 1: the
+  // last block first, which for causal calls is the heaviest); each tile's key blocks run from
+  // kv_turn downwards, cyclically (kv_turn < 0: upwards from block 0).
+  int q_turn, kv_turn;
+  // Rows still crossing from other GPUs: rows [src_start[s], src_start[s + 1]) come from source
+  // s, resident once arrive[s] (a flag in this GPU's memory the source writes) reaches
+  // arrive_seq; the producer waits for a source's flag before its first load of that source's
+  // rows (bounded by arrive_limit_ns, then kStatusPeerTimeout). arrive == nullptr: all rows are
+  // resident. Source arrive_self is resident from the start.
+  const long long* arrive;
+  long long arrive_seq, arrive_limit_ns;
+  int n_src, arrive_self;
+  int src_start[COZY_MAX_PEERS + 1];
 };
+
+// The query block of tile index t (q_turn downwards, cyclically).
+__device__ __forceinline__ int tile_qblock(const AttentionParams& p, int t) {
+  int qb = p.q_turn - t % p.q_blocks;
+  return qb < 0 ? qb + p.q_blocks : qb;
+}
+
+// The key block of walk step i for a tile with n_blocks key blocks.
+__device__ __forceinline__ int walk_block(const AttentionParams& p, int i, int n_blocks) {
+  if (p.kv_turn < 0) return i;
+  const int first = min(p.kv_turn, n_blocks - 1);
+  const int b = first - i;
+  return b < 0 ? b + n_blocks : b;
+}
+
+// Waits (lane 0 of the calling warp, bounded) until *flag reaches seq with acquire semantics at
+// system scope. Returns false when the time limit passes (status: peer timeout) or the CTA or
+// launch already gave up.
+__device__ __forceinline__ bool wait_flag(const long long* flag, long long seq, long long limit_ns,
+                                          volatile int* abort, int* status) {
+  const uint64_t start = global_timer_ns();
+  for (uint32_t spin = 0;; ++spin) {
+    long long v;
+    asm volatile("ld.acquire.sys.global.s64 %0, [%1];" : "=l"(v) : "l"(flag) : "memory");
+    if (v >= seq) return true;
+    if ((spin & 63u) == 63u) {
+      if (*abort) return false;
+      if (status != nullptr && *reinterpret_cast<volatile int*>(status) != kStatusOk) {
+        *abort = 1;
+        return false;
+      }
+      if (global_timer_ns() - start > static_cast<uint64_t>(limit_ns)) {
+        *abort = 1;
+        if (status != nullptr) atomicCAS(status, kStatusOk, kStatusPeerTimeout);
+        return false;
+      }
+    }
+    __nanosleep(32);
+  }
+}
 
 template <int HD, bool FP8>
 struct AttentionSmem {
@@ -363,12 +417,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // Work unit -> tile (query block x, head, batch), x fastest. Heaviest causal blocks first:
-  // block x takes query block (q_blocks - 1 - x).
+  // Work unit -> tile (query block x, head, batch), x fastest; tile x takes query block
+  // tile_qblock(x) (for causal calls q_turn is the last block: heaviest first).
   int part = -1, split_tile = 0;
   const int tile = SPLIT ? unit_tile(p, static_cast<int>(blockIdx.x), &part, &split_tile)
                          : static_cast<int>(blockIdx.x);
-  const int qb = p.q_blocks - 1 - tile % p.q_blocks;
+  const int qb = tile_qblock(p, tile);
   const int head = (tile / p.q_blocks) % p.heads_q;
   const int b = tile / (p.q_blocks * p.heads_q);
   const int kv_head = (head + p.q_base) / p.group - p.kv_base;
@@ -452,7 +506,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       reg_fence(r1);
       reg_fence(r2);
       reg_fence(r3);
-      const int kv0 = j * kBlockN;
+      const int kv0 = walk_block(p, j, n_blocks) * kBlockN;
       // multipliers of the two 64-key halves (bf16: the softmax scale)
       float sc_lo = scale, sc_hi = scale;
       if constexpr (FP8) {
@@ -566,7 +620,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int head = (e_tile / p.q_blocks) % p.heads_q;
     const int b = e_tile / (p.q_blocks * p.heads_q);
     const int kv_head = (head + p.q_base) / p.group - p.kv_base;
-    const int q_row = (p.q_blocks - 1 - e_tile % p.q_blocks) * (kQTiles * kBlockM) +
+    const int q_row = tile_qblock(p, e_tile) * (kQTiles * kBlockM) +
                       e_s * kBlockM + quarter * 32 + e_lane;
     const uint32_t e_tO = *reinterpret_cast<volatile uint32_t*>(tmem_slot) +
                           (static_cast<uint32_t>(quarter * 32) << 16) + 256u +
@@ -711,48 +765,78 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------------------ TMA producer
     // The whole warp walks the schedule (warp-uniform control flow); one elected lane issues.
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
-    // Tiles in order K_0, V_0, K_1, V_1, ...: tile i sits in ring slot i % kStages. Q and K_0
-    // complete q_full; block j's V_j and K_{j+1} complete kv_full[j & 1] together, so the MMA
-    // warp waits once per block for both.
+    // Tiles in order K_0, V_0, K_1, V_1, ... of this unit's walk: tile i sits in ring slot
+    // i % kStages. Q and K_0 complete q_full; walk step j's V_j and K_{j+1} complete
+    // kv_full[j & 1] together, so the MMA warp waits once per step for both.
+    auto tile_block = [&](int i) { return walk_block(p, kv_first + (i >> 1), n_blocks); };
     auto load_tile = [&](int i, uint64_t* bar) {
       const int stage = i % kStages;
       const CUtensorMap* map = (i & 1) ? &tm_v : &tm_k;
       for (int box = 0; box < L::kBoxes; ++box)
         tma_load_4d(sKV + stage * L::kTileBytes + box * L::kBoxBytes, map, bar, box * 64,
-                    (kv_first + (i >> 1)) * kBlockN, kv_head, b);
+                    tile_block(i) * kBlockN, kv_head, b);
     };
-    if (elect_one()) {
-      mbar_expect_tx(q_full, kQTiles * L::kTileBytes + (n_kv > 0 ? L::kTileBytes : 0));
-      for (int s = 0; s < kQTiles; ++s)
-        for (int box = 0; box < L::kBoxes; ++box)
-          tma_load_4d(sQ + s * L::kTileBytes + box * L::kBoxBytes, &tm_q, q_full, box * 64,
-                      q0 + s * kBlockM, head, b);
-      if (n_kv > 0) load_tile(0, q_full);
-    }
-    __syncwarp();
+    // Rows [r0, r1) resident: wait for each source not seen yet (warp-uniform; lane 0 polls),
+    // then order the flag reads before the tensor copies that read the rows (async proxy).
+    uint32_t seen = p.arrive != nullptr ? (1u << p.arrive_self) : 0xffffffffu;
+    auto resident = [&](int r0, int r1) -> bool {
+      uint32_t need = 0;
+      for (int src = 0; src < p.n_src; ++src)
+        if (p.src_start[src] < r1 && p.src_start[src + 1] > r0) need |= 1u << src;
+      need &= ~seen;
+      if (need == 0) return true;
+      while (need != 0) {
+        const int src = __ffs(need) - 1;
+        bool arrived = true;
+        if (lane == 0)
+          arrived = wait_flag(p.arrive + src, p.arrive_seq, p.arrive_limit_ns, abort, p.status);
+        if (!__shfl_sync(0xffffffffu, arrived, 0)) return false;
+        seen |= 1u << src;
+        need &= need - 1;
+      }
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+      return true;
+    };
+    bool issued_q = false;
     int pairs = 0;
-    for (int j = 0; j < n_kv; ++j) {
-      const int iv = 2 * j + 1, ik = 2 * j + 2;
-      const bool more = j + 1 < n_kv;
-      // both slots free: the MMAs that read their previous tiles have completed
-      if (iv >= kStages &&
-          !warp_wait(&kv_empty[iv % kStages], ((iv / kStages) - 1) & 1, abort, p.status))
-        break;
-      if (more && ik >= kStages &&
-          !warp_wait(&kv_empty[ik % kStages], ((ik / kStages) - 1) & 1, abort, p.status))
-        break;
+    if (resident(q0, q0 + kQTiles * kBlockM) &&
+        (n_kv == 0 || resident(tile_block(0) * kBlockN, tile_block(0) * kBlockN + kBlockN))) {
       if (elect_one()) {
-        mbar_expect_tx(&kv_full[j & 1], (more ? 2 : 1) * L::kTileBytes);
-        load_tile(iv, &kv_full[j & 1]);
-        if (more) load_tile(ik, &kv_full[j & 1]);
+        mbar_expect_tx(q_full, kQTiles * L::kTileBytes + (n_kv > 0 ? L::kTileBytes : 0));
+        for (int s = 0; s < kQTiles; ++s)
+          for (int box = 0; box < L::kBoxes; ++box)
+            tma_load_4d(sQ + s * L::kTileBytes + box * L::kBoxBytes, &tm_q, q_full, box * 64,
+                        q0 + s * kBlockM, head, b);
+        if (n_kv > 0) load_tile(0, q_full);
       }
       __syncwarp();
-      pairs = j + 1;
+      issued_q = true;
+      for (int j = 0; j < n_kv; ++j) {
+        const int iv = 2 * j + 1, ik = 2 * j + 2;
+        const bool more = j + 1 < n_kv;
+        // both slots free: the MMAs that read their previous tiles have completed
+        if (iv >= kStages &&
+            !warp_wait(&kv_empty[iv % kStages], ((iv / kStages) - 1) & 1, abort, p.status))
+          break;
+        if (more && ik >= kStages &&
+            !warp_wait(&kv_empty[ik % kStages], ((ik / kStages) - 1) & 1, abort, p.status))
+          break;
+        const int bv = tile_block(iv) * kBlockN, bk = more ? tile_block(ik) * kBlockN : bv;
+        if (!resident(bv, bv + kBlockN) || !resident(bk, bk + kBlockN)) break;
+        if (elect_one()) {
+          mbar_expect_tx(&kv_full[j & 1], (more ? 2 : 1) * L::kTileBytes);
+          load_tile(iv, &kv_full[j & 1]);
+          if (more) load_tile(ik, &kv_full[j & 1]);
+        }
+        __syncwarp();
+        pairs = j + 1;
+      }
     }
     // Every copy this CTA issued lands before the CTA unwinds (already true on the normal path,
     // where the MMA warp waited for each one).
-    drain_wait(q_full, 0, p.status);
-    for (int j = max(0, pairs - 2); j < pairs; ++j) drain_wait(&kv_full[j & 1], (j >> 1) & 1, p.status);
+    if (issued_q) drain_wait(q_full, 0, p.status);
+    for (int j = max(0, pairs - 2); j < pairs; ++j)
+      drain_wait(&kv_full[j & 1], (j >> 1) & 1, p.status);
     __syncwarp();
   } else if (warp == 9) {
     // ------------------------------------------------------------------------- MMA issuer
@@ -1018,9 +1102,17 @@ static int sm_count(int device) {
   return counts[device];
 }
 
+// Where the split's workspace comes from: `given` (a caller's buffer of `given_bytes`; too
+// small: the launch runs unsplit) or, with given == nullptr, the library's per-stream one.
+struct WorkspaceChoice {
+  void* given;
+  size_t given_bytes;
+};
+
 template <int HD, bool FP8>
 static int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
-                  AttentionParams& p, bool allow_split, cudaStream_t stream) {
+                  AttentionParams& p, bool allow_split, const WorkspaceChoice* choice,
+                  cudaStream_t stream) {
   using L = AttentionSmem<HD, FP8>;
   static bool configured[64] = {};
   int device = 0;
@@ -1045,8 +1137,12 @@ static int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMa
   p.ws_ml = nullptr;
   p.counters = nullptr;
   if (plan.n_split > 0) {
-    uint8_t* ws = static_cast<uint8_t*>(
-        split_workspace(device, stream, split_bytes(plan.n_split, plan.parts, HD)));
+    const size_t need = split_bytes(plan.n_split, plan.parts, HD);
+    uint8_t* ws = nullptr;
+    if (choice != nullptr && choice->given != nullptr)
+      ws = choice->given_bytes >= need ? static_cast<uint8_t*>(choice->given) : nullptr;
+    else
+      ws = static_cast<uint8_t*>(split_workspace(device, stream, need));
     if (ws == nullptr) {
       p.n_full = static_cast<int>(tiles);
       p.parts = 1;
@@ -1088,6 +1184,7 @@ static int attention_launch(const void* q, const void* k, const void* v, void* o
                             const long long* v_strides, const long long* o_strides,
                             const CozyHeadMap* head_map, const CozyScatter* scatter, int causal,
                             float scale, int* status, const Fp8Operands* fp8, bool allow_split,
+                            const Arrival* arrival, const WorkspaceChoice* choice,
                             cudaStream_t stream) {
   if (head_dim != 64 && head_dim != 128) return cudaErrorNotSupported;
   if (fp8 != nullptr && head_dim != 128) return cudaErrorNotSupported;
@@ -1185,6 +1282,38 @@ static int attention_launch(const void* q, const void* k, const void* v, void* o
       for (int i = 0; i < 3; ++i) p.outs_strides[w][i] = scatter->strides[w][i];
     }
   }
+  // walk orders: the last query block first; key blocks upwards
+  p.q_turn = p.q_blocks - 1;
+  p.kv_turn = -1;
+  p.arrive = nullptr;
+  p.arrive_seq = 0;
+  p.arrive_limit_ns = 0;
+  p.n_src = 0;
+  p.arrive_self = 0;
+  if (arrival != nullptr) {
+    if (arrival->flags == nullptr || arrival->n_src < 1 || arrival->n_src > COZY_MAX_PEERS ||
+        arrival->self < 0 || arrival->self >= arrival->n_src || arrival->limit_ns <= 0 ||
+        reinterpret_cast<uintptr_t>(arrival->flags) % 8 != 0 || seq_q != seq_k)
+      return cudaErrorInvalidValue;
+    if (arrival->src_start[0] != 0 || arrival->src_start[arrival->n_src] != seq_k)
+      return cudaErrorInvalidValue;
+    for (int r = 0; r < arrival->n_src; ++r)
+      if (arrival->src_start[r + 1] < arrival->src_start[r]) return cudaErrorInvalidValue;
+    p.arrive = arrival->flags;
+    p.arrive_seq = arrival->seq;
+    p.arrive_limit_ns = arrival->limit_ns;
+    p.n_src = arrival->n_src;
+    p.arrive_self = arrival->self;
+    for (int r = 0; r <= arrival->n_src; ++r) p.src_start[r] = arrival->src_start[r];
+    // This GPU's own rows are resident first: every tile's keys start there and walk down
+    // through the sources in the order they arrive (each source sends to the ranks after it in
+    // turn, so source self - 1 lands first); non-causal query blocks start there too.
+    const int lo = arrival->src_start[arrival->self], hi = arrival->src_start[arrival->self + 1];
+    if (hi > lo) {
+      p.kv_turn = (hi - 1) / kBlockN;
+      if (!causal) p.q_turn = (hi - 1) / (kQTiles * kBlockM);
+    }
+  }
   p.q_scale = p.k_scale = p.v_scale = nullptr;
   p.scale_seq = 0;
   p.n_cuts = 0;
@@ -1195,10 +1324,10 @@ static int attention_launch(const void* q, const void* k, const void* v, void* o
     p.scale_seq = fp8->scale_seq;
     p.n_cuts = fp8->n_cuts;
     for (int c = 0; c < fp8->n_cuts; ++c) p.cuts[c] = fp8->cuts[c];
-    return launch<128, true>(mq, mk, mv, p, allow_split, stream);
+    return launch<128, true>(mq, mk, mv, p, allow_split, choice, stream);
   }
-  if (head_dim == 128) return launch<128, false>(mq, mk, mv, p, allow_split, stream);
-  return launch<64, false>(mq, mk, mv, p, allow_split, stream);
+  if (head_dim == 128) return launch<128, false>(mq, mk, mv, p, allow_split, choice, stream);
+  return launch<64, false>(mq, mk, mv, p, allow_split, choice, stream);
 }
 
 int attention_forward(const void* q, const void* k, const void* v, void* out, int batch,
@@ -1209,7 +1338,7 @@ int attention_forward(const void* q, const void* k, const void* v, void* out, in
                       float scale, int* status, cudaStream_t stream) {
   return attention_launch(q, k, v, out, batch, seq_q, seq_k, heads_q, heads_kv, head_dim,
                           q_strides, k_strides, v_strides, o_strides, head_map, scatter, causal,
-                          scale, status, nullptr, true, stream);
+                          scale, status, nullptr, true, nullptr, nullptr, stream);
 }
 
 // The split plan attention_forward takes on the current device for a non-FP8 call of this shape
@@ -1249,7 +1378,7 @@ int attention_forward_unsplit(const void* q, const void* k, const void* v, void*
                               int causal, float scale, int* status, cudaStream_t stream) {
   return attention_launch(q, k, v, out, batch, seq_q, seq_k, heads_q, heads_kv, head_dim,
                           q_strides, k_strides, v_strides, o_strides, head_map, scatter, causal,
-                          scale, status, nullptr, false, stream);
+                          scale, status, nullptr, false, nullptr, nullptr, stream);
 }
 
 int attention_forward_fp8(const void* q, const void* k, const void* v, const float* q_scale,
@@ -1262,7 +1391,38 @@ int attention_forward_fp8(const void* q, const void* k, const void* v, const flo
   const Fp8Operands fp8 = {q_scale, k_scale, v_scale, scale_seq, cuts, n_cuts};
   return attention_launch(q, k, v, out, batch, seq_q, seq_k, heads_q, heads_kv, head_dim,
                           q_strides, k_strides, v_strides, o_strides, head_map, scatter, causal,
-                          scale, status, &fp8, true, stream);
+                          scale, status, &fp8, true, nullptr, nullptr, stream);
+}
+
+}  // namespace cozy
+
+namespace cozy {
+
+int attention_forward_ex(const void* q, const void* k, const void* v, void* out, int batch,
+                         int seq_q, int seq_k, int heads_q, int heads_kv, int head_dim,
+                         const long long* q_strides, const long long* k_strides,
+                         const long long* v_strides, const long long* o_strides,
+                         const CozyHeadMap* head_map, const CozyScatter* scatter, int causal,
+                         float scale, int* status, const Arrival* arrival, void* workspace,
+                         size_t workspace_bytes, cudaStream_t stream) {
+  // a null workspace must not fall back to the library's own (it would allocate)
+  static char none;
+  const WorkspaceChoice choice = {workspace != nullptr ? workspace : &none,
+                                  workspace != nullptr ? workspace_bytes : 0};
+  return attention_launch(q, k, v, out, batch, seq_q, seq_k, heads_q, heads_kv, head_dim,
+                          q_strides, k_strides, v_strides, o_strides, head_map, scatter, causal,
+                          scale, status, nullptr, true, arrival, &choice, stream);
+}
+
+size_t attention_workspace_bytes(int batch, int seq_q, int seq_k, int heads_q, int head_dim,
+                                 int causal, int sms) {
+  if (batch <= 0 || seq_q <= 0 || seq_k <= 0 || heads_q <= 0 || sms <= 0 || causal ||
+      (head_dim != 64 && head_dim != 128))
+    return 0;
+  const long long tiles = static_cast<long long>(batch) * heads_q *
+                          ((seq_q + kQTiles * kBlockM - 1) / (kQTiles * kBlockM));
+  const SplitPlan plan = plan_split(tiles, (seq_k + kBlockN - 1) / kBlockN, sms, head_dim);
+  return plan.n_split > 0 ? split_bytes(plan.n_split, plan.parts, head_dim) : 0;
 }
 
 }  // namespace cozy

@@ -15,9 +15,11 @@
 
 namespace cozy {
 
-__global__ void peer_signal_kernel(CozyPeerSlots slots, long long seq) {
+__global__ void peer_signal_kernel(CozyPeerSlots slots, long long seq, const int* status) {
   const int i = threadIdx.x;
   __threadfence_system();
+  // after a timed-out wait on this GPU nothing more is published to the peers
+  if (status != nullptr && *reinterpret_cast<const volatile int*>(status) != kStatusOk) return;
   if (i < slots.count) {
     long long* slot = slots.slot[i];
     asm volatile("st.release.sys.global.s64 [%0], %1;" ::"l"(slot), "l"(seq) : "memory");
@@ -46,6 +48,25 @@ __global__ void peer_wait_kernel(const long long* flags, int count, long long se
   }
   __syncthreads();
   __threadfence_system();
+}
+
+int peer_signal(const CozyPeerSlots* slots, long long seq, const int* status,
+                cudaStream_t stream) {
+  if (slots == nullptr || slots->count < 0 || slots->count > COZY_MAX_PEERS)
+    return cudaErrorInvalidValue;
+  for (int i = 0; i < slots->count; ++i)
+    if (slots->slot[i] == nullptr || reinterpret_cast<uintptr_t>(slots->slot[i]) % 8)
+      return cudaErrorInvalidValue;
+  peer_signal_kernel<<<1, 32, 0, stream>>>(*slots, seq, status);
+  return cudaGetLastError();
+}
+
+int peer_wait(const long long* flags, int count, long long seq, long long limit_ns, int* status,
+              cudaStream_t stream) {
+  if (flags == nullptr || count < 0 || count > COZY_MAX_PEERS || limit_ns <= 0)
+    return cudaErrorInvalidValue;
+  peer_wait_kernel<<<1, 32, 0, stream>>>(flags, count, seq, limit_ns, status);
+  return cudaGetLastError();
 }
 
 }  // namespace cozy
@@ -81,22 +102,13 @@ int cozy_ipc_free(void* ptr) { return cudaFree(ptr); }
 int cozy_ipc_handle_bytes(void) { return static_cast<int>(sizeof(cudaIpcMemHandle_t)); }
 
 int cozy_peer_signal(const CozyPeerSlots* slots, long long seq, uintptr_t stream) {
-  if (slots == nullptr || slots->count < 0 || slots->count > COZY_MAX_PEERS)
-    return cudaErrorInvalidValue;
-  for (int i = 0; i < slots->count; ++i)
-    if (slots->slot[i] == nullptr || reinterpret_cast<uintptr_t>(slots->slot[i]) % 8)
-      return cudaErrorInvalidValue;
-  cozy::peer_signal_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(*slots, seq);
-  return cudaGetLastError();
+  return cozy::peer_signal(slots, seq, nullptr, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int cozy_peer_wait(const long long* flags, int count, long long seq, long long limit_ns,
                    int* status, uintptr_t stream) {
-  if (flags == nullptr || count < 0 || count > COZY_MAX_PEERS || limit_ns <= 0)
-    return cudaErrorInvalidValue;
-  cozy::peer_wait_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      flags, count, seq, limit_ns, status);
-  return cudaGetLastError();
+  return cozy::peer_wait(flags, count, seq, limit_ns, status,
+                         reinterpret_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -284,8 +284,18 @@ int head_norm_rope(const void* x, void* out, int batch, int seq, int heads, int 
   return cudaGetLastError();
 }
 
+// remote: the destinations are mostly other GPUs' memory (bulk copies out of shared memory);
+// otherwise every destination is this GPU's own memory (16-byte stores a thread).
+int ulysses_pack_to(const CozyPackTensor* tensors, int count, int world, int rows, int batch,
+                    int head_dim, const CozyRope* rope, bool remote, cudaStream_t stream);
+
 int ulysses_pack(const CozyPackTensor* tensors, int count, int world, int rows, int batch,
                  int head_dim, const CozyRope* rope, cudaStream_t stream) {
+  return ulysses_pack_to(tensors, count, world, rows, batch, head_dim, rope, world > 1, stream);
+}
+
+int ulysses_pack_to(const CozyPackTensor* tensors, int count, int world, int rows, int batch,
+                    int head_dim, const CozyRope* rope, bool remote, cudaStream_t stream) {
   if (count < 1 || count > 3 || world < 1 || world > COZY_MAX_PEERS || rows < 0 || batch < 1)
     return cudaErrorInvalidValue;
   if (head_dim != 64 && head_dim != 128) return cudaErrorNotSupported;
@@ -323,8 +333,7 @@ int ulysses_pack(const CozyPackTensor* tensors, int count, int world, int rows, 
   const int rows_per_block = kPackRows * 256 / (head_dim / 8);
   const long long blocks = (dest_rows + rows_per_block - 1) / rows_per_block;
   dim3 grid(static_cast<unsigned>(blocks), world, count);
-  // one destination: this GPU's own memory, direct stores; more: mostly peers, bulk copies
-  if (world > 1) {
+  if (remote) {
     if (head_dim == 128) pack_kernel<128, true><<<grid, 256, 0, stream>>>(a);
     else pack_kernel<64, true><<<grid, 256, 0, stream>>>(a);
   } else {

@@ -207,3 +207,119 @@ def close(handle) -> None:
     if found is not None:
         found.close()
         dist.barrier(group=handle)
+
+
+# ------------------------------------------------------------------ the C-side layer group
+def layer_shape(rows, batch: int, heads: int, heads_kv: int, dim: int, causal: bool
+                ) -> _lib.LayerShape:
+    """`CozyLayerShape` of a layer: every rank's rows and the head layout."""
+    shape = _lib.LayerShape()
+    shape.world = len(rows)
+    for r, n in enumerate(rows):
+        shape.rows[r] = int(n)
+    shape.batch, shape.heads_q, shape.heads_kv = batch, heads, heads_kv
+    shape.head_dim, shape.causal = dim, int(causal)
+    return shape
+
+
+class LayerGroup:
+    """One rank's `CozyGroup`: the buffers, flags and side stream the C layer entry
+    (`cozy_ulysses_layer_fwd`) runs one node's Ulysses layer with. Formed on first use of a
+    process group (collective) and grown when a larger layer comes, as `PeerGroup` is."""
+
+    def __init__(self, handle, device: torch.device, *, rank: int | None = None,
+                 world: int | None = None, local: bool = False) -> None:
+        lib = _lib.load()
+        self.handle, self.device, self.local = handle, device, local
+        self.rank = dist.get_rank(handle) if rank is None else rank
+        self.world = dist.get_world_size(handle) if world is None else world
+        self.lock = threading.Lock()
+        ptr = ctypes.c_void_p()
+        with torch.cuda.device(device):
+            _lib.check("cozy_group_create", lib.cozy_group_create(self.rank, self.world,
+                                                                  ctypes.byref(ptr)))
+        self.ptr = ptr
+        if local:
+            _lib.check("cozy_group_make_local", lib.cozy_group_make_local(self.ptr))
+
+    def needs(self, shape: _lib.LayerShape) -> bool:
+        grow = ctypes.c_int(0)
+        _lib.check("cozy_group_needs", _lib.load().cozy_group_needs(self.ptr, ctypes.byref(shape),
+                                                                    ctypes.byref(grow)))
+        return bool(grow.value)
+
+    def ensure(self, shape: _lib.LayerShape) -> None:
+        """Grow the buffers for `shape` on every rank together (all ranks agree: the decision
+        follows from the agreed rows)."""
+        if not self.needs(shape):
+            return
+        lib = _lib.load()
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.handle)  # no rank still writes into the buffers about to go
+        blob = ctypes.create_string_buffer(lib.cozy_group_blob_bytes())
+        with torch.cuda.device(self.device):
+            _lib.check("cozy_group_reserve", lib.cozy_group_reserve(self.ptr, ctypes.byref(shape),
+                                                                    blob))
+        gathered: list = [None] * self.world
+        dist.all_gather_object(gathered, bytes(blob.raw), group=self.handle)
+        blobs = ctypes.create_string_buffer(b"".join(gathered), len(blob.raw) * self.world)
+        with torch.cuda.device(self.device):
+            _lib.check("cozy_group_open", lib.cozy_group_open(self.ptr, blobs))
+
+    def flag_mode(self) -> str:
+        mode = _lib.load().cozy_group_flag_mode(self.ptr)
+        return {1: "stream write", 2: "host word copy"}.get(mode, str(mode))
+
+    def flag(self, kind: int, src: int) -> int:
+        """The last call number rank `src` published here (0: Q/K/V landed, 1: output rows)."""
+        value = ctypes.c_longlong(0)
+        _lib.check("cozy_group_flag", _lib.load().cozy_group_flag(self.ptr, kind, src,
+                                                                  ctypes.byref(value)))
+        return value.value
+
+    def run(self, phase: str, call: _lib.LayerCall, stream: int) -> None:
+        entry = f"cozy_ulysses_layer_{phase}"
+        _lib.check(entry, getattr(_lib.load(), entry)(self.ptr, ctypes.byref(call), stream))
+
+    def close(self) -> None:
+        if self.ptr is not None and self.ptr.value:
+            torch.cuda.synchronize(self.device)
+            _lib.load().cozy_group_destroy(self.ptr)
+        self.ptr = None
+
+
+def local_layer_groups(world: int, device: torch.device, shape: _lib.LayerShape
+                       ) -> list[LayerGroup]:
+    """Every rank of a `world`-rank group in this process, on one GPU: buffers are plain
+    allocations the ranks address directly (tests simulate the layer with them: every rank's
+    begin, then every rank's attend, then every rank's end)."""
+    groups = [LayerGroup(None, device, rank=r, world=world, local=True) for r in range(world)]
+    lib = _lib.load()
+    with torch.cuda.device(device):
+        for g in groups:
+            _lib.check("cozy_group_reserve", lib.cozy_group_reserve(g.ptr, ctypes.byref(shape),
+                                                                    None))
+        ptrs = (ctypes.c_void_p * world)(*(g.ptr.value for g in groups))
+        _lib.check("cozy_group_connect_local", lib.cozy_group_connect_local(ptrs, world))
+    return groups
+
+
+_LAYER_GROUPS: weakref.WeakKeyDictionary = weakref.WeakKeyDictionary()
+
+
+def layer_group_for(handle, device: torch.device) -> LayerGroup:
+    """This rank's layer group for `handle` (formed on first use; collective)."""
+    with _GROUPS_LOCK:
+        found = _LAYER_GROUPS.get(handle)
+        if found is None:
+            found = _LAYER_GROUPS[handle] = LayerGroup(handle, device)
+        return found
+
+
+def close_layer(handle) -> None:
+    """Release the layer group of `handle` (collective with the group's other ranks)."""
+    with _GROUPS_LOCK:
+        found = _LAYER_GROUPS.pop(handle, None)
+    if found is not None:
+        found.close()
+        dist.barrier(group=handle)

@@ -28,7 +28,9 @@ passes `rows`.
 
 from __future__ import annotations
 
+import ctypes
 import json
+import math
 import os
 import threading
 import weakref
@@ -622,7 +624,11 @@ def _form_check(handle, device: torch.device) -> bool:
         over_peer = exchange(q, k, v, handle, None, rows=rows, transport="peer")
         over_nccl = exchange(q, k, v, handle, None, rows=rows, transport="nccl")
         torch.cuda.synchronize(device)
-        ok = bool(torch.equal(over_peer, over_nccl)) and not int(
+        # The NVLink layer walks each tile's keys from this rank's own rows on, the NCCL path
+        # from row 0: the sums differ in order, so the outputs agree to bf16 rounding, not bit
+        # for bit. A transport that moved wrong or stale bytes misses by far more.
+        diff = (over_peer.float() - over_nccl.float()).abs()
+        ok = bool(diff.max().item() <= 1e-2 and diff.mean().item() <= 1e-3) and not int(
             attention.status_word(device).item()
         )
     except RuntimeError:
@@ -641,6 +647,43 @@ def _transport(handle, asked: str | None) -> str:
     return choice
 
 
+def _layer_call(
+    query: Tensor, key: Tensor, value: Tensor, out: Tensor, rows: Sequence[int], causal: bool,
+    scale: float | None, rope: RopeSpec | None, norm_q: Norm | None, norm_k: Norm | None,
+    status: int, wait_limit_ns: int = 0,
+) -> tuple[_lib.LayerCall, list]:
+    """`CozyLayerCall` for this rank's tensors, and the objects it points into (keep them alive
+    until the call is queued)."""
+    batch, _, heads, dim = (int(n) for n in query.shape)
+    call = _lib.LayerCall()
+    call.shape = peer.layer_shape(rows, batch, heads, int(key.shape[2]), dim, causal)
+    call.q, call.k, call.v = query.data_ptr(), key.data_ptr(), value.data_ptr()
+    for field, t in (("q_strides", query), ("k_strides", key), ("v_strides", value)):
+        if t.stride(3) != 1:
+            raise ValueError("the head dimension must be contiguous")
+        getattr(call, field)[:] = [t.stride(1), t.stride(2), t.stride(0)]
+    call.out = out.data_ptr()
+    call.scale = 1.0 / math.sqrt(dim) if scale is None else float(scale)
+    keep: list = []
+    if rope is not None:
+        r = _rope_struct(rope, 0)
+        keep.append(r)
+        call.rope = ctypes.pointer(r)
+    for i, norm in enumerate((norm_q, norm_k)):
+        if norm is None:
+            continue
+        setattr(call, "norm_q" if i == 0 else "norm_k", 1)
+        if norm.weight is not None:
+            w = norm.weight.to(device=query.device, dtype=torch.float32).contiguous()
+            keep.append(w)
+            setattr(call, "norm_q_weight" if i == 0 else "norm_k_weight", w.data_ptr())
+        call.norm_offset[i] = float(norm.offset)
+        call.norm_eps[i] = float(norm.eps)
+    call.wait_limit_ns = int(wait_limit_ns)
+    call.status = status
+    return call, keep
+
+
 def _exchange_peer(
     query: Tensor,
     key: Tensor,
@@ -655,61 +698,30 @@ def _exchange_peer(
     norm_q: Norm | None,
     norm_k: Norm | None,
 ) -> Tensor:
-    """The exchange over NVLink stores issued by the kernels themselves (`peer.PeerGroup`):
-    stage 1 writes every peer's heads into that peer's receive buffer, the attention writes every
-    output row into its owner's landing buffer; flags say when a call's writes have landed."""
+    """The exchange over NVLink through the C layer entry (`cozy_ulysses_layer_*` on this
+    rank's `peer.LayerGroup`): the first stage writes this rank's own block into its receive
+    buffer and the others into staging, the copy engines move them to their owners with an
+    arrival flag each, the attention starts on this rank's own rows at once and waits per source
+    inside the kernel, its epilogue stores every output row into its owner's landing buffer,
+    and flags say when a call's rows have landed."""
     batch, mine, heads, dim = (int(n) for n in query.shape)
     device = query.device
-    world, total = layout.world, layout.total
-    rows = layout.rows
-    el = query.element_size()
-    sizes = {
-        "q": total * batch * max(layout.q_n) * dim * el,
-        "k": total * batch * max(layout.kv_n) * dim * el,
-        "v": total * batch * max(layout.kv_n) * dim * el,
-        "land": batch * max(rows) * heads * dim * el,
-    }
-    pg = peer.group_for(handle, device)
-    status = attention.status_word(device).data_ptr()
-    with pg.lock:
-        pg.ensure(sizes)
-        seq = pg.next_seq()
-        s = seq & 1
-        step = RankStep(query, key, value, layout, rank, rope=rope, norm_q=norm_q, norm_k=norm_k)
-        start = layout.start(rank)
-        q_dst = [pg.peer(p, s, "q") + start * batch * layout.q_n[p] * dim * el for p in range(world)]
-        k_dst = [pg.peer(p, s, "k") + start * batch * layout.kv_n[p] * dim * el for p in range(world)]
-        v_dst = [pg.peer(p, s, "v") + start * batch * layout.kv_n[p] * dim * el for p in range(world)]
-        step.pack_to(q_dst, k_dst, v_dst)
-        pg.signal(peer.QKV, seq)
-        pg.wait(peer.QKV, seq, status)
+    lg = peer.layer_group_for(handle, device)
+    out = torch.empty((batch, mine, heads, dim), dtype=query.dtype, device=device)
+    call, keep = _layer_call(
+        query, key, value, out, layout.rows, causal, scale, rope, norm_q, norm_k,
+        attention.status_word(device).data_ptr(),
+    )
+    stream = torch.cuda.current_stream(device).cuda_stream
+    with lg.lock:
+        lg.ensure(call.shape)
+        lg.run("begin", call, stream)
         first = _Clock.mark(query)
-        qn, kvn = layout.q_n[rank], layout.kv_n[rank]
-        if qn:
-            scatter = _lib.Scatter()
-            scatter.world = world
-            scatter.head_offset = layout.q_lo[rank]
-            acc = 0
-            for p in range(world):
-                scatter.row_start[p] = acc
-                acc += rows[p]
-                scatter.out[p] = pg.peer(p, s, "land")
-                scatter.strides[p][0] = heads * dim
-                scatter.strides[p][1] = dim
-                scatter.strides[p][2] = rows[p] * heads * dim
-            scatter.row_start[world] = acc
-            step.attend(
-                pg.view(s, "q", query.dtype)[: total * batch * qn * dim],
-                pg.view(s, "k", query.dtype)[: total * batch * kvn * dim],
-                pg.view(s, "v", query.dtype)[: total * batch * kvn * dim],
-                None, causal, scale, scatter=scatter,
-            )
+        lg.run("attend", call, stream)
         last = _Clock.mark(query)
-        pg.signal(peer.OUT, seq)
-        pg.wait(peer.OUT, seq, status)
-        out = torch.empty((batch, mine, heads, dim), dtype=query.dtype, device=device)
-        land = pg.view(s, "land", query.dtype)[: batch * mine * heads * dim]
-        out.copy_(land.view(batch, mine, heads, dim))
+        lg.run("end", call, stream)
+    del keep
+    step = RankStep(query, key, value, layout, rank)
     _CLOCK.add((began, first, last, _Clock.mark(query)), step.moved())
     return out
 

@@ -330,6 +330,83 @@ COZY_API int cozy_peer_signal(const CozyPeerSlots* slots, long long seq, uintptr
 COZY_API int cozy_peer_wait(const long long* flags, int count, long long seq, long long limit_ns,
                             int* status, uintptr_t stream);
 
+/* ------------------------------------------------------------ the whole layer (one node)
+ * One rank's group: what it maps for a Ulysses attention layer between the GPUs of one node —
+ * receive and landing buffers (two sets, by call parity), arrival flags, a staging buffer for
+ * the blocks it sends, the attention's split workspace — and a side stream for its copies.
+ * Formed once per group and grown when a larger layer comes; no layer call allocates. Replaces
+ * the reference's exchange (src/cozy_runtime/internal/parallel/ulysses.py:607-766) with its
+ * group formation and mapped copy-engine buffers (copy_engine.py:408-449), for callers that run
+ * the layer without Python.
+ *
+ * Formation (every rank of the group, together):
+ *   cozy_group_create(rank, world, &g) on the rank's device (current);
+ *   cozy_group_needs(g, &shape, &grow): whether the buffers must grow for this shape (all ranks
+ *     answer alike); when they must: synchronize every rank's device and meet (a barrier over
+ *     the caller's channel), then cozy_group_reserve(g, &shape, blob) (cozy_group_blob_bytes()
+ *     bytes of IPC handles), exchange the blobs (all-gather, rank order) and cozy_group_open(g,
+ *     blobs).
+ * A call: cozy_ulysses_layer_fwd(g, &call, stream) on every rank; no other collective.
+ * Errors: cudaError_t values; a wait on a peer that runs past call.wait_limit_ns sets *status
+ * to 2 and the rank publishes nothing more. cozy_group_destroy releases everything (after the
+ * group's last call on every rank). */
+typedef struct CozyGroup CozyGroup;
+
+typedef struct CozyLayerShape {
+  int world;
+  int rows[COZY_MAX_PEERS]; /* every rank's sequence rows, in rank order */
+  int batch, heads_q, heads_kv, head_dim, causal;
+} CozyLayerShape;
+
+typedef struct CozyLayerCall {
+  CozyLayerShape shape;
+  /* this rank's rows [batch, rows[rank], heads, head_dim] bf16, element strides {seq, head,
+   * batch} (each a multiple of 8); K and V have heads_kv heads */
+  const void* q;
+  const void* k;
+  const void* v;
+  long long q_strides[3], k_strides[3], v_strides[3];
+  void* out; /* [batch, rows[rank], heads_q, head_dim] bf16, contiguous */
+  float scale; /* 0: 1/sqrt(head_dim) */
+  const CozyRope* rope; /* NULL: no RoPE; else tables over the whole sequence (token0 ignored) */
+  int norm_q, norm_k;   /* per-head RMSNorm of Q / K before RoPE */
+  const float* norm_q_weight;
+  const float* norm_k_weight; /* NULL: unit weight */
+  float norm_offset[2];       /* Q, K: weight + offset multiplies the normalised row */
+  float norm_eps[2];          /* Q, K */
+  long long wait_limit_ns; /* the longest a wait on another rank may take (0: 10 s) */
+  int* status;             /* device status word (0 = fine) */
+} CozyLayerCall;
+
+COZY_API int cozy_group_create(int rank, int world, CozyGroup** group);
+COZY_API int cozy_group_destroy(CozyGroup* group);
+COZY_API int cozy_group_blob_bytes(void);
+COZY_API int cozy_group_needs(const CozyGroup* group, const CozyLayerShape* shape, int* grow);
+COZY_API int cozy_group_reserve(CozyGroup* group, const CozyLayerShape* shape, void* blob);
+COZY_API int cozy_group_open(CozyGroup* group, const void* blobs);
+/* One process holding every rank of a group on one GPU (tests): mark each group local before
+ * its first reserve (blob may then be NULL), then connect them instead of opening blobs. */
+COZY_API int cozy_group_make_local(CozyGroup* group);
+COZY_API int cozy_group_connect_local(CozyGroup* const* groups, int world);
+/* How arrival flags cross: 1 = a stream memory write (cuStreamWriteValue64, fenced), 2 = a copy
+ * of a pinned host word behind the blocks on the same stream. */
+COZY_API int cozy_group_flag_mode(const CozyGroup* group);
+/* The last call number rank `src` published to this rank (kind 0: its Q/K/V blocks landed;
+ * kind 1: its output rows landed); a synchronous read, for monitoring and tests. */
+COZY_API int cozy_group_flag(const CozyGroup* group, int kind, int src, long long* value);
+
+/* The layer: cozy_ulysses_layer_fwd = begin (first stage, copies and flags to every rank),
+ * attend (the attention, waiting per source inside the kernel, output rows stored into their
+ * owners' landing buffers; then "landed" flags), end (bounded wait for every rank's rows, copy
+ * into out). The phases exist separately so one process can simulate all ranks on one GPU
+ * (every rank's begin, then every rank's attend, then every rank's end). */
+COZY_API int cozy_ulysses_layer_fwd(CozyGroup* group, const CozyLayerCall* call, uintptr_t stream);
+COZY_API int cozy_ulysses_layer_begin(CozyGroup* group, const CozyLayerCall* call,
+                                      uintptr_t stream);
+COZY_API int cozy_ulysses_layer_attend(CozyGroup* group, const CozyLayerCall* call,
+                                       uintptr_t stream);
+COZY_API int cozy_ulysses_layer_end(CozyGroup* group, const CozyLayerCall* call, uintptr_t stream);
+
 /* Name of a code returned above (a cudaError_t, or one of this library's). */
 COZY_API const char* cozy_error_name(int code);
 
