@@ -80,28 +80,24 @@ def make_rope(cfg: dict):
     return rope.llama(cfg["seq"], cfg["dim"], cfg["rope"][1])
 
 
-#: A timed region at least this long runs under the power cap: its kernels are held to the
-#: sustained peak (a cuBLAS GEMM looped for seconds), shorter ones to the burst peak.
-SUSTAINED_AFTER_S = 0.2
+#: A kernel is held to the sustained peak (a cuBLAS GEMM looped for seconds under the power cap)
+#: only when a single step runs at least this long; shorter steps are held to the burst peak.
+SUSTAINED_STEP_S = 1.0
 
 
-def peaks(fp8: bool = False, sustained: bool = False) -> tuple[float, float, str]:
-    """The tensor roofline denominator (and the burst figure beside it). Burst for a kernel
-    timed alone, sustained for one timed inside a long run of steps, as MEASURED_PEAKS.json
-    gives both. FP8 has no measured figure on this pool: twice the measured bf16 figure (the
-    dense e4m3:bf16 ratio of the part), labelled as such."""
+def peaks(fp8: bool = False) -> tuple[float, float, str]:
+    """The tensor roofline denominators (burst, sustained) from MEASURED_PEAKS.json, and their
+    source. FP8 has no measured figure on this pool: twice the measured bf16 figure (the dense
+    e4m3:bf16 ratio of the part), labelled as such."""
     path = ROOT / "MEASURED_PEAKS.json"
     mult, what = (2.0, "2 x ") if fp8 else (1.0, "")
     if path.exists():
         data = json.loads(path.read_text())
         burst = float(data["bf16_tflops"])
         held = float(data.get("bf16_tflops_sustained", burst))
-        if sustained and "bf16_tflops_sustained" in data:
-            return (mult * held, mult * burst,
-                    f"{what}measured bf16 sustained (MEASURED_PEAKS.json bf16_tflops_sustained; "
-                    f"timed region >= {SUSTAINED_AFTER_S} s under the power cap)")
-        return mult * burst, mult * burst, f"{what}measured bf16 burst (MEASURED_PEAKS.json bf16_tflops)"
-    return mult * FALLBACK_BF16_TFLOPS, mult * FALLBACK_BF16_TFLOPS, f"{what}fallback bf16"
+        return mult * burst, mult * held, f"{what}measured bf16 (MEASURED_PEAKS.json)"
+    return (mult * FALLBACK_BF16_TFLOPS, mult * FALLBACK_BF16_TFLOPS,
+            f"{what}fallback bf16 (MEASURED_PEAKS.json absent)")
 
 
 class NvmlSampler:
@@ -282,23 +278,82 @@ def cpu_baseline(cfg: dict, budget_s: float = 12.0) -> dict:
     }
 
 
+def _reference_rank(rank, world, port, cfg, steps, warmup, threads, sample_seq, outdir):
+    """One gloo process of the reference arm: the reference's CPU path for a layer, restated by
+    the oracle (`exchange_group`: its collectives included, torch SDPA in bf16 as `compute`),
+    on this rank's rows of a sampled layer; writes every step's time (max over ranks)."""
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    import oracle
+
+    torch.set_num_threads(threads)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=timedelta(seconds=900))
+    rows = oracle.sequence_rows(sample_seq, world)
+    gen = torch.Generator().manual_seed(100 + rank)
+    b, d, amp = cfg["batch"], cfg["dim"], cfg["amp"]
+    q, k, v = ((torch.randn(b, rows[rank], world, d, generator=gen) * amp).to(torch.bfloat16)
+               for _ in range(3))
+
+    def compute(qq, kk, vv):
+        return oracle.attention_fp32(qq, kk, vv, causal=cfg["causal"],
+                                     dtype=torch.bfloat16).to(torch.bfloat16)
+
+    times = []
+    for i in range(warmup + steps):
+        dist.barrier()
+        began = time.perf_counter()
+        oracle.exchange_group(q, k, v, dist.group.WORLD, compute)
+        took = torch.tensor([time.perf_counter() - began], dtype=torch.float64)
+        dist.all_reduce(took, op=dist.ReduceOp.MAX)
+        if i >= warmup:
+            times.append(took.item())
+    if rank == 0:
+        Path(outdir, "times.json").write_text(json.dumps(times))
+    dist.destroy_process_group()
+
+
 def run_reference(args, cfg) -> None:
-    """`--impl reference`: the reference's CPU path for this layer (no GPU), rank 0 only."""
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
+    """`--impl reference`: the reference's CPU path for this layer (the oracle's restatement of
+    its exchange over gloo, torch SDPA as compute) on the box's host cores, as W = --gpus gloo
+    processes; rank 0 of a torchrun launch alone runs it. Each step is a bounded sample: one
+    head a process over a sequence of at most 8192 tokens (SDPA's rate does not depend on the
+    length at these sizes), whole exchanges timed as the max over processes; `value` is the
+    sample's TFLOP/s, `ms_per_step` the whole layer's FLOPs at that rate."""
+    import socket
+    import tempfile
+
+    import torch.multiprocessing as mp
+
+    if int(os.environ.get("RANK", "0")) != 0:
         return
-    samples = []
-    for i in range(args.warmup + args.steps):
-        base = cpu_baseline(cfg, budget_s=max(1.0, 60.0 / (args.steps + args.warmup)))
-        if i >= args.warmup:
-            samples.append(base)
-    value = statistics.median(s["value"] for s in samples)
+    world = max(1, args.gpus)
+    cores = os.cpu_count() or 1
+    threads = max(1, cores // world)
+    sample_seq = min(cfg["seq"], 8192)
+    with socket.socket() as sock:
+        sock.bind(("127.0.0.1", 0))
+        port = sock.getsockname()[1]
+    with tempfile.TemporaryDirectory() as tmp:
+        mp.spawn(_reference_rank, args=(world, port, cfg, args.steps, args.warmup, threads,
+                                        sample_seq, tmp), nprocs=world, join=True)
+        times = json.loads(Path(tmp, "times.json").read_text())
+    step_s = statistics.median(times)
+    sample = dict(cfg, seq=sample_seq, heads=world, heads_kv=world)
+    value = layer_flops(sample) / step_s / 1e12
     flops = layer_flops(cfg)
-    base = samples[-1]
+    kind_note = (f"{world} gloo processes x {threads} threads ({world * threads} of {cores} host "
+                 f"threads), one head a process over {sample_seq} tokens (of {cfg['seq']}), "
+                 f"the oracle's restatement of the reference's exchange (all-to-all over gloo, "
+                 f"torch SDPA in bf16), median of {len(times)} steps of {step_s:.3f} s "
+                 f"(max over processes); RoPE/RMSNorm not included")
     line = {
         "impl": "reference",
         "metric": METRIC,
-        "value": value,
+        "value": round(value, 5),
         "unit": "TFLOP/s",
         "n_gpus": args.gpus,
         "steps": args.steps,
@@ -307,14 +362,164 @@ def run_reference(args, cfg) -> None:
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
-        "dtype": "fp32",
+        "dtype": "bf16",
         "data": "synthetic",
-        "config": {"workload": cfg["workload"], "parallelism": "cpu", "sampled": True},
-        "cpu_baseline": {**base, "value": value},
-        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+        "config": {"workload": cfg["workload"], "parallelism": f"gloo{world} (cpu)",
+                   "sampled": True},
+        "cpu_baseline": {"value": round(value, 5), "unit": "TFLOP/s", "cores": world * threads,
+                         "kind": "port", "sample": kind_note},
+        "e2e": {"value": round(value, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def first_law_fp32(x, spec, norm: bool, token0: int):
+    """The first stage's RMSNorm (unit weight, eps 1e-6) and RoPE in fp32 torch on the GPU: the
+    plain PyTorch reference the parity check holds the layer to. x: [B, S, H, D]."""
+    import torch
+
+    y = x.float()
+    if norm:
+        y = y * torch.rsqrt(y.pow(2).mean(-1, keepdim=True) + 1e-6)
+    if spec is None:
+        return y
+    seq, rot = y.shape[1], spec.rotary
+    tok = torch.arange(token0, token0 + seq, device=y.device)
+    cos, sin = spec.cos.reshape(-1), spec.sin.reshape(-1)
+    out = y.clone()
+    if spec.interleaved:
+        col = torch.arange(rot // 2, device=y.device) * spec.stride_channel
+        idx = tok[:, None] * spec.stride_token + col[None, :]
+        c, sn = cos[idx][None, :, None, :], sin[idx][None, :, None, :]
+        lo, hi = y[..., 0:rot:2], y[..., 1:rot:2]
+        out[..., 0:rot:2] = lo * c - hi * sn
+        out[..., 1:rot:2] = hi * c + lo * sn
+    else:
+        half = rot // 2
+        col = torch.arange(rot, device=y.device) * spec.stride_channel
+        idx = tok[:, None] * spec.stride_token + col[None, :]
+        c, sn = cos[idx][None, :, None, :], sin[idx][None, :, None, :]
+        lo, hi = y[..., :half], y[..., half:rot]
+        out[..., :half] = lo * c[..., :half] - hi * sn[..., :half]
+        out[..., half:rot] = hi * c[..., half:] + lo * sn[..., half:]
+    return out
+
+
+def parity_check(q, k, v, out, rows, rank, group, cfg, spec, device) -> dict:
+    """One step's output on every rank against fp32 attention computed on that rank's GPU: three
+    query heads, up to 512 of this rank's rows (its first and last 256), the keys and values of
+    the whole sequence gathered from every rank. The path's bf16 bar: max-abs ≤ 2e-2, mean-abs
+    ≤ 2e-3 (max over ranks)."""
+    import torch
+    import torch.distributed as dist
+
+    heads, hkv = cfg["heads"], cfg["heads_kv"]
+    grouping = heads // hkv
+    pick = sorted({0, heads // 2, heads - 1})
+    kv_pick = sorted({h // grouping for h in pick})
+    start, mine = sum(rows[:rank]), rows[rank]
+    kx = first_law_fp32(k[:, :, kv_pick], spec, cfg["norm"], start)
+    vx = v[:, :, kv_pick].float()
+    if group is not None:
+        # every rank's rows of these heads (uneven rows: padded to the largest, then cropped)
+        most = max(rows)
+        pad = torch.zeros(kx.shape[0], most, len(kv_pick), kx.shape[3], device=device)
+        kk, vv = pad.clone(), pad.clone()
+        kk[:, :mine], vv[:, :mine] = kx, vx
+        ks, vs = [torch.empty_like(kk) for _ in rows], [torch.empty_like(vv) for _ in rows]
+        dist.all_gather(ks, kk, group=group)
+        dist.all_gather(vs, vv, group=group)
+        kx = torch.cat([t[:, :n] for t, n in zip(ks, rows, strict=True)], dim=1)
+        vx = torch.cat([t[:, :n] for t, n in zip(vs, rows, strict=True)], dim=1)
+    sel = torch.arange(mine, device=device)
+    if mine > 512:
+        sel = torch.cat([sel[:256], sel[-256:]])
+    worst, total, count = 0.0, 0.0, 0
+    for h in pick:
+        qx = first_law_fp32(q[:, :, [h]], spec, cfg["norm"], start)[:, sel]
+        kvh = kv_pick.index(h // grouping)
+        for b in range(q.shape[0]):
+            sc = (qx[b, :, 0] @ kx[b, :, kvh].T) / (q.shape[3] ** 0.5)
+            if cfg["causal"]:
+                cols = torch.arange(kx.shape[1], device=device)
+                sc = sc.masked_fill(cols[None, :] > (start + sel)[:, None], float("-inf"))
+            want = torch.softmax(sc, dim=-1) @ vx[b, :, kvh]
+            err = (out[b, sel, h].float() - want).abs()
+            worst = max(worst, err.max().item())
+            total += err.sum().item()
+            count += err.numel()
+    stats = torch.tensor([worst, total / max(count, 1)], dtype=torch.float64, device=device)
+    if group is not None:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX, group=group)
+    worst, mean = stats.tolist()
+    return {"max_abs": round(worst, 5), "mean_abs": round(mean, 6),
+            "ok": bool(worst <= 2e-2 and mean <= 2e-3),
+            "checked": f"heads {pick}, up to 512 rows a rank, vs fp32 torch on the GPU"}
+
+
+def attention_alone(cfg, layout, rank, steps, device) -> float:
+    """ms per launch of this rank's attention with every operand resident (no crossing): the
+    same kernel and shapes as inside the layer, on [B, S, heads, D] operands."""
+    import torch
+
+    from cozy_runtime_b200 import attention
+
+    qn, kvn = layout.q_n[rank], layout.kv_n[rank]
+    if qn == 0:
+        return 0.0
+    total, b, d = layout.total, cfg["batch"], cfg["dim"]
+    gen = torch.Generator(device=device).manual_seed(7)
+    q = torch.randn(b, total, qn, d, generator=gen, device=device).to(torch.bfloat16)
+    k = torch.randn(b, total, kvn, d, generator=gen, device=device).to(torch.bfloat16)
+    v = torch.randn(b, total, kvn, d, generator=gen, device=device).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    head_map = (layout.group, layout.q_lo[rank], layout.kv_lo[rank])
+    for _ in range(2):
+        attention.attention_into(out, q, k, v, causal=cfg["causal"], head_map=head_map)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        attention.attention_into(out, q, k, v, causal=cfg["causal"], head_map=head_map)
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def cudnn_attention(cfg, layout, rank, device) -> dict | None:
+    """torch SDPA on cuDNN alone (the reference's B200 bf16 row, attention_upstream.py:191-215)
+    on this rank's per-GPU shape, CUDA events, 5 launches after 2."""
+    import torch
+    import torch.nn.functional as F
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    qn, total, b, d = layout.q_n[rank], layout.total, cfg["batch"], cfg["dim"]
+    if qn == 0:
+        return None
+    kvn = max(1, qn // layout.group)
+    gen = torch.Generator(device=device).manual_seed(9)
+    q = torch.randn(b, qn, total, d, generator=gen, device=device).to(torch.bfloat16)
+    k = torch.randn(b, kvn, total, d, generator=gen, device=device).to(torch.bfloat16)
+    v = torch.randn(b, kvn, total, d, generator=gen, device=device).to(torch.bfloat16)
+    try:
+        with sdpa_kernel([SDPBackend.CUDNN_ATTENTION]):
+            def call():
+                return F.scaled_dot_product_attention(q, k, v, is_causal=cfg["causal"],
+                                                      enable_gqa=kvn != qn)
+            for _ in range(2):
+                call()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(5):
+                call()
+            e1.record()
+            torch.cuda.synchronize()
+    except Exception as exc:  # noqa: BLE001 - reported, not fatal
+        return {"unavailable": str(exc)[:200]}
+    ms = e0.elapsed_time(e1) / 5
+    return {"ms": round(ms, 4), "tflops": round(layer_flops(cfg, heads=qn) / ms / 1e9, 1),
+            "heads": qn, "seq": total, "layout": "[B, H, S, D] contiguous",
+            "call": "torch SDPA, SDPBackend.CUDNN_ATTENTION only"}
 
 
 def main() -> None:
@@ -326,6 +531,10 @@ def main() -> None:
     parser.add_argument("--impl", default="cozy", choices=["cozy", "reference"])
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
+    parser.add_argument("--no-extras", action="store_true",
+                        help="skip the parity check, attention-alone, cuDNN and long-run legs")
+    parser.add_argument("--long-run-s", type=float, default=0.5,
+                        help="after the timed steps, steps until this long has passed (clocks)")
     parser.add_argument("--narrow", action="store_true",
                         help="the int8 wire (exchange(..., narrow=True)); not the headline")
     parser.add_argument("--heads", type=int, default=0,
@@ -398,24 +607,72 @@ def main() -> None:
     with sampler:
         e0.record()
         for _ in range(args.steps):
-            step(q, k, v)
+            out = step(q, k, v)
         e1.record()
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
     clock = ulysses.taken()
     attention.check_status(device)
-    attn_ms = clock["attention_ms"] / max(1, clock["calls"])
     layout = ulysses.plan(rows, heads, hkv)
-    my_flops = layer_flops(cfg, heads=layout.q_n[rank])
     calls = max(1, clock["calls"])
-    stats = torch.tensor([ms, attn_ms, clock["exposed_ms"] / calls, clock["before_ms"] / calls,
-                          clock["after_ms"] / calls], dtype=torch.float64, device=device)
-    achieved = torch.tensor([my_flops / (attn_ms * 1e-3) / 1e12 if attn_ms else 0.0],
-                            dtype=torch.float64, device=device)
+    attn_span = clock["attention_ms"] / calls
+    stats = torch.tensor([ms, attn_span, clock["before_ms"] / calls, clock["after_ms"] / calls],
+                         dtype=torch.float64, device=device)
     if group is not None:
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
-        dist.all_reduce(achieved, op=dist.ReduceOp.MIN)
-    ms_max, attn_max, exposed_max, before_max, after_max = stats.tolist()
+    ms_max, span_max, before_max, after_max = stats.tolist()
+
+    # ---- outside the timed region: the output checked, the attention alone, cuDNN, clocks
+    extras: dict = {}
+    if not args.no_extras and not fp8 and not args.narrow:
+        extras["parity"] = parity_check(q, k, v, out, rows, rank, group, cfg, spec, device)
+        alone = torch.tensor([attention_alone(cfg, layout, rank, max(3, args.steps // 4),
+                                              device)], dtype=torch.float64, device=device)
+        if group is not None:
+            dist.all_reduce(alone, op=dist.ReduceOp.MAX)
+        extras["attention_alone_ms"] = alone.item()
+        if rank == 0:
+            extras["cudnn"] = cudnn_attention(cfg, layout, rank, device)
+    long_run = None
+    if not args.no_extras and args.long_run_s > 0:
+        # more steps until long_run_s has passed, each timed on the device: the median step and
+        # the clocks of a timed region long enough to be steady
+        if group is not None:
+            dist.barrier()
+        sampler_long = clock_sampler(local_gpu_index(local)) if rank == 0 else NullSampler()
+        marks = []
+        began = time.perf_counter()
+        with sampler_long:
+            while True:
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                step(q, k, v)
+                b.record()
+                marks.append((a, b))
+                if len(marks) % 8 == 0:
+                    torch.cuda.synchronize()
+                    go = torch.tensor([time.perf_counter() - began < args.long_run_s],
+                                      dtype=torch.int32, device=device)
+                    if group is not None:  # every rank runs the same number of steps
+                        dist.all_reduce(go, op=dist.ReduceOp.MIN)
+                    if not go.item():
+                        break
+            torch.cuda.synchronize()
+        per = torch.tensor([statistics.median(a.elapsed_time(b) for a, b in marks)],
+                           dtype=torch.float64, device=device)
+        if group is not None:
+            dist.all_reduce(per, op=dist.ReduceOp.MAX)
+        attention.check_status(device)
+        ulysses.taken()
+        long_run = {"steps": len(marks), "seconds": round(time.perf_counter() - began, 3),
+                    "median_step_ms": round(per.item(), 4), "clocks": sampler_long.summary()}
+
+    transport = ulysses.transport_of(group, device)
+    flag_mode = None
+    if transport == "peer":
+        from cozy_runtime_b200 import peer
+
+        flag_mode = peer.layer_group_for(group, device).flag_mode()
 
     # ---- end to end through the public call, host buffers in and out every step
     e2e_ms = h2d = d2h = None
@@ -443,12 +700,12 @@ def main() -> None:
         def run_step(i):
             s = i % 2
             compute.wait_event(loaded[s])
-            out = step(*slots[s])
+            result = step(*slots[s])
             freed[s].record(compute)
             d2h_stream.wait_event(freed[s])
             with torch.cuda.stream(d2h_stream):
-                host_outs[s].copy_(out, non_blocking=True)
-            out.record_stream(d2h_stream)
+                host_outs[s].copy_(result, non_blocking=True)
+            result.record_stream(d2h_stream)
 
         def e2e_run(n):
             for ev in freed:
@@ -480,20 +737,31 @@ def main() -> None:
 
     flops = layer_flops(cfg)
     if rank == 0:
-        timed_s = ms_max * args.steps / 1e3
-        peak, burst, peak_src = peaks(fp8, sustained=timed_s >= SUSTAINED_AFTER_S)
-        ach = achieved.item()
+        burst, held, peak_src = peaks(fp8)
+        sustained = ms_max / 1e3 >= SUSTAINED_STEP_S
+        peak = held if sustained else burst
+        my_flops = layer_flops(cfg, heads=layout.q_n[rank])
+        alone_ms = extras.get("attention_alone_ms")
+        # the dominant kernel's rate: alone (every operand resident) where measured, else its
+        # span inside the layer (which includes waiting for rows still crossing)
+        kernel_ms = alone_ms if alone_ms else span_max
+        ach = my_flops / (kernel_ms * 1e-3) / 1e12 if kernel_ms else 0.0
         # my kernels a step: first stage + attention, then per transport the land (NCCL) or
-        # two signal and two wait kernels (peer); FP8 adds the statistics kernel
-        transport = os.environ.get("COZY_ULYSSES_TRANSPORT", "peer")
-        per_step = 2 + (0 if world == 1 else (1 if transport == "nccl" else 4)) + (1 if fp8 else 0)
+        # a signal and a wait kernel (peer: the crossing is copy engines and stream writes); FP8
+        # adds the statistics kernel
+        kernels = 1 + (1 if (cfg["rope"] or cfg["norm"] or world > 1) else 0)
+        if world > 1:
+            kernels += {"peer": 2, "nccl": 1}.get(transport, 0)
+        if fp8:
+            kernels += 1 + (2 if world > 1 else 0)
         if args.narrow:  # key sums, shift, pack, 3 widens, attention, return pack, land widen
-            per_step = 9 + (2 if cfg["rope"] or cfg["norm"] else 0) + (
+            kernels = 9 + (2 if cfg["rope"] or cfg["norm"] else 0) + (
                 4 if world > 1 and transport == "peer" else 0)
         profile = ROOT / "profiles" / f"attention_fwd_{args.config}_traffic.json"
         traffic = None
         if profile.exists():
             traffic = json.loads(profile.read_text()).get("dram_bytes_per_launch")
+        exposed = ms_max - (alone_ms if alone_ms else span_max)
         line = {
             "metric": METRIC,
             "value": round(flops / (ms_max * 1e-3) / 1e12, 2),
@@ -521,16 +789,21 @@ def main() -> None:
                 "wire": "int8 (narrow)" if args.narrow else ("e4m3" if fp8 else "bf16"),
                 "l2": "inputs larger than L2 (no flush)",
             },
+            "transport": transport,
+            "flag_mode": flag_mode,
             "layer": {
-                "attention_ms": round(attn_max, 4),
-                "exposed_ms": round(exposed_max, 4),
-                "exposed_frac": round(exposed_max / ms_max, 4) if ms_max else None,
-                # exposed before the attention (first stage, crossing, arrival flags) and after
-                # it (return flags, copy out), each the max over ranks
+                "attention_span_ms": round(span_max, 4),
+                "attention_alone_ms": None if alone_ms is None else round(alone_ms, 4),
+                # exposed = layer - the attention alone: the crossing, first stage, flags and
+                # copy-out that did not hide under the attention (max over ranks of each)
+                "exposed_ms": round(exposed, 4),
+                "exposed_frac": round(exposed / ms_max, 4) if ms_max else None,
                 "before_attention_ms": round(before_max, 4),
                 "after_attention_ms": round(after_max, 4),
             },
+            "parity": extras.get("parity"),
             "clocks": sampler.summary(),
+            "long_run": long_run,
             "e2e": None if e2e_ms is None else {
                 "value": round(flops / (e2e_ms.item() * 1e-3) / 1e12, 2),
                 "unit": "TFLOP/s",
@@ -542,18 +815,22 @@ def main() -> None:
                 "step i's compute (double-buffered inputs); every step's copies inside the "
                 "timed region",
             },
-            "gpu_launches": per_step * args.steps,
+            "gpu_launches": kernels * args.steps,
             "roofline": {
                 "bound": "tensor",
                 "kernel": f"attention_fwd_kernel<128, {'true' if fp8 else 'false'}>",
                 "achieved": round(ach, 2),
                 "peak": peak,
                 "unit": "TFLOP/s",
-                "frac": round(ach / peak, 4),
-                "peak_source": peak_src,
-                "frac_of_burst": round(ach / burst, 4),
+                "frac": round(ach / peak, 4) if peak else None,
+                "peak_source": peak_src + (" sustained (steps of 1 s or more)" if sustained
+                                           else " burst"),
+                "frac_of_sustained": round(ach / held, 4) if held else None,
+                "measured_on": "the attention alone, operands resident" if alone_ms
+                else "the attention's span inside the layer",
                 "traffic": traffic,
             },
+            "cudnn": extras.get("cudnn"),
         }
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(cfg)

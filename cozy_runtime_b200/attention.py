@@ -36,6 +36,58 @@ def check_status(device: torch.device) -> None:
         raise RuntimeError(f"attention kernel reported: {_lib.STATUS_NAMES.get(word, word)}")
 
 
+class _Watch:
+    """A watch on a device's status word that never synchronizes: after each call the word is
+    copied into pinned host memory behind the call's work; the next call reads it once that copy
+    has completed (an event query) and raises if a wait timed out."""
+
+    def __init__(self) -> None:
+        self.host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self.event: torch.cuda.Event | None = None
+
+    def after(self, word: Tensor, stream: torch.cuda.Stream) -> None:
+        with torch.cuda.stream(stream):
+            self.host.copy_(word, non_blocking=True)
+        self.event = torch.cuda.Event()
+        self.event.record(stream)
+
+    def failed(self) -> int:
+        if self.event is None or not self.event.query():
+            return 0
+        return int(self.host[0])
+
+
+_WATCHES: dict[int, _Watch] = {}
+
+
+def watch_after_call(device: torch.device) -> None:
+    """Queue the copy of `device`'s status word behind the call just enqueued (no sync)."""
+    if torch.cuda.is_current_stream_capturing():
+        return
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    watch = _WATCHES.get(index)
+    if watch is None:
+        watch = _WATCHES[index] = _Watch()
+    watch.after(status_word(device), torch.cuda.current_stream(device))
+
+
+def raise_if_failed(device: torch.device) -> None:
+    """Raise if an earlier call on `device` reported a timed-out wait, as far as the watch has
+    seen without synchronizing (the reference raises after any failure of an exchange,
+    src/cozy_runtime/internal/parallel/ulysses.py:754-758). The word is cleared, so the error is
+    raised once."""
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    watch = _WATCHES.get(index)
+    word = watch.failed() if watch is not None else 0
+    if word:
+        watch.host.zero_()
+        watch.event = None
+        status_word(device).zero_()
+        raise RuntimeError(
+            f"an earlier attention call on {device} reported: {_lib.STATUS_NAMES.get(word, word)}"
+        )
+
+
 def _strides(t: Tensor) -> ctypes.Array:
     """Element strides {seq, head, batch} of a [batch, seq, heads, dim] view."""
     if t.stride(3) != 1:
@@ -113,8 +165,10 @@ def forward(
     why = refusal(query, key, {"attn_mask": attn_mask, "dropout_p": dropout_p})
     if why:
         raise ValueError(f"cozy-b200 attention: {why}")
+    raise_if_failed(query.device)
     out = torch.empty(query.shape, dtype=query.dtype, device=query.device)
     attention_into(out, query, key, value, causal=is_causal, scale=scale)
+    watch_after_call(query.device)
     return out
 
 

@@ -92,7 +92,7 @@ struct AttentionParams {
   // Walk orders. Query blocks run from q_turn downwards, cyclically (q_turn = q_blocks - 1: the
   // last block first, which for causal calls is the heaviest); each tile's key blocks run from
   // kv_turn downwards, cyclically (kv_turn < 0: upwards from block 0).
-  int q_turn, kv_turn;
+  int q_turn, kv_turn, q_seg;
   // Rows still crossing from other GPUs: rows [src_start[s], src_start[s + 1]) come from source
   // s, resident once arrive[s] (a flag in this GPU's memory the source writes) reaches
   // arrive_seq; the producer waits for a source's flag before its first load of that source's
@@ -104,10 +104,26 @@ struct AttentionParams {
   int src_start[COZY_MAX_PEERS + 1];
 };
 
-// The query block of tile index t (q_turn downwards, cyclically).
-__device__ __forceinline__ int tile_qblock(const AttentionParams& p, int t) {
-  int qb = p.q_turn - t % p.q_blocks;
-  return qb < 0 ? qb + p.q_blocks : qb;
+// Tile index t -> (query block, head, batch). The query blocks are taken in walk order (from
+// q_turn downwards, cyclically) in segments of q_seg blocks: every (head, batch) takes the
+// first segment's blocks, then every (head, batch) the next segment's, and so on, consecutive
+// tiles sharing a (head, batch) and with it their keys and values in L2. q_seg = q_blocks keeps
+// each (head, batch)'s blocks together; a smaller segment (the query blocks of one GPU's rows)
+// runs every head's resident rows before any rows still crossing.
+struct TileAt {
+  int qb, head, b;
+};
+
+__device__ __forceinline__ TileAt tile_at(const AttentionParams& p, int t) {
+  const int hb = p.heads_q * p.batch;
+  const int seg = t / (p.q_seg * hb);
+  const int first = seg * p.q_seg;
+  const int len = min(p.q_seg, p.q_blocks - first);
+  const int within = t - seg * p.q_seg * hb;
+  const int pair = within / len;
+  int qb = p.q_turn - (first + within % len);
+  if (qb < 0) qb += p.q_blocks;
+  return {qb, pair % p.heads_q, pair / p.heads_q};
 }
 
 // The key block of walk step i for a tile with n_blocks key blocks.
@@ -417,14 +433,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // Work unit -> tile (query block x, head, batch), x fastest; tile x takes query block
-  // tile_qblock(x) (for causal calls q_turn is the last block: heaviest first).
+  // Work unit -> tile -> (query block, head, batch); for causal calls the walk starts at the
+  // last query block: the heaviest tiles first.
   int part = -1, split_tile = 0;
   const int tile = SPLIT ? unit_tile(p, static_cast<int>(blockIdx.x), &part, &split_tile)
                          : static_cast<int>(blockIdx.x);
-  const int qb = tile_qblock(p, tile);
-  const int head = (tile / p.q_blocks) % p.heads_q;
-  const int b = tile / (p.q_blocks * p.heads_q);
+  const TileAt at = tile_at(p, tile);
+  const int qb = at.qb, head = at.head, b = at.b;
   const int kv_head = (head + p.q_base) / p.group - p.kv_base;
   const int q0 = qb * (kQTiles * kBlockM);
   int kv_end = p.seq_k;
@@ -617,10 +632,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     int part = -1, split_tile = 0;
     const int e_tile =
         SPLIT ? unit_tile(p, fresh_ctaid(), &part, &split_tile) : fresh_ctaid();
-    const int head = (e_tile / p.q_blocks) % p.heads_q;
-    const int b = e_tile / (p.q_blocks * p.heads_q);
+    const TileAt e_at = tile_at(p, e_tile);
+    const int head = e_at.head;
+    const int b = e_at.b;
     const int kv_head = (head + p.q_base) / p.group - p.kv_base;
-    const int q_row = tile_qblock(p, e_tile) * (kQTiles * kBlockM) +
+    const int q_row = e_at.qb * (kQTiles * kBlockM) +
                       e_s * kBlockM + quarter * 32 + e_lane;
     const uint32_t e_tO = *reinterpret_cast<volatile uint32_t*>(tmem_slot) +
                           (static_cast<uint32_t>(quarter * 32) << 16) + 256u +
@@ -1284,6 +1300,7 @@ static int attention_launch(const void* q, const void* k, const void* v, void* o
   }
   // walk orders: the last query block first; key blocks upwards
   p.q_turn = p.q_blocks - 1;
+  p.q_seg = p.q_blocks;
   p.kv_turn = -1;
   p.arrive = nullptr;
   p.arrive_seq = 0;
@@ -1311,7 +1328,12 @@ static int attention_launch(const void* q, const void* k, const void* v, void* o
     const int lo = arrival->src_start[arrival->self], hi = arrival->src_start[arrival->self + 1];
     if (hi > lo) {
       p.kv_turn = (hi - 1) / kBlockN;
-      if (!causal) p.q_turn = (hi - 1) / (kQTiles * kBlockM);
+      if (!causal) {
+        // every head's query blocks over this GPU's rows run first, then the next source's
+        const int rows_q = kQTiles * kBlockM;
+        p.q_turn = (hi - 1) / rows_q;
+        p.q_seg = min(p.q_blocks, max(1, (hi - 1) / rows_q - lo / rows_q + 1));
+      }
     }
   }
   p.q_scale = p.k_scale = p.v_scale = nullptr;

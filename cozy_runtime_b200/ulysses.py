@@ -479,6 +479,27 @@ def exchange(
     compute: Compute | None = None,
     site: str = "",
     narrow: bool | Callable[[int], bool] = False,
+    **options,
+) -> Tensor:
+    """Sequence shards -> whole sequences per head subset -> attention -> back (keywords: those
+    of `_exchange`). Raises when an earlier call on this device reported a timed-out wait, seen
+    without synchronizing: the status word is copied to the host behind every call."""
+    if query.is_cuda:
+        attention.raise_if_failed(query.device)
+    out = _exchange(query, key, value, handle, compute, site, narrow, **options)
+    if query.is_cuda:
+        attention.watch_after_call(query.device)
+    return out
+
+
+def _exchange(
+    query: Tensor,
+    key: Tensor,
+    value: Tensor,
+    handle,
+    compute: Compute | None = None,
+    site: str = "",
+    narrow: bool | Callable[[int], bool] = False,
     *,
     rows: Sequence[int] | None = None,
     causal: bool = False,
@@ -564,13 +585,12 @@ def exchange(
         )
     step = RankStep(query, key, value, layout, rank, rope=rope, norm_q=norm_q, norm_k=norm_k)
     step.pack()
-    crossed = False
-    try:
+    with _Crossing(handle) as crossing:
         if world == 1:
             q_recv, k_recv, v_recv = step.q_send, step.k_send, step.v_send
         else:
             q_recv, k_recv, v_recv = step.receive_buffers()
-            crossed = True
+            crossing.crossed = True
             dist.all_to_all_single(q_recv, step.q_send, step.q_in, step.q_sizes, group=handle)
             dist.all_to_all_single(k_recv, step.k_send, step.kv_in, step.kv_sizes, group=handle)
             dist.all_to_all_single(v_recv, step.v_send, step.kv_in, step.kv_sizes, group=handle)
@@ -586,10 +606,6 @@ def exchange(
             returned = torch.empty(sum(step.back_sizes), dtype=query.dtype, device=query.device)
             dist.all_to_all_single(returned, o_send, step.back_sizes, step.back_in, group=handle)
             out = step.land(returned)
-    except BaseException:
-        if crossed:
-            _abort(handle)
-        raise
     _CLOCK.add((began, first, last, _Clock.mark(query)), step.moved())
     return out
 
@@ -636,6 +652,19 @@ def _form_check(handle, device: torch.device) -> bool:
     agreed = torch.tensor([1 if ok else 0], dtype=torch.int32, device=device)
     dist.all_reduce(agreed, op=dist.ReduceOp.MIN, group=handle)
     return bool(agreed.item())
+
+
+def transport_of(handle, device: torch.device | None = None) -> str:
+    """Which transport `exchange` takes on `handle` with native attention: "local" (one rank),
+    "peer" (the NVLink layer, once its formation check passed) or "nccl"."""
+    if handle is None or dist.get_world_size(handle) == 1:
+        return "local"
+    if _transport(handle, None) != "peer":
+        return "nccl"
+    state = _FORMED.get(handle)
+    if state is None and device is not None:
+        state = _peer_ready(handle, device)
+    return "peer" if state is True else "nccl"
 
 
 def _transport(handle, asked: str | None) -> str:
@@ -795,10 +824,9 @@ def _exchange_narrow(
     step = narrow_mod.NarrowStep(query, key, value, layout, rank)
     k_sum = torch.zeros(batch, heads_kv, dim, dtype=torch.float32, device=device)
     narrow_mod.key_sum_into(key, k_sum)
-    crossed = False
-    try:
+    with _Crossing(handle) as crossing:
         if world > 1:
-            crossed = True
+            crossing.crossed = True
             dist.all_reduce(k_sum, op=dist.ReduceOp.SUM, group=handle)
         shift = step.shift(k_sum)
         qn, kvn = layout.q_n[rank], layout.kv_n[rank]
@@ -905,10 +933,6 @@ def _exchange_narrow(
                                    [z // dim for z in back_sizes], group=handle)
             returned = (codes, scales)
         out = step.land(*returned)
-    except BaseException:
-        if crossed:
-            _abort(handle)
-        raise
     _CLOCK.add((began, first_mark, last, _Clock.mark(query)), round(moved))
     return out
 
@@ -1019,10 +1043,37 @@ def _scatter(layout: Plan, rank: int, heads: int, dim: int, landing) -> _lib.Sca
 
 def _abort(handle) -> None:
     """After crossing began, a failing rank ends its group so peers blocked in collectives raise
-    (the reference's `abort_process_group`, ulysses.py:754-758)."""
+    (the reference's `abort_process_group`, src/cozy_runtime/internal/parallel/group.py:360-372,
+    called at ulysses.py:754-758): the group's own abort where its backend has one (NCCL), else
+    torch's process-group abort; a group without either (gloo) is left to its timeout, as in the
+    reference."""
     abort = getattr(handle, "abort", None)
-    if callable(abort):
-        try:
+    try:
+        if callable(abort):
             abort()
-        except Exception:  # noqa: BLE001 - the original error is what the caller sees
-            pass
+            return
+        import torch.distributed.distributed_c10d as c10d
+
+        whole = getattr(c10d, "_abort_process_group", None)
+        if whole is not None:
+            whole(handle)
+    except Exception:  # noqa: BLE001 - the original error is what the caller sees
+        pass
+
+
+class _Crossing:
+    """The part of an exchange after its first crossing began: an exception raised inside ends
+    the group before it propagates, so peers waiting in a collective raise instead of waiting
+    for this rank. `crossed` is set once the first crossing is under way."""
+
+    def __init__(self, handle) -> None:
+        self.handle = handle
+        self.crossed = False
+
+    def __enter__(self) -> _Crossing:
+        return self
+
+    def __exit__(self, kind, exc, tb) -> bool:
+        if kind is not None and self.crossed:
+            _abort(self.handle)
+        return False

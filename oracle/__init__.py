@@ -14,6 +14,7 @@ reference's own code (`tests/golden/make_golden.py`, fixtures `tests/golden/*.np
 from oracle.ulysses_oracle import (  # noqa: F401
     attention_fp32,
     exchange,
+    exchange_group,
     exchange_narrow,
     fp8_attention_law,
     head_norm_rope,

@@ -119,6 +119,67 @@ def exchange(
     return [whole[:, s : s + n] for s, n in zip(starts, rows, strict=True)]
 
 
+def exchange_group(
+    query: Tensor,
+    key: Tensor,
+    value: Tensor,
+    group,
+    compute: Callable[[Tensor, Tensor, Tensor], Tensor],
+) -> Tensor:
+    """One rank's part of the exchange over a real process group (gloo on CPU): the reference's
+    own CPU path for a layer, collectives included.
+
+    Restates src/cozy_runtime/internal/parallel/ulysses.py:633-766 (`_exchange`) with its
+    crossings: every rank's rows agreed over the group (the meeting, :89-133), heads padded to a
+    multiple of W (:647), this rank's rows of each peer's `local` heads sent as one stacked
+    [Q; K; V] block per peer by `all_to_all_single` (`_pack`/`_send`, :325-417), the whole
+    sequence unpacked in rank order (:420-432), `compute` on [B, S, local, D], the attended
+    rows sent back to their owners (`_returned`, :459-502), landed (:435-457) and cropped
+    (:766). Grouped K/V heads cross replicated to the query heads they serve. Returns this
+    rank's [B, S_r, H, D] output.
+    """
+    import torch.distributed as dist
+
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    batch, mine, heads, dim = (int(n) for n in query.shape)
+    group_size = heads // int(key.shape[2])
+    counts = [torch.zeros(1, dtype=torch.int64) for _ in range(world)]
+    dist.all_gather(counts, torch.tensor([mine], dtype=torch.int64), group=group)
+    rows = [int(c.item()) for c in counts]
+    total = sum(rows)
+    k = key.repeat_interleave(group_size, dim=2)
+    v = value.repeat_interleave(group_size, dim=2)
+    padded = heads_padded(heads, world)
+    q = query
+    if padded != heads:
+        pad = (0, 0, 0, padded - heads)
+        q, k, v = (torch.nn.functional.pad(t, pad) for t in (q, k, v))
+    local = padded // world
+    # send: for peer p, [3][S_r][B][local][D] of heads [p·local, (p+1)·local)
+    stacked = torch.stack((q, k, v))  # [3, B, S_r, Hp, D]
+    send = torch.cat([stacked[:, :, :, p * local:(p + 1) * local].permute(0, 2, 1, 3, 4)
+                      .reshape(-1) for p in range(world)])
+    block = 3 * batch * local * dim
+    recv = torch.empty(total * block, dtype=q.dtype)
+    dist.all_to_all_single(recv, send, [r * block for r in rows], [mine * block] * world,
+                           group=group)
+    parts, at = [], 0
+    for r in rows:  # source r's rows, in rank order = sequence order
+        parts.append(recv[at:at + r * block].view(3, r, batch, local, dim))
+        at += r * block
+    whole = torch.cat(parts, dim=1).permute(0, 2, 1, 3, 4)  # [3, B, S, local, D]
+    attended = compute(whole[0], whole[1], whole[2])  # [B, S, local, D]
+    starts = [sum(rows[:r]) for r in range(world)]
+    back = torch.cat([attended[:, s:s + n].permute(1, 0, 2, 3).reshape(-1)
+                      for s, n in zip(starts, rows, strict=True)])
+    unit = batch * local * dim
+    landed = torch.empty(world * mine * unit, dtype=attended.dtype)
+    dist.all_to_all_single(landed, back, [mine * unit] * world, [r * unit for r in rows],
+                           group=group)
+    out = landed.view(world, mine, batch, local, dim).permute(2, 1, 0, 3, 4)
+    return out.reshape(batch, mine, padded, dim)[:, :, :heads]
+
+
 def head_norm_rope(
     x: Tensor,
     cos: Tensor,

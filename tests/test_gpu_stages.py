@@ -73,3 +73,30 @@ def test_peer_wait_times_out_into_status():
     torch.cuda.synchronize()
     assert code == 0 and int(status.item()) == 0
     assert torch.ones(3, device=device).sum().item() == 3.0
+
+
+def test_exchange_raises_after_a_timeout():
+    """A wait that ran out (a flag nothing sets, 0.2 s) leaves status 2; the exchange sees it
+    without synchronizing (the status word is copied to the host behind each call) and the
+    call after the one that copied it raises, once; later calls work."""
+    from cozy_runtime_b200 import _lib, attention, ulysses
+
+    lib = _lib.load()
+    device = torch.device("cuda", 0)
+    g = torch.Generator(device=device).manual_seed(2)
+    q, k, v = (torch.randn(1, 300, 2, 128, generator=g, device=device).to(torch.bfloat16)
+               for _ in range(3))
+    status = attention.status_word(device)
+    status.zero_()
+    ulysses.exchange(q, k, v, None)  # a watch exists
+    torch.cuda.synchronize()
+    flags = torch.zeros(1, dtype=torch.int64, device=device)
+    assert lib.cozy_peer_wait(flags.data_ptr(), 1, 1, 200_000_000, status.data_ptr(),
+                              torch.cuda.current_stream().cuda_stream) == 0
+    ulysses.exchange(q, k, v, None)  # queued behind the timed-out wait: copies status 2
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="peer"):
+        ulysses.exchange(q, k, v, None)
+    out = ulysses.exchange(q, k, v, None)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0 and torch.isfinite(out.float()).all()

@@ -2,6 +2,7 @@
 C ABI library's exports (no compute calls)."""
 
 import ctypes
+import os
 import re
 from pathlib import Path
 
@@ -262,3 +263,54 @@ def test_candidate_row_matches_the_kernel():
     assert row.families == frozenset({"tcgen05"}) and row.dtypes == ("bfloat16",)
     assert row.head_dims == (64, 128) and row.causal and row.gqa and not row.masks
     assert row.local is au.COZY_B200 and row.local.head_local
+
+
+def _crossing_rank(rank, world, port, outdir):
+    import time
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from cozy_runtime_b200 import ulysses
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=timedelta(seconds=5))
+    group = dist.group.WORLD
+    x = torch.arange(4 * world, dtype=torch.float32) + 100 * rank
+    got = torch.empty_like(x)
+    began = time.perf_counter()
+    outcome = "returned"
+    try:
+        with ulysses._Crossing(group) as crossing:
+            crossing.crossed = True
+            dist.all_to_all_single(got, x, group=group)  # the first crossing
+            if rank == 1:
+                raise ValueError("compute failed after the crossing")
+            back = torch.empty_like(x)
+            dist.all_to_all_single(back, got, group=group)  # the return: rank 1 never comes
+    except ValueError:
+        outcome = "ValueError"
+    except RuntimeError:
+        outcome = "RuntimeError"
+    elapsed = time.perf_counter() - began
+    with open(os.path.join(outdir, f"{rank}.txt"), "w") as fh:
+        fh.write(f"{outcome} {elapsed:.1f}")
+
+
+def test_failure_after_crossing_ends_the_wait_of_peers():
+    """A rank whose compute raises after the first crossing ends its group on the way out (the
+    reference's abort_process_group after a crossing): the peer blocked in the return crossing
+    raises within the group's timeout instead of waiting for it. Two gloo ranks on CPU."""
+    import socket
+    import tempfile
+
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    with tempfile.TemporaryDirectory() as tmp:
+        mp.spawn(_crossing_rank, args=(2, port, tmp), nprocs=2, join=True)
+        outcomes = [open(os.path.join(tmp, f"{r}.txt")).read().split() for r in range(2)]
+    assert outcomes[1][0] == "ValueError"
+    assert outcomes[0][0] == "RuntimeError" and float(outcomes[0][1]) < 60

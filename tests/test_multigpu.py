@@ -32,8 +32,15 @@ def _port() -> int:
         return s.getsockname()[1]
 
 
+def _sdpa_compute(qq, kk, vv):
+    """A caller's own head-local compute: torch SDPA in fp32 on [B, S, h, D] views."""
+    o = torch.nn.functional.scaled_dot_product_attention(
+        qq.transpose(1, 2).float(), kk.transpose(1, 2).float(), vv.transpose(1, 2).float())
+    return o.transpose(1, 2).to(qq.dtype)
+
+
 def _rank(rank, world, port, inputs, causal, outdir, rope_args, transport, fp8=False,
-          narrow=False):
+          narrow=False, compute=False):
     import torch.distributed as dist
 
     from cozy_runtime_b200 import rope as rope_mod
@@ -51,8 +58,8 @@ def _rank(rank, world, port, inputs, causal, outdir, rope_args, transport, fp8=F
     if rope_args is not None:
         spec = rope_mod.axial(rope_args[0], (44, 42, 42), after=rope_args[1]).to(device)
     outs = [
-        ulysses.exchange(q, k, v, dist.group.WORLD, None, causal=causal, rope=spec,
-                         transport=transport, fp8=fp8, narrow=narrow)
+        ulysses.exchange(q, k, v, dist.group.WORLD, _sdpa_compute if compute else None,
+                         causal=causal, rope=spec, transport=transport, fp8=fp8, narrow=narrow)
         for _ in range(3)
     ]
     torch.cuda.synchronize()
@@ -67,12 +74,12 @@ def _rank(rank, world, port, inputs, causal, outdir, rope_args, transport, fp8=F
 
 
 def _run(inputs, world, causal=False, rope_args=None, transport="peer", fp8=False,
-         narrow=False):
+         narrow=False, compute=False):
     import torch.multiprocessing as mp
 
     with tempfile.TemporaryDirectory() as tmp:
         mp.spawn(_rank, args=(world, _port(), inputs, causal, tmp, rope_args, transport, fp8,
-                              narrow),
+                              narrow, compute),
                  nprocs=world, join=True)
         return torch.cat([torch.load(os.path.join(tmp, f"{r}.pt")) for r in range(world)], dim=1)
 
@@ -175,3 +182,15 @@ def test_narrow_exchange_against_oracle(world, hq, hkv, causal, transport):
     want = torch.cat(oracle.exchange_narrow(
         *parts, lambda a, b, c: oracle.attention_fp32(a, b, c, causal=causal)), dim=1)
     _check(got, want.float())
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_exchange_with_callable_compute(world):
+    """The bf16 exchange with a caller's own compute (sparse producers' use) across processes:
+    NCCL crossing, [B, S, h, D] operands, against the oracle."""
+    if world > _gpus():
+        pytest.skip(f"needs {world} GPUs")
+    g = torch.Generator().manual_seed(40 + world)
+    q, k, v = (torch.randn(1, 803, 8, 128, generator=g).to(torch.bfloat16) for _ in range(3))
+    got = _run((q, k, v), world, compute=True)
+    _check(got, oracle.attention_fp32(q, k, v))
