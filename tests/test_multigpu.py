@@ -1,15 +1,20 @@
-"""The exchange between GPU processes (one per GPU) over both transports — in-kernel NVLink peer
-stores and NCCL all-to-all — against the reference's golden outputs and the oracle. Needs two or
-more GPUs; skipped otherwise.
+"""The exchange between GPU processes (one per GPU) over both transports — the NVLink layer
+(copy-engine crossing overlapped with the attention) and NCCL all-to-all — against the
+reference's golden outputs and the oracle. Needs two or more GPUs; skipped otherwise.
 
-Each case spawns W processes (W ≤ visible GPUs), every rank passes its `tensor_split` rows and
-the rows come from the store meeting (no `rows` argument), as the reference's exchange does.
-NVLS is off (`NCCL_NVLS_ENABLE=0`), as the reference's group formation sets it.
+Every rank passes its `tensor_split` rows and the rows come from the store meeting (no `rows`
+argument), as the reference's exchange does. NVLS is off (`NCCL_NVLS_ENABLE=0`), as the
+reference's group formation sets it. To keep process start-up and NCCL formation out of every
+case, the cases of one degree W run in one set of W processes (started once, on the first test
+that needs that degree); each case's inputs are rebuilt in every process from a small
+description, each case runs three times (the repeats must agree bit for bit), and the tests
+then check what the processes saved.
 """
 
 import os
 import socket
 import tempfile
+import traceback
 
 import pytest
 import torch
@@ -20,6 +25,7 @@ from tests._golden import load, narrow_cases, tensor, ulysses_cases
 pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
 
 MAX_ABS, MEAN_ABS = 2e-2, 2e-3
+GRID, TEXT = (2, 6, 10), 17
 
 
 def _gpus() -> int:
@@ -32,6 +38,65 @@ def _port() -> int:
         return s.getsockname()[1]
 
 
+# ----------------------------------------------------------------------------- the cases
+def _random_inputs(seed, seq, hq, hkv, outliers=False):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(1, seq, hq, 128, generator=g)
+    k = torch.randn(1, seq, hkv, 128, generator=g)
+    v = torch.randn(1, seq, hkv, 128, generator=g)
+    if outliers:
+        k = torch.where(torch.rand(k.shape, generator=g) < 0.01, k * 8, k)
+    return tuple(t.to(torch.bfloat16) for t in (q, k, v))
+
+
+def inputs_of(case: dict):
+    """The whole [B, S, H, D] Q, K, V of a case (every process rebuilds them alike)."""
+    if "golden" in case:
+        data = load(case["golden"])
+        return tuple(tensor(data[key]) for key in ("q", "k", "v"))
+    return _random_inputs(case["seed"], case["seq"], case["hq"], case["hkv"],
+                          case.get("outliers", False))
+
+
+def _cases() -> list[dict]:
+    out = []
+    for name in ulysses_cases():
+        world = int(load(name)["world"])
+        for transport in ("peer", "nccl"):
+            out.append({"id": f"golden-{name}-{transport}", "world": world, "golden": name,
+                        "causal": bool(load(name)["causal"]), "transport": transport})
+    for world, hq, hkv, causal, rotate in [(2, 8, 8, False, True), (4, 8, 2, True, False),
+                                           (8, 8, 8, False, True), (8, 32, 8, True, False),
+                                           (3, 5, 5, False, True), (7, 32, 8, True, False)]:
+        for transport in ("peer", "nccl"):
+            out.append({"id": f"oracle-w{world}-{hq}-{hkv}-{causal}-{rotate}-{transport}",
+                        "world": world, "seed": world + hq, "seq": 2 * 6 * 10 + TEXT, "hq": hq,
+                        "hkv": hkv, "causal": causal, "rotate": rotate, "transport": transport})
+    for world, hq, hkv, causal in [(2, 4, 4, False), (8, 16, 16, False), (4, 8, 2, True)]:
+        out.append({"id": f"fp8-w{world}-{hq}-{hkv}-{causal}", "world": world,
+                    "seed": world * 7 + hq, "seq": 1000, "hq": hq, "hkv": hkv, "causal": causal,
+                    "outliers": True, "fp8": True, "transport": "peer"})
+    for name in narrow_cases():
+        world = int(load(name)["world"])
+        for transport in ("peer", "nccl"):
+            out.append({"id": f"narrowgolden-{name}-{transport}", "world": world,
+                        "golden": name, "causal": bool(load(name)["causal"]), "narrow": True,
+                        "transport": transport})
+    for world, hq, hkv, causal in [(2, 4, 4, False), (4, 8, 2, True), (8, 16, 16, False)]:
+        for transport in ("peer", "nccl"):
+            out.append({"id": f"narrow-w{world}-{hq}-{hkv}-{causal}-{transport}", "world": world,
+                        "seed": world * 31 + hq, "seq": 1000 + world, "hq": hq, "hkv": hkv,
+                        "causal": causal, "narrow": True, "transport": transport})
+    for world in (2, 4, 8):
+        out.append({"id": f"compute-w{world}", "world": world, "seed": 40 + world, "seq": 803,
+                    "hq": 8, "hkv": 8, "causal": False, "compute": True, "transport": "nccl"})
+    return out
+
+
+CASES = {c["id"]: c for c in _cases()}
+
+
+# ----------------------------------------------------------------------- the processes
 def _sdpa_compute(qq, kk, vv):
     """A caller's own head-local compute: torch SDPA in fp32 on [B, S, h, D] views."""
     o = torch.nn.functional.scaled_dot_product_attention(
@@ -39,49 +104,79 @@ def _sdpa_compute(qq, kk, vv):
     return o.transpose(1, 2).to(qq.dtype)
 
 
-def _rank(rank, world, port, inputs, causal, outdir, rope_args, transport, fp8=False,
-          narrow=False, compute=False):
+def _batch_rank(rank, world, port, cases, outdir):
     import torch.distributed as dist
 
+    from cozy_runtime_b200 import attention, ulysses
     from cozy_runtime_b200 import rope as rope_mod
-    from cozy_runtime_b200 import ulysses
 
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     device = torch.device("cuda", rank)
     torch.cuda.set_device(device)
+    from datetime import timedelta
+
     dist.init_process_group(
         "nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
-        device_id=device,
+        device_id=device, timeout=timedelta(seconds=120),
     )
-    q, k, v = (torch.tensor_split(t, world, dim=1)[rank].contiguous().to(device) for t in inputs)
-    spec = None
-    if rope_args is not None:
-        spec = rope_mod.axial(rope_args[0], (44, 42, 42), after=rope_args[1]).to(device)
-    outs = [
-        ulysses.exchange(q, k, v, dist.group.WORLD, _sdpa_compute if compute else None,
-                         causal=causal, rope=spec, transport=transport, fp8=fp8, narrow=narrow)
-        for _ in range(3)
-    ]
-    torch.cuda.synchronize()
-    from cozy_runtime_b200 import attention
-
-    attention.check_status(device)
-    out = outs[0]
-    assert all(torch.equal(out, o) for o in outs[1:]), "repeated calls differ"
-    torch.save(out.cpu(), os.path.join(outdir, f"{rank}.pt"))
+    for case in cases:
+        path = os.path.join(outdir, f"{case['id']}.{rank}")
+        try:
+            q, k, v = (torch.tensor_split(t, world, dim=1)[rank].contiguous().to(device)
+                       for t in inputs_of(case))
+            spec = None
+            if case.get("rotate"):
+                spec = rope_mod.axial(GRID, (44, 42, 42), after=TEXT).to(device)
+            outs = [
+                ulysses.exchange(
+                    q, k, v, dist.group.WORLD, _sdpa_compute if case.get("compute") else None,
+                    causal=case["causal"], rope=spec, transport=case["transport"],
+                    fp8=case.get("fp8", False), narrow=case.get("narrow", False))
+                for _ in range(3)
+            ]
+            torch.cuda.synchronize()
+            attention.check_status(device)
+            if not all(torch.equal(outs[0], o) for o in outs[1:]):
+                raise AssertionError("repeated calls differ")
+            torch.save(outs[0].cpu(), path + ".pt")
+            with open(path + ".transport", "w") as fh:
+                fh.write(ulysses.transport_of(dist.group.WORLD, device)
+                         if case["transport"] == "peer" else "nccl")
+        except Exception:  # noqa: BLE001 - recorded for the test that owns the case
+            with open(path + ".err", "w") as fh:
+                fh.write(traceback.format_exc())
     dist.barrier()
     dist.destroy_process_group()
 
 
-def _run(inputs, world, causal=False, rope_args=None, transport="peer", fp8=False,
-         narrow=False, compute=False):
-    import torch.multiprocessing as mp
+_RUNS: dict[int, str] = {}
+_TMP = tempfile.TemporaryDirectory()
 
-    with tempfile.TemporaryDirectory() as tmp:
-        mp.spawn(_rank, args=(world, _port(), inputs, causal, tmp, rope_args, transport, fp8,
-                              narrow, compute),
-                 nprocs=world, join=True)
-        return torch.cat([torch.load(os.path.join(tmp, f"{r}.pt")) for r in range(world)], dim=1)
+
+def _result(case_id: str) -> torch.Tensor:
+    """The whole output of a case (its degree's processes run once, on first need)."""
+    case = CASES[case_id]
+    world = case["world"]
+    if world < 2 or world > _gpus():
+        pytest.skip(f"needs {world} GPUs")
+    if world not in _RUNS:
+        import torch.multiprocessing as mp
+
+        outdir = os.path.join(_TMP.name, f"w{world}")
+        os.makedirs(outdir, exist_ok=True)
+        todo = [c for c in CASES.values() if c["world"] == world]
+        mp.spawn(_batch_rank, args=(world, _port(), todo, outdir), nprocs=world, join=True)
+        _RUNS[world] = outdir
+    outdir = _RUNS[world]
+    parts = []
+    for rank in range(world):
+        path = os.path.join(outdir, f"{case_id}.{rank}")
+        if os.path.exists(path + ".err"):
+            raise AssertionError(f"rank {rank}:\n" + open(path + ".err").read())
+        parts.append(torch.load(path + ".pt"))
+        if CASES[case_id]["transport"] == "peer":
+            assert open(path + ".transport").read() == "peer", "the peer transport did not form"
+    return torch.cat(parts, dim=1)
 
 
 def _check(got, want):
@@ -90,60 +185,37 @@ def _check(got, want):
     assert err.mean().item() <= MEAN_ABS, f"mean-abs {err.mean().item():.3e}"
 
 
-@pytest.mark.parametrize("transport", ["peer", "nccl"])
-@pytest.mark.parametrize("name", ulysses_cases())
-def test_exchange_matches_reference_golden(name, transport):
-    case = load(name)
-    world = int(case["world"])
-    if world < 2 or world > _gpus():
-        pytest.skip(f"needs {world} GPUs")
-    inputs = tuple(tensor(case[key]) for key in ("q", "k", "v"))
-    got = _run(inputs, world, causal=bool(case["causal"]), transport=transport)
-    _check(got, tensor(case["out"]).float())
+# ---------------------------------------------------------------------------- the tests
+@pytest.mark.parametrize("case_id", [c for c in CASES if c.startswith("golden-")])
+def test_exchange_matches_reference_golden(case_id):
+    got = _result(case_id)
+    _check(got, tensor(load(CASES[case_id]["golden"])["out"]).float())
 
 
-@pytest.mark.parametrize(
-    "world,hq,hkv,causal,rotate",
-    [(2, 8, 8, False, True), (4, 8, 2, True, False), (8, 8, 8, False, True), (8, 32, 8, True, False),
-     (3, 5, 5, False, True)],
-)
-@pytest.mark.parametrize("transport", ["peer", "nccl"])
-def test_exchange_against_oracle(world, hq, hkv, causal, rotate, transport):
-    if world > _gpus():
-        pytest.skip(f"needs {world} GPUs")
+@pytest.mark.parametrize("case_id", [c for c in CASES if c.startswith("oracle-")])
+def test_exchange_against_oracle(case_id):
     from cozy_runtime_b200 import rope as rope_mod
 
-    g = torch.Generator().manual_seed(world + hq)
-    grid, text = (2, 6, 10), 17
-    seq = 2 * 6 * 10 + text
-    q = torch.randn(1, seq, hq, 128, generator=g).to(torch.bfloat16)
-    k = torch.randn(1, seq, hkv, 128, generator=g).to(torch.bfloat16)
-    v = torch.randn(1, seq, hkv, 128, generator=g).to(torch.bfloat16)
-    got = _run((q, k, v), world, causal=causal, rope_args=(grid, text) if rotate else None,
-               transport=transport)
-    if rotate:
-        spec = rope_mod.axial(grid, (44, 42, 42), after=text)
+    case = CASES[case_id]
+    got = _result(case_id)
+    q, k, v = inputs_of(case)
+    if case["rotate"]:
+        spec = rope_mod.axial(GRID, (44, 42, 42), after=TEXT)
         q, k = (oracle.head_norm_rope(t.float(), spec.cos, spec.sin, rotary=128, interleaved=True,
                                       normalize=False).to(torch.bfloat16) for t in (q, k))
-    _check(got, oracle.attention_fp32(q, k, v, causal=causal))
+    _check(got, oracle.attention_fp32(q, k, v, causal=case["causal"]))
 
 
-@pytest.mark.parametrize("world,hq,hkv,causal", [(2, 4, 4, False), (8, 16, 16, False), (4, 8, 2, True)])
-def test_fp8_exchange_peer_against_law(world, hq, hkv, causal):
+@pytest.mark.parametrize("case_id", [c for c in CASES if c.startswith("fp8-")])
+def test_fp8_exchange_peer_against_law(case_id):
     """The FP8 path over the NVLink transport (statistics all-reduced, e4m3 codes and scales
     stored into the owners' buffers) against the oracle's FP8 law and exact attention."""
-    if world > _gpus():
-        pytest.skip(f"needs {world} GPUs")
-    g = torch.Generator().manual_seed(world * 7 + hq)
-    seq = 1000
-    q = torch.randn(1, seq, hq, 128, generator=g)
-    k = torch.randn(1, seq, hkv, 128, generator=g)
-    v = torch.randn(1, seq, hkv, 128, generator=g)
-    k = torch.where(torch.rand(k.shape, generator=g) < 0.01, k * 8, k)
-    q, k, v = (t.to(torch.bfloat16) for t in (q, k, v))
-    got = _run((q, k, v), world, causal=causal, fp8=True).float()
-    rows = [t.shape[0] for t in torch.tensor_split(torch.empty(seq), world)]
-    law = oracle.fp8_attention_law(*(torch.split(t, rows, dim=1) for t in (q, k, v)), causal=causal)
+    case = CASES[case_id]
+    got = _result(case_id).float()
+    q, k, v = inputs_of(case)
+    rows = [t.shape[0] for t in torch.tensor_split(torch.empty(case["seq"]), case["world"])]
+    law = oracle.fp8_attention_law(*(torch.split(t, rows, dim=1) for t in (q, k, v)),
+                                   causal=case["causal"])
 
     def cos(a, b):
         a = a.permute(0, 2, 1, 3).reshape(a.shape[2], -1)
@@ -151,46 +223,31 @@ def test_fp8_exchange_peer_against_law(world, hq, hkv, causal):
         return torch.nn.functional.cosine_similarity(a, b, dim=1).min().item()
 
     assert cos(got, law) >= 0.999
-    assert cos(got, oracle.attention_fp32(q, k, v, causal=causal)) >= 0.995
+    assert cos(got, oracle.attention_fp32(q, k, v, causal=case["causal"])) >= 0.995
 
 
-@pytest.mark.parametrize("transport", ["peer", "nccl"])
-@pytest.mark.parametrize("name", narrow_cases())
-def test_narrow_exchange_matches_reference_golden(name, transport):
+@pytest.mark.parametrize("case_id", [c for c in CASES if c.startswith("narrowgolden-")])
+def test_narrow_exchange_matches_reference_golden(case_id):
     """The int8 wire between GPU processes against the reference's own narrow exchange."""
-    case = load(name)
-    world = int(case["world"])
-    if world < 2 or world > _gpus():
-        pytest.skip(f"needs {world} GPUs")
-    inputs = tuple(tensor(case[key]) for key in ("q", "k", "v"))
-    got = _run(inputs, world, causal=bool(case["causal"]), transport=transport, narrow=True)
-    _check(got, tensor(case["out"]).float())
+    got = _result(case_id)
+    _check(got, tensor(load(CASES[case_id]["golden"])["out"]).float())
 
 
-@pytest.mark.parametrize("world,hq,hkv,causal", [(2, 4, 4, False), (4, 8, 2, True), (8, 16, 16, False)])
-@pytest.mark.parametrize("transport", ["peer", "nccl"])
-def test_narrow_exchange_against_oracle(world, hq, hkv, causal, transport):
-    if world > _gpus():
-        pytest.skip(f"needs {world} GPUs")
-    g = torch.Generator().manual_seed(world * 31 + hq)
-    seq = 1000 + world
-    q = torch.randn(1, seq, hq, 128, generator=g).to(torch.bfloat16)
-    k = torch.randn(1, seq, hkv, 128, generator=g).to(torch.bfloat16)
-    v = torch.randn(1, seq, hkv, 128, generator=g).to(torch.bfloat16)
-    got = _run((q, k, v), world, causal=causal, transport=transport, narrow=True)
-    parts = [torch.tensor_split(t, world, dim=1) for t in (q, k, v)]
+@pytest.mark.parametrize("case_id", [c for c in CASES if c.startswith("narrow-w")])
+def test_narrow_exchange_against_oracle(case_id):
+    case = CASES[case_id]
+    got = _result(case_id)
+    q, k, v = inputs_of(case)
+    parts = [torch.tensor_split(t, case["world"], dim=1) for t in (q, k, v)]
     want = torch.cat(oracle.exchange_narrow(
-        *parts, lambda a, b, c: oracle.attention_fp32(a, b, c, causal=causal)), dim=1)
+        *parts, lambda a, b, c: oracle.attention_fp32(a, b, c, causal=case["causal"])), dim=1)
     _check(got, want.float())
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_exchange_with_callable_compute(world):
+@pytest.mark.parametrize("case_id", [c for c in CASES if c.startswith("compute-")])
+def test_exchange_with_callable_compute(case_id):
     """The bf16 exchange with a caller's own compute (sparse producers' use) across processes:
     NCCL crossing, [B, S, h, D] operands, against the oracle."""
-    if world > _gpus():
-        pytest.skip(f"needs {world} GPUs")
-    g = torch.Generator().manual_seed(40 + world)
-    q, k, v = (torch.randn(1, 803, 8, 128, generator=g).to(torch.bfloat16) for _ in range(3))
-    got = _run((q, k, v), world, compute=True)
+    got = _result(case_id)
+    q, k, v = inputs_of(CASES[case_id])
     _check(got, oracle.attention_fp32(q, k, v))
