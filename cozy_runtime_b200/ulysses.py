@@ -482,8 +482,17 @@ def exchange(
     **options,
 ) -> Tensor:
     """Sequence shards -> whole sequences per head subset -> attention -> back (keywords: those
-    of `_exchange`). Raises when an earlier call on this device reported a timed-out wait, seen
-    without synchronizing: the status word is copied to the host behind every call."""
+    of `_exchange`). fp32 and fp16 inputs with the native attention cross and multiply as bf16
+    and come back in their own dtype. Raises when an earlier call on this device reported a
+    timed-out wait, seen without synchronizing: the status word is copied to the host behind
+    every call."""
+    if query.is_cuda and compute is None and query.dtype in (torch.float32, torch.float16):
+        # the kernels compute in bf16 (fp32 softmax and accumulation): other floating inputs
+        # cross and multiply as bf16 and the output returns in the query's dtype
+        wide = query.dtype
+        out = exchange(query.to(torch.bfloat16), key.to(torch.bfloat16),
+                       value.to(torch.bfloat16), handle, None, site, narrow, **options)
+        return out.to(wide)
     if query.is_cuda:
         attention.raise_if_failed(query.device)
     out = _exchange(query, key, value, handle, compute, site, narrow, **options)

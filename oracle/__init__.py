@@ -17,6 +17,7 @@ from oracle.ulysses_oracle import (  # noqa: F401
     exchange_group,
     exchange_narrow,
     fp8_attention_law,
+    hadamard_matrix,
     head_norm_rope,
     heads_padded,
     narrow_law,
