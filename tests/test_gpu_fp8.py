@@ -139,22 +139,27 @@ def test_fp8_exchange_public_call_degree1():
     assert _cosine_per_head(got.float().cpu(), exact).min().item() >= 0.995
 
 
-def _law_rows_gpu(q, k, v, rows, block=64):
-    """The FP8 recipe's law (the oracle's `fp8_attention_law`, one rank: blocks of 64 tokens
-    from multiples of 64) in fp32 torch on the GPU, for query rows `rows` of every head."""
+def _law_rows_gpu(q, k, v, rows, starts, block=64):
+    """The FP8 recipe's law (the oracle's `fp8_attention_law`: blocks of 64 tokens of the whole
+    sequence from multiples of 64, cut where a rank's rows begin) in fp32 torch on the GPU, for
+    query rows `rows` of every head."""
     e4 = 448.0
     q, k, v = q.float(), k.float(), v.float()
     k = k - k.mean(dim=1, keepdim=True)
     h = oracle.hadamard_matrix(q.shape[-1]).to(q.device)
     q, k = q @ h, k @ h
+    seq = q.shape[1]
+    edges = torch.tensor(sorted(set(range(0, seq, block)) | set(starts)), device=q.device)
+    ids = torch.bucketize(torch.arange(seq, device=q.device), edges, right=True) - 1
 
     def blocks(x):
         b, s, hh, d = x.shape
-        nb = -(-s // block)
-        xf = torch.nn.functional.pad(x, (0, 0, 0, 0, 0, nb * block - s)).view(b, nb, block, hh, d)
-        ds = (xf.abs().amax(dim=(2, 4)) / e4).clamp(min=1e-12)
-        codes = (xf / ds[:, :, None, :, None]).clamp(-e4, e4).to(torch.float8_e4m3fn).float()
-        return (codes * ds[:, :, None, :, None]).view(b, nb * block, hh, d)[:, :s]
+        row_max = x.abs().amax(dim=3)  # [B, S, H]
+        amax = torch.zeros(b, len(edges), hh, device=x.device).scatter_reduce(
+            1, ids[None, :, None].expand(b, s, hh), row_max, reduce="amax")
+        ds = (amax / e4).clamp(min=1e-12)[:, ids]  # [B, S, H]
+        codes = (x / ds[..., None]).clamp(-e4, e4).to(torch.float8_e4m3fn).float()
+        return codes * ds[..., None]
 
     q, k = blocks(q), blocks(k)
     vs = (v.abs().amax(dim=1, keepdim=True) / e4).clamp(min=1e-12)
@@ -203,7 +208,8 @@ def test_fp8_at_full_c4_length():
     worst_exact, worst_law = 1.0, 1.0
     for first in range(0, heads, 8):
         part = slice(first, first + 8)
-        law = _law_rows_gpu(q[:, :, part], k[:, :, part], v[:, :, part], rows)
+        law = _law_rows_gpu(q[:, :, part], k[:, :, part], v[:, :, part], rows,
+                            [9450 * r for r in range(world)])
         for i in range(law.shape[1]):
             h = first + i
             s = (q[0, rows, h].float() @ k[0, :, h].float().T) / math.sqrt(128)
