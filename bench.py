@@ -673,6 +673,25 @@ def main() -> None:
         from cozy_runtime_b200 import peer
 
         flag_mode = peer.layer_group_for(group, device).flag_mode()
+    crossing = None
+    if transport == "peer" and group is not None:
+        # the latest call's crossing on each rank: its copy-engine copies to the other ranks and
+        # their flag writes, timed on the side stream (bytes / time = the NVLink rate reached)
+        torch.cuda.synchronize()
+        got = peer.layer_group_for(group, device).crossing() or (0.0, 0)
+        each = torch.tensor([got[0], float(got[1])], dtype=torch.float64, device=device)
+        every = [torch.empty_like(each) for _ in range(world)]
+        dist.all_gather(every, each)
+        ms_each = [t[0].item() for t in every]
+        bytes_each = [int(t[1].item()) for t in every]
+        crossing = {
+            "ms_max": round(max(ms_each), 4),
+            "bytes_per_rank": bytes_each[0],
+            "gbs_per_rank_min": round(min(b / (m * 1e-3) / 1e9 for b, m in
+                                          zip(bytes_each, ms_each, strict=True) if m > 0), 1)
+            if all(m > 0 for m in ms_each) else None,
+            "how": "cudaMemcpyAsync peer copies on a side stream, beside the attention",
+        }
 
     # ---- end to end through the public call, host buffers in and out every step
     e2e_ms = h2d = d2h = None
@@ -791,6 +810,7 @@ def main() -> None:
             },
             "transport": transport,
             "flag_mode": flag_mode,
+            "crossing": crossing,
             "layer": {
                 "attention_span_ms": round(span_max, 4),
                 "attention_alone_ms": None if alone_ms is None else round(alone_ms, 4),

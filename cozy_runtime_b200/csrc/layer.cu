@@ -178,6 +178,9 @@ struct CozyGroup {
   long long* ring = nullptr;  // pinned host words the flag copies read when they are not
   cudaStream_t side = nullptr;
   cudaEvent_t packed = nullptr, sent = nullptr;
+  // timing of the crossing: the side stream's copies and flags of the latest call
+  cudaEvent_t cross_start = nullptr, cross_end = nullptr;
+  unsigned long long cross_bytes = 0;
   std::mutex lock;
 };
 
@@ -251,6 +254,8 @@ int cozy_group_create(int rank, int world, CozyGroup** group) {
     e = cudaStreamCreateWithPriority(&g->side, cudaStreamNonBlocking, greatest);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&g->packed, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&g->sent, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreate(&g->cross_start);
+  if (e == cudaSuccess) e = cudaEventCreate(&g->cross_end);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) {
     cozy_group_destroy(g);
@@ -268,6 +273,8 @@ int cozy_group_destroy(CozyGroup* g) {
   if (g->ring != nullptr) cudaFreeHost(g->ring);
   if (g->packed != nullptr) cudaEventDestroy(g->packed);
   if (g->sent != nullptr) cudaEventDestroy(g->sent);
+  if (g->cross_start != nullptr) cudaEventDestroy(g->cross_start);
+  if (g->cross_end != nullptr) cudaEventDestroy(g->cross_end);
   if (g->side != nullptr) cudaStreamDestroy(g->side);
   delete g;
   return e;
@@ -387,6 +394,19 @@ int cozy_group_flag(const CozyGroup* g, int kind, int src, long long* value) {
                     cudaMemcpyDeviceToHost);
 }
 
+int cozy_group_crossing(CozyGroup* g, float* ms, unsigned long long* bytes) {
+  if (g == nullptr || ms == nullptr || bytes == nullptr) return cudaErrorInvalidValue;
+  std::lock_guard<std::mutex> guard(g->lock);
+  if (g->seq == 0) return cudaErrorNotReady;
+  const cudaError_t e = cudaEventElapsedTime(ms, g->cross_start, g->cross_end);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return e;
+  }
+  *bytes = g->cross_bytes;
+  return cudaSuccess;
+}
+
 int cozy_group_flag_mode(const CozyGroup* g) {
   if (g == nullptr) return -1;
   return g->write_value ? 1 : 2;
@@ -450,12 +470,15 @@ int cozy_ulysses_layer_begin(CozyGroup* g, const CozyLayerCall* c, uintptr_t str
   if ((e = cudaEventRecord(g->packed, stream)) != cudaSuccess) return e;
   // 2. the crossing: copy engines, destination by destination, each followed by its flag
   if ((e = cudaStreamWaitEvent(g->side, g->packed, 0)) != cudaSuccess) return e;
+  if ((e = cudaEventRecord(g->cross_start, g->side)) != cudaSuccess) return e;
+  g->cross_bytes = 0;
   for (int step = 1; step < world; ++step) {
     const int p = (me + step) % world;
     for (int i = 0; i < 3; ++i) {
       const int n = i == 0 ? plan.q_n[p] : plan.kv_n[p];
       const size_t bytes = mine * b * n * d * el;
       if (bytes == 0) continue;
+      g->cross_bytes += bytes;
       uint8_t* dst = static_cast<uint8_t*>(g->peer[p][set][i]) + row_offset(plan, s, me, n);
       if ((e = cudaMemcpyAsync(dst, static_cast<uint8_t*>(g->stage) + block_off[i][p], bytes,
                                cudaMemcpyDeviceToDevice, g->side)) != cudaSuccess)
@@ -476,6 +499,7 @@ int cozy_ulysses_layer_begin(CozyGroup* g, const CozyLayerCall* c, uintptr_t str
         return e;
     }
   }
+  if ((e = cudaEventRecord(g->cross_end, g->side)) != cudaSuccess) return e;
   return cudaEventRecord(g->sent, g->side);
 }
 

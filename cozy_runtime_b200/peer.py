@@ -277,6 +277,15 @@ class LayerGroup:
                                                                   ctypes.byref(value)))
         return value.value
 
+    def crossing(self) -> tuple[float, int] | None:
+        """(ms, bytes) of the latest call's crossing on this rank (copies to the other ranks and
+        their flags, on the side stream), or None while it is under way."""
+        ms, nbytes = ctypes.c_float(0), ctypes.c_ulonglong(0)
+        code = _lib.load().cozy_group_crossing(self.ptr, ctypes.byref(ms), ctypes.byref(nbytes))
+        if code != _lib.SUCCESS:
+            return None
+        return ms.value, nbytes.value
+
     def run(self, phase: str, call: _lib.LayerCall, stream: int) -> None:
         entry = f"cozy_ulysses_layer_{phase}"
         _lib.check(entry, getattr(_lib.load(), entry)(self.ptr, ctypes.byref(call), stream))

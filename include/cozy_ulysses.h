@@ -394,6 +394,10 @@ COZY_API int cozy_group_flag_mode(const CozyGroup* group);
 /* The last call number rank `src` published to this rank (kind 0: its Q/K/V blocks landed;
  * kind 1: its output rows landed); a synchronous read, for monitoring and tests. */
 COZY_API int cozy_group_flag(const CozyGroup* group, int kind, int src, long long* value);
+/* The latest call's crossing on this rank: milliseconds from its first copy to its last flag
+ * write on the side stream, and the bytes its copies moved to the other ranks (for NVLink
+ * bandwidth: bytes / ms). cudaErrorNotReady while that call's copies are still under way. */
+COZY_API int cozy_group_crossing(CozyGroup* group, float* ms, unsigned long long* bytes);
 
 /* The layer: cozy_ulysses_layer_fwd = begin (first stage, copies and flags to every rank),
  * attend (the attention, waiting per source inside the kernel, output rows stored into their
