@@ -93,6 +93,12 @@ class Fp8Stats(Structure):
         ("head_dim", c_int),
         ("k_sum", c_void_p),
         ("v_amax", c_void_p),
+        ("normalize", c_int),
+        ("norm_weight", c_void_p),
+        ("norm_offset", c_float),
+        ("norm_eps", c_float),
+        ("rotate", c_int),
+        ("rope", Rope),
     ]
 
 
@@ -112,6 +118,11 @@ class Fp8Tensor(Structure):
         ("scale_seq", c_longlong),
         ("head_lo", c_int * MAX_PEERS),
         ("head_n", c_int * MAX_PEERS),
+        ("normalize", c_int),
+        ("norm_weight", c_void_p),
+        ("norm_offset", c_float),
+        ("norm_eps", c_float),
+        ("rotate", c_int),
     ]
 
 
@@ -126,6 +137,7 @@ class Fp8Pack(Structure):
         ("head_dim", c_int),
         ("row0", c_int),
         ("head_turn", c_int),
+        ("rope", Rope),
     ]
 
 

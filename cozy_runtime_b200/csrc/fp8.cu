@@ -9,6 +9,9 @@
 // this rank's rows); V quantised with one fp32 scale per
 // (batch, head, channel) over the whole sequence. Codes are round-to-nearest-even, saturating.
 //
+// With RoPE / RMSNorm (the first stage's law, norm_rope.cuh) the recipe applies to the rotated
+// Q and K, rounded to bf16 as the bf16 first stage leaves them: one pass over HBM does all of it.
+//
 // fp8_stats_kernel: this rank's partial K sums and V channel absmax (the host all-reduces them).
 // fp8_pack_kernel:  one CTA per (block, head, batch) of one tensor: rows loaded once,
 //                   mean subtracted, block absmax reduced in the CTA, codes written to every
@@ -19,30 +22,104 @@
 #include <stdint.h>
 
 #include "../../include/cozy_ulysses.h"
+#include "norm_rope.cuh"
 
 namespace cozy {
 
 constexpr float kE4M3Max = 448.0f;
 constexpr float kScaleFloor = 1e-12f;
 
-__global__ void __launch_bounds__(128) fp8_stats_kernel(CozyFp8Stats a) {
-  const int d = threadIdx.x;  // one channel per thread (head_dim 128)
-  const int head = blockIdx.y, b = blockIdx.z;
-  const int r0 = blockIdx.x * 256;
-  const int r1 = min(a.rows, r0 + 256);
-  const __nv_bfloat16* k = static_cast<const __nv_bfloat16*>(a.key) + b * a.k_strides[2] +
-                           head * a.k_strides[1] + d;
-  const __nv_bfloat16* v = static_cast<const __nv_bfloat16*>(a.value) + b * a.v_strides[2] +
-                           head * a.v_strides[1] + d;
-  float sum = 0.f, amax = 0.f;
-  for (int r = r0; r < r1; ++r) {
-    sum += __bfloat162float(k[r * a.k_strides[0]]);
-    amax = fmaxf(amax, fabsf(__bfloat162float(v[r * a.v_strides[0]])));
+// bf16 rounding of the first stage's fp32 result (the bf16 first stage stores exactly this)
+__device__ __forceinline__ float bf16_round(float x) {
+  return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+template <typename T>
+__device__ __host__ __forceinline__ bool first_stage_law(const T& t) {
+  return t.normalize || t.rotate;
+}
+
+__device__ __forceinline__ void unpack8(const uint4& v, float (&x)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    x[2 * i] = f.x;
+    x[2 * i + 1] = f.y;
   }
-  const int o = (b * a.heads + head) * 128 + d;
-  atomicAdd(a.k_sum + o, sum);
-  // non-negative floats order like their bit patterns
-  atomicMax(reinterpret_cast<unsigned int*>(a.v_amax) + o, __float_as_uint(amax));
+}
+
+// blockIdx: x = slab of kStatsRows rows, y = head, z = batch. 256 threads: 16 a row (8 channels
+// each, 16-byte loads), 16 rows a pass; UNROLL rows a thread are loaded (raw, 16 bytes each of K
+// and V) before their math.
+constexpr int kStatsRows = 256;
+
+template <bool LAW>
+__global__ void __launch_bounds__(256, 3) fp8_stats_kernel(const CozyFp8Stats a) {
+  constexpr int UNROLL = LAW ? 2 : 4;
+  const int chunk = threadIdx.x & 15;
+  const int row_in = threadIdx.x >> 4;
+  const int d0 = chunk * 8;
+  const int head = blockIdx.y, b = blockIdx.z;
+  const int r0 = blockIdx.x * kStatsRows;
+  const __nv_bfloat16* key = static_cast<const __nv_bfloat16*>(a.key) + b * a.k_strides[2] +
+                             head * a.k_strides[1] + d0;
+  const __nv_bfloat16* value = static_cast<const __nv_bfloat16*>(a.value) + b * a.v_strides[2] +
+                               head * a.v_strides[1] + d0;
+  float sum[8], amax[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) sum[i] = amax[i] = 0.f;
+  for (int base = 0; base < kStatsRows; base += 16 * UNROLL) {
+    uint4 kr[UNROLL], vr[UNROLL];
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+      const int r = r0 + base + u * 16 + row_in;
+      kr[u] = vr[u] = make_uint4(0u, 0u, 0u, 0u);
+      if (r < a.rows) {
+        kr[u] = *reinterpret_cast<const uint4*>(key + r * a.k_strides[0]);
+        vr[u] = *reinterpret_cast<const uint4*>(value + r * a.v_strides[0]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+      const int r = r0 + base + u * 16 + row_in;
+      float x[8], y[8];
+      unpack8(kr[u], x);
+      unpack8(vr[u], y);
+      if constexpr (LAW) {  // a row past the end is zeros: its table row is clamped, unused
+        norm_rope_row<128>(x, d0, chunk, row_group_mask<16>(),
+                           a.rope.token0 + min(r, a.rows - 1), a, a.rope);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[i] = r < a.rows ? bf16_round(x[i]) : 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        sum[i] += x[i];
+        amax[i] = fmaxf(amax[i], fabsf(y[i]));
+      }
+    }
+  }
+  // the CTA's 16 row groups into one partial per channel, then one atomic per channel
+  __shared__ float part_sum[16][128], part_max[16][128];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    part_sum[row_in][d0 + i] = sum[i];
+    part_max[row_in][d0 + i] = amax[i];
+  }
+  __syncthreads();
+  if (threadIdx.x < 128) {
+    const int d = threadIdx.x;
+    float s = 0.f, m = 0.f;
+#pragma unroll
+    for (int g = 0; g < 16; ++g) {
+      s += part_sum[g][d];
+      m = fmaxf(m, part_max[g][d]);
+    }
+    const int o = (b * a.heads + head) * 128 + d;
+    atomicAdd(a.k_sum + o, s);
+    // non-negative floats order like their bit patterns
+    atomicMax(reinterpret_cast<unsigned int*>(a.v_amax) + o, __float_as_uint(m));
+  }
 }
 
 __device__ __forceinline__ uint32_t e4m3x4(float a, float b, float c, float d) {
@@ -53,8 +130,13 @@ __device__ __forceinline__ uint32_t e4m3x4(float a, float b, float c, float d) {
 }
 
 // blockIdx: x = 64-row block of this rank, y = head, z = batch * 3 + tensor (0 Q, 1 K, 2 V).
-// 256 threads: 16 per row (8 channels each), 16 rows per pass, 4 passes.
-__global__ void __launch_bounds__(256) fp8_pack_kernel(const CozyFp8Pack a) {
+// 512 threads: 16 per row (8 channels each), 32 rows per pass, 2 passes (a thread's two rows are
+// loaded before any math; 3 CTAs an SM keep 48 KB of loads in flight).
+constexpr int kPackThreads = 512;
+constexpr int kPackPasses = 64 * 16 / kPackThreads;
+
+template <bool LAW>
+__global__ void __launch_bounds__(kPackThreads, 3) fp8_pack_kernel(const CozyFp8Pack a) {
   const int tensor = blockIdx.z % 3;
   const int b = blockIdx.z / 3;
   const CozyFp8Tensor& t = a.t[tensor];
@@ -73,29 +155,41 @@ __global__ void __launch_bounds__(256) fp8_pack_kernel(const CozyFp8Pack a) {
   const int block0 = gblock * 64 - a.row0;  // may be negative: rows below lo_row are skipped
   const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(t.src) + b * t.src_strides[2] +
                              head * t.src_strides[1] + d0;
-  float mean[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  float x[kPackPasses][8];
+  {
+    uint4 raw[kPackPasses];
+#pragma unroll
+    for (int pass = 0; pass < kPackPasses; ++pass) {
+      const int r = block0 + pass * 32 + row_in;
+      raw[pass] = make_uint4(0u, 0u, 0u, 0u);
+      if (r >= lo_row && r < hi_row) raw[pass] = *reinterpret_cast<const uint4*>(src + r * t.src_strides[0]);
+    }
+#pragma unroll
+    for (int pass = 0; pass < kPackPasses; ++pass) unpack8(raw[pass], x[pass]);
+  }
+  if constexpr (LAW) {  // RMSNorm + RoPE, rounded to bf16 (rows outside: zeros, unused)
+    if (first_stage_law(t)) {
+#pragma unroll
+      for (int pass = 0; pass < kPackPasses; ++pass) {
+        const int r = block0 + pass * 32 + row_in;
+        const bool in = r >= lo_row && r < hi_row;
+        norm_rope_row<128>(x[pass], d0, chunk, row_group_mask<16>(),
+                           a.rope.token0 + (in ? r : lo_row), t, a.rope);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[pass][i] = in ? bf16_round(x[pass][i]) : 0.f;
+      }
+    }
+  }
   if (t.mean_sum != nullptr) {
     const float* ms = t.mean_sum + (b * t.heads + head) * 128 + d0;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) mean[i] = ms[i] * t.mean_inv_count;
-  }
-  float x[4][8];
-  float amax = 0.f;
+    for (int i = 0; i < 8; ++i) {
+      const float mean = ms[i] * t.mean_inv_count;
 #pragma unroll
-  for (int pass = 0; pass < 4; ++pass) {
-    const int r = block0 + pass * 16 + row_in;
-    if (r >= lo_row && r < hi_row) {
-      const uint4 v = *reinterpret_cast<const uint4*>(src + r * t.src_strides[0]);
-      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = __bfloat1622float2(h[i]);
-        x[pass][2 * i] = f.x - mean[2 * i];
-        x[pass][2 * i + 1] = f.y - mean[2 * i + 1];
+      for (int pass = 0; pass < kPackPasses; ++pass) {
+        const int r = block0 + pass * 32 + row_in;
+        if (r >= lo_row && r < hi_row) x[pass][i] -= mean;
       }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) x[pass][i] = 0.f;
     }
   }
   if (t.hadamard) {
@@ -103,7 +197,7 @@ __global__ void __launch_bounds__(256) fp8_pack_kernel(const CozyFp8Pack a) {
     // this thread's 8 channels, bits 3-6 its chunk, i.e. lanes 1, 2, 4, 8 apart in the row's
     // group of 16. Butterfly (a, b) -> (a + b, a - b); then the orthonormal 1/sqrt(128).
 #pragma unroll
-    for (int pass = 0; pass < 4; ++pass) {
+    for (int pass = 0; pass < kPackPasses; ++pass) {
 #pragma unroll
       for (int bit = 1; bit < 8; bit <<= 1)
 #pragma unroll
@@ -126,8 +220,9 @@ __global__ void __launch_bounds__(256) fp8_pack_kernel(const CozyFp8Pack a) {
       for (int i = 0; i < 8; ++i) x[pass][i] *= 0.08838834764831845f;  // 1/sqrt(128)
     }
   }
+  float amax = 0.f;
 #pragma unroll
-  for (int pass = 0; pass < 4; ++pass)
+  for (int pass = 0; pass < kPackPasses; ++pass)
 #pragma unroll
     for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(x[pass][i]));
   float inv[8];
@@ -137,14 +232,14 @@ __global__ void __launch_bounds__(256) fp8_pack_kernel(const CozyFp8Pack a) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) inv[i] = 1.f / cs[i];
   } else {  // per 64-token block: reduce the absmax over the CTA
-    __shared__ float warp_max[8];
+    __shared__ float warp_max[kPackThreads / 32];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = amax;
     __syncthreads();
     float m = warp_max[0];
 #pragma unroll
-    for (int w = 1; w < 8; ++w) m = fmaxf(m, warp_max[w]);
+    for (int w = 1; w < kPackThreads / 32; ++w) m = fmaxf(m, warp_max[w]);
     scale = fmaxf(m / kE4M3Max, kScaleFloor);
     const float is = 1.f / scale;
 #pragma unroll
@@ -157,8 +252,8 @@ __global__ void __launch_bounds__(256) fp8_pack_kernel(const CozyFp8Pack a) {
     uint8_t* dst = static_cast<uint8_t*>(t.dst[p]);
     float* sdst = t.scale_dst[p];
 #pragma unroll
-    for (int pass = 0; pass < 4; ++pass) {
-      const int r = block0 + pass * 16 + row_in;
+    for (int pass = 0; pass < kPackPasses; ++pass) {
+      const int r = block0 + pass * 32 + row_in;
       if (r < lo_row || r >= hi_row) continue;
       const uint2 codes = make_uint2(
           e4m3x4(x[pass][0] * inv[0], x[pass][1] * inv[1], x[pass][2] * inv[2], x[pass][3] * inv[3]),
@@ -172,11 +267,31 @@ __global__ void __launch_bounds__(256) fp8_pack_kernel(const CozyFp8Pack a) {
   }
 }
 
+// The RoPE table a rotating tensor reads (the bf16 first stage's checks).
+static int check_rope(const CozyRope& r) {
+  if (r.cos == nullptr || r.sin == nullptr) return cudaErrorInvalidValue;
+  if (r.rotary < 0 || r.rotary > 128 || r.rotary % 2 || r.token0 < 0) return cudaErrorInvalidValue;
+  if (!r.interleaved && r.rotary % 16) return cudaErrorNotSupported;
+  return cudaSuccess;
+}
+
 int fp8_stats(const CozyFp8Stats* a, cudaStream_t stream) {
   if (a->head_dim != 128 || a->rows < 0 || a->batch < 1 || a->heads < 1) return cudaErrorNotSupported;
+  if (a->key == nullptr || a->value == nullptr || a->k_sum == nullptr || a->v_amax == nullptr ||
+      reinterpret_cast<uintptr_t>(a->key) % 16 || reinterpret_cast<uintptr_t>(a->value) % 16)
+    return cudaErrorInvalidValue;
+  for (int k = 0; k < 3; ++k)
+    if (a->k_strides[k] % 8 || a->v_strides[k] % 8) return cudaErrorInvalidValue;
+  if (a->rotate) {
+    const int e = check_rope(a->rope);
+    if (e != cudaSuccess) return e;
+  }
   if (a->rows == 0) return cudaSuccess;
-  dim3 grid((a->rows + 255) / 256, a->heads, a->batch);
-  fp8_stats_kernel<<<grid, 128, 0, stream>>>(*a);
+  dim3 grid((a->rows + kStatsRows - 1) / kStatsRows, a->heads, a->batch);
+  if (first_stage_law(*a))
+    fp8_stats_kernel<true><<<grid, 256, 0, stream>>>(*a);
+  else
+    fp8_stats_kernel<false><<<grid, 256, 0, stream>>>(*a);
   return cudaGetLastError();
 }
 
@@ -194,6 +309,10 @@ int fp8_pack(const CozyFp8Pack* a, cudaStream_t stream) {
       if (t.head_n[p] > 0 && (t.dst[p] == nullptr || reinterpret_cast<uintptr_t>(t.dst[p]) % 8))
         return cudaErrorInvalidValue;
     heads = t.heads > heads ? t.heads : heads;
+    if (t.rotate) {
+      const int e = check_rope(a->rope);
+      if (e != cudaSuccess) return e;
+    }
   }
   if (a->rows == 0) return cudaSuccess;
   if (a->row0 < 0) return cudaErrorInvalidValue;
@@ -202,7 +321,10 @@ int fp8_pack(const CozyFp8Pack* a, cudaStream_t stream) {
     return cudaErrorInvalidValue;
   const int blocks = (a->row0 + a->rows + 63) / 64 - a->row0 / 64;
   dim3 grid(blocks, heads, a->batch * 3);
-  fp8_pack_kernel<<<grid, 256, 0, stream>>>(*a);
+  if (first_stage_law(a->t[0]) || first_stage_law(a->t[1]) || first_stage_law(a->t[2]))
+    fp8_pack_kernel<true><<<grid, kPackThreads, 0, stream>>>(*a);
+  else
+    fp8_pack_kernel<false><<<grid, kPackThreads, 0, stream>>>(*a);
   return cudaGetLastError();
 }
 

@@ -3,7 +3,9 @@
 Per rank and call: partial statistics of its rows (K sums, V channel absmax; `cozy_fp8_stats`),
 made global by the caller (one all-reduce each: SUM, MAX — the reference's `_Shift` does the
 K mean the same way, `src/cozy_runtime/internal/parallel/ulysses.py:588-604`); the first stage
-(`cozy_fp8_pack`) writes e4m3 codes of Q and K (one scale per 64-token × head block — 64 tokens
+(`cozy_fp8_pack`; per-head RMSNorm and RoPE first when asked, rounded to bf16 as the bf16 first
+stage leaves them, so RoPE, quantisation and the transpose are one pass) writes e4m3 codes of Q
+and K (one scale per 64-token × head block — 64 tokens
 of the whole sequence from a multiple of 64, cut at rank boundaries — K less the
 global mean, both rotated by the orthonormal Hadamard of order 128 first, as the reference's
 FA4-fp8 row does, `src/cozy_runtime/internal/attention_upstream.py:276-317`) and V (one scale per
@@ -28,6 +30,15 @@ SCALE_FLOOR = 1e-12
 BLOCK = 64
 
 
+def _norm_fields(t, norm) -> None:
+    """A per-head RMSNorm's fields (`ulysses.Norm` or None) into an FP8 stage descriptor."""
+    t.normalize = int(norm is not None)
+    if norm is not None:
+        t.norm_weight = norm.weight.data_ptr() if norm.weight is not None else None
+        t.norm_offset = float(norm.offset)
+        t.norm_eps = float(norm.eps)
+
+
 def scale_seq(total: int) -> int:
     """Per-token scale rows are padded to whole 128-key tiles (the kernel reads them so)."""
     return -(-total // 128) * 128
@@ -36,11 +47,15 @@ def scale_seq(total: int) -> int:
 class Fp8Step:
     """One rank's FP8 stages of one exchange (`ulysses.Plan` layout, `rank`)."""
 
-    def __init__(self, query: Tensor, key: Tensor, value: Tensor, layout, rank: int) -> None:
+    def __init__(self, query: Tensor, key: Tensor, value: Tensor, layout, rank: int, *,
+                 rope=None, norm_q=None, norm_k=None) -> None:
         if query.shape[3] != 128:
             raise ValueError("the FP8 path serves head_dim 128")
         self.query, self.key, self.value = query, key, value
         self.layout, self.rank = layout, rank
+        # the first stage's law (per-head RMSNorm, then RoPE by global position) before the
+        # recipe: `rope` a RopeSpec over the whole sequence, `norm_*` ulysses.Norm or None
+        self.rope, self.norm_q, self.norm_k = rope, norm_q, norm_k
         self.batch, self.mine, self.heads, self.dim = (int(n) for n in query.shape)
         self.heads_kv = int(key.shape[2])
         self.total = layout.total
@@ -56,6 +71,9 @@ class Fp8Step:
         st.v_strides[:] = [self.value.stride(1), self.value.stride(2), self.value.stride(0)]
         st.rows, st.batch, st.heads, st.head_dim = self.mine, self.batch, self.heads_kv, self.dim
         st.k_sum, st.v_amax = k_sum.data_ptr(), v_amax.data_ptr()
+        _norm_fields(st, self.norm_k)
+        if self.rope is not None:
+            st.rotate, st.rope = 1, self.rope.struct(self.layout.start(self.rank))
         code = _lib.load().cozy_fp8_stats(
             ctypes.byref(st), torch.cuda.current_stream(self.query.device).cuda_stream
         )
@@ -76,15 +94,19 @@ class Fp8Step:
         v_dst: Sequence[int],
         qs_dst: Sequence[int],
         ks_dst: Sequence[int],
+        scale_rows: int | None = None,
     ) -> None:
         """Codes into every peer's receive buffers (addresses of this rank's first row there)
-        and Q/K per-token scales into their scale arrays (addresses of this rank's first token)."""
+        and Q/K per-token scales into their scale arrays (addresses of this rank's first token;
+        a head's scales are `scale_rows` apart, default the padded whole sequence)."""
         lay = self.layout
         pk = _lib.Fp8Pack()
         pk.world, pk.rows, pk.batch, pk.head_dim = lay.world, self.mine, self.batch, self.dim
         pk.row0 = lay.start(self.rank)
         # start at this rank's own heads: the ranks then write to different peers at a time
         pk.head_turn = lay.q_lo[self.rank] if lay.q_n[self.rank] else 0
+        if self.rope is not None:
+            pk.rope = self.rope.struct(lay.start(self.rank))
         specs = [
             (self.query, lay.q_lo, lay.q_n, q_dst, qs_dst, None, None),
             (self.key, lay.kv_lo, lay.kv_n, k_dst, ks_dst, k_sum, None),
@@ -99,7 +121,10 @@ class Fp8Step:
             t.mean_sum = mean.data_ptr() if mean is not None else None
             t.mean_inv_count = 1.0 / self.total
             t.channel_scale = chan.data_ptr() if chan is not None else None
-            t.scale_seq = self.sseq
+            t.scale_seq = self.sseq if scale_rows is None else scale_rows
+            if i < 2:
+                _norm_fields(t, self.norm_q if i == 0 else self.norm_k)
+                t.rotate = int(self.rope is not None)
             for p in range(lay.world):
                 t.dst[p] = dst[p]
                 t.scale_dst[p] = sdst[p] if sdst is not None else None

@@ -34,6 +34,16 @@ class RopeSpec:
             self.rotary, self.interleaved,
         )
 
+    def struct(self, token0: int):
+        """The `CozyRope` a first stage reads: table row `token0` is its first row's."""
+        from cozy_runtime_b200 import _lib
+
+        r = _lib.Rope()
+        r.cos, r.sin = self.cos.data_ptr(), self.sin.data_ptr()
+        r.stride_token, r.stride_channel = self.stride_token, self.stride_channel
+        r.token0, r.rotary, r.interleaved = token0, self.rotary, int(self.interleaved)
+        return r
+
 
 def _freqs(dim: int, theta: float) -> Tensor:
     return 1.0 / (theta ** (torch.arange(0, dim, 2, dtype=torch.float64) / dim))
@@ -110,13 +120,7 @@ def head_norm_rope(
         raise ValueError("head_norm_rope serves bf16 CUDA tensors")
     batch, seq, heads, dim = x.shape
     out = torch.empty_like(x) if out is None else out
-    rope_arg = None
-    if tables is not None:
-        rope_arg = _lib.Rope()
-        rope_arg.cos, rope_arg.sin = tables.cos.data_ptr(), tables.sin.data_ptr()
-        rope_arg.stride_token, rope_arg.stride_channel = tables.stride_token, tables.stride_channel
-        rope_arg.token0, rope_arg.rotary = token0, tables.rotary
-        rope_arg.interleaved = int(tables.interleaved)
+    rope_arg = None if tables is None else tables.struct(token0)
     w = None
     if weight is not None:
         w = weight.to(device=x.device, dtype=torch.float32).contiguous()

@@ -267,15 +267,7 @@ def _pack_tensor(
 
 
 def _rope_struct(rope: RopeSpec, token0: int) -> _lib.Rope:
-    r = _lib.Rope()
-    r.cos = rope.cos.data_ptr()
-    r.sin = rope.sin.data_ptr()
-    r.stride_token = rope.stride_token
-    r.stride_channel = rope.stride_channel
-    r.token0 = token0
-    r.rotary = rope.rotary
-    r.interleaved = int(rope.interleaved)
-    return r
+    return rope.struct(token0)
 
 
 def pack(
@@ -529,7 +521,8 @@ def _exchange(
     (NCCL all-to-all); default `COZY_ULYSSES_TRANSPORT`, else "peer" for native attention on a
     CUDA group of one node. `fp8`: Q, K and V cross and multiply as e4m3 (`fp8.Fp8Step`: K less
     its global mean, Q/K Hadamard-rotated with 64-token block scales, V per-channel scales, P as
-    e4m3; head_dim 128, native attention, degree 1 or the peer transport). `narrow` (or
+    e4m3; head_dim 128, native attention, either transport; RMSNorm/RoPE fused into the e4m3
+    first stage). `narrow` (or
     `narrow(total)`): Q, K less its turned global mean, V and the output cross as int8 with a
     bf16 scale per row after a Hadamard turn (`narrow.NarrowStep`, the reference's wire; head
     dims 64 and 128; any dimension that is not a power of two stays wide, as in the reference).
@@ -574,12 +567,12 @@ def _exchange(
         )
 
     if fp8:
-        if compute is not None or rope is not None or norm_q is not None or norm_k is not None:
-            raise NotImplementedError("the FP8 path serves native attention without RoPE/RMSNorm")
-        if world > 1 and (_transport(handle, transport) != "peer"
-                          or not _peer_ready(handle, query.device)):
-            raise NotImplementedError("the FP8 path crosses over the peer transport only")
-        return _exchange_fp8(query, key, value, handle, layout, rank, began, causal, scale)
+        if compute is not None:
+            raise NotImplementedError("the FP8 path serves the native e4m3 attention only")
+        over_peer = world > 1 and (_transport(handle, transport) == "peer"
+                                   and _peer_ready(handle, query.device))
+        return _exchange_fp8(query, key, value, handle, layout, rank, began, causal, scale,
+                             rope=rope, norm_q=norm_q, norm_k=norm_k, over_peer=over_peer)
     if world == 1 and rope is None and norm_q is None and norm_k is None and compute is None:
         out = torch.empty((batch, mine, heads, dim), dtype=query.dtype, device=query.device)
         first = _Clock.mark(query)
@@ -956,15 +949,22 @@ def _exchange_fp8(
     began,
     causal: bool,
     scale: float | None,
+    *,
+    rope: RopeSpec | None = None,
+    norm_q: Norm | None = None,
+    norm_k: Norm | None = None,
+    over_peer: bool = True,
 ) -> Tensor:
     """The FP8 exchange: statistics all-reduced (K sums, V channel absmax), e4m3 codes and their
-    scales written into every owner's receive buffers (peer transport; local at degree 1), the
-    e4m3 attention, bf16 rows to their owners."""
+    scales written into every owner's receive buffers (peer transport; local at degree 1) or
+    into per-destination send blocks crossing by NCCL all-to-all, the e4m3 attention, bf16 rows
+    to their owners. RMSNorm / RoPE, when given, run inside the e4m3 first stage."""
     batch, mine, heads, dim = (int(n) for n in query.shape)
     heads_kv = int(key.shape[2])
     device = query.device
     world, total, rows = layout.world, layout.total, layout.rows
-    step = fp8_mod.Fp8Step(query, key, value, layout, rank)
+    step = fp8_mod.Fp8Step(query, key, value, layout, rank, rope=rope, norm_q=norm_q,
+                           norm_k=norm_k)
     k_sum = torch.zeros(batch, heads_kv, dim, dtype=torch.float32, device=device)
     v_amax = torch.zeros(batch, heads_kv, dim, dtype=torch.float32, device=device)
     step.stats_into(k_sum, v_amax)
@@ -989,6 +989,8 @@ def _exchange_fp8(
         step.attend(q8, k8, v8, qs, ks, v_local, causal=causal, scale=scale, into=out)
         _CLOCK.add((began, first, _Clock.mark(query), _Clock.mark(query)), 0)
         return out
+    if not over_peer:
+        return _exchange_fp8_nccl(step, k_sum, v_scale, v_local, handle, began, causal, scale)
     sizes = {
         "q8": total * batch * max(layout.q_n) * dim,
         "k8": total * batch * max(layout.kv_n) * dim,
@@ -1030,6 +1032,80 @@ def _exchange_fp8(
         land = pg.view(s, "land", query.dtype)[: batch * mine * heads * dim]
         out.copy_(land.view(batch, mine, heads, dim))
     _CLOCK.add((began, first, last, _Clock.mark(query)), 0)
+    return out
+
+
+def _exchange_fp8_nccl(step, k_sum: Tensor, v_scale: Tensor, v_local: Tensor, handle, began,
+                       causal: bool, scale: float | None) -> Tensor:
+    """The FP8 exchange over NCCL: the e4m3 first stage writes per-destination send blocks
+    (codes [rows][B][n_p][128]; block scales [B][n_p][rows]), four all-to-alls move codes and
+    scales, the scales are laid out per head over the whole sequence, and the bf16 output returns
+    as the bf16 path's does (all-to-all, then `land`)."""
+    query = step.query
+    lay, rank, device = step.layout, step.rank, query.device
+    batch, mine, dim = step.batch, step.mine, step.dim
+    world, total = lay.world, lay.total
+    qn, kvn = lay.q_n[rank], lay.kv_n[rank]
+    u8, f32 = torch.uint8, torch.float32
+    q_sizes = [mine * batch * lay.q_n[p] * dim for p in range(world)]
+    kv_sizes = [mine * batch * lay.kv_n[p] * dim for p in range(world)]
+    qs_sizes = [batch * lay.q_n[p] * mine for p in range(world)]
+    ks_sizes = [batch * lay.kv_n[p] * mine for p in range(world)]
+    q_send = torch.empty(sum(q_sizes), dtype=u8, device=device)
+    k_send = torch.empty(sum(kv_sizes), dtype=u8, device=device)
+    v_send = torch.empty(sum(kv_sizes), dtype=u8, device=device)
+    qs_send = torch.empty(sum(qs_sizes), dtype=f32, device=device)
+    ks_send = torch.empty(sum(ks_sizes), dtype=f32, device=device)
+
+    def at(buf: Tensor, sizes: Sequence[int]) -> list[int]:
+        return [buf.data_ptr() + off * buf.element_size() for off in _offsets(sizes)]
+
+    sseq = step.sseq
+    # send blocks hold this rank's rows only: a head's scales are `mine` apart there
+    step.pack_to(k_sum, v_scale, at(q_send, q_sizes), at(k_send, kv_sizes), at(v_send, kv_sizes),
+                 at(qs_send, qs_sizes), at(ks_send, ks_sizes), scale_rows=mine)
+    rows = lay.rows
+    q_in = [r * batch * qn * dim for r in rows]
+    kv_in = [r * batch * kvn * dim for r in rows]
+    q8 = torch.empty(sum(q_in), dtype=u8, device=device)
+    k8 = torch.empty(sum(kv_in), dtype=u8, device=device)
+    v8 = torch.empty(sum(kv_in), dtype=u8, device=device)
+    qs_in = [batch * qn * r for r in rows]
+    ks_in = [batch * kvn * r for r in rows]
+    qs_got = torch.empty(sum(qs_in), dtype=f32, device=device)
+    ks_got = torch.empty(sum(ks_in), dtype=f32, device=device)
+    with _Crossing(handle) as crossing:
+        crossing.crossed = True
+        dist.all_to_all_single(q8, q_send, q_in, q_sizes, group=handle)
+        dist.all_to_all_single(k8, k_send, kv_in, kv_sizes, group=handle)
+        dist.all_to_all_single(v8, v_send, kv_in, kv_sizes, group=handle)
+        dist.all_to_all_single(qs_got, qs_send, qs_in, qs_sizes, group=handle)
+        dist.all_to_all_single(ks_got, ks_send, ks_in, ks_sizes, group=handle)
+
+        def whole(got: Tensor, n: int, sizes: Sequence[int]) -> Tensor:
+            # source blocks [B][n][rows_s] side by side -> [B][n][scale_seq], padding zero
+            out = torch.zeros(batch, max(n, 1), sseq, dtype=f32, device=device)
+            if n:
+                parts = [t.view(batch, n, r) for t, r in zip(torch.split(got, sizes), rows,
+                                                              strict=True)]
+                out[:, :, :total] = torch.cat(parts, dim=2)
+            return out.view(-1)
+
+        qs, ks = whole(qs_got, qn, qs_in), whole(ks_got, kvn, ks_in)
+        o_send = torch.empty(total * batch * qn * dim, dtype=query.dtype, device=device)
+        first = _Clock.mark(query)
+        if qn:
+            ov = o_send.view(total, batch, qn, dim).permute(1, 0, 2, 3)
+            step.attend(q8, k8, v8, qs, ks, v_local, causal=causal, scale=scale, into=ov)
+        last = _Clock.mark(query)
+        back = RankStep(query, step.key, step.value, lay, rank)
+        returned = torch.empty(sum(back.back_sizes), dtype=query.dtype, device=device)
+        dist.all_to_all_single(returned, o_send, back.back_sizes, back.back_in, group=handle)
+        out = back.land(returned)
+    moved = (sum(q_sizes) - q_sizes[rank] + 2 * (sum(kv_sizes) - kv_sizes[rank])
+             + 4 * (sum(qs_sizes) - qs_sizes[rank] + sum(ks_sizes) - ks_sizes[rank])
+             + query.element_size() * (sum(back.back_in) - back.back_in[rank]))
+    _CLOCK.add((began, first, last, _Clock.mark(query)), moved)
     return out
 
 

@@ -162,7 +162,9 @@ COZY_API int cozy_ulysses_land(const void* returned, int world, int rows, int ba
  * (attention_upstream.py:293-317). head_dim 128. */
 
 /* This rank's partial statistics: k_sum[b][h][d] += Σ_rows key, v_amax[b][h][d] = max(|value|)
- * (the caller zero-fills both and all-reduces them: SUM and MAX). */
+ * (the caller zero-fills both and all-reduces them: SUM and MAX). The keys summed are the first
+ * stage's keys: per-head RMSNorm (when `normalize`) then RoPE (when `rotate`, table row
+ * rope.token0 + row) in fp32, rounded to bf16 — the keys the FP8 first stage quantises. */
 typedef struct CozyFp8Stats {
   const void* key;
   const void* value;
@@ -171,6 +173,12 @@ typedef struct CozyFp8Stats {
   int rows, batch, heads, head_dim;
   float* k_sum;
   float* v_amax;
+  int normalize;            /* K's per-head RMSNorm: weight NULL = unit, else weight + offset */
+  const float* norm_weight;
+  float norm_offset;
+  float norm_eps;
+  int rotate;               /* RoPE per `rope` */
+  CozyRope rope;
 } CozyFp8Stats;
 
 /* One tensor of the FP8 first stage. Block mode (Q, K): `channel_scale` NULL; the per-token
@@ -180,7 +188,10 @@ typedef struct CozyFp8Stats {
  * the row times the orthonormal Hadamard matrix (QKᵀ is unchanged; a channel outlier spreads over
  * the head before its block scale is taken), as the reference's FA4-fp8 path rotates Q and K
  * (src/cozy_runtime/internal/attention_upstream.py:276-317). Codes go to dst[p] as
- * [rows][batch][head_n[p]][128] bytes, as CozyPackTensor. */
+ * [rows][batch][head_n[p]][128] bytes, as CozyPackTensor. `normalize` / `rotate` (Q and K): the
+ * first stage's per-head RMSNorm and RoPE (CozyFp8Pack.rope, table row rope.token0 + row) come
+ * first, in fp32, rounded to bf16 as the bf16 first stage rounds them; the FP8 recipe then
+ * applies to those values, so RoPE, quantisation and the transpose are one pass over HBM. */
 typedef struct CozyFp8Tensor {
   const void* src;
   long long src_strides[3];
@@ -194,6 +205,11 @@ typedef struct CozyFp8Tensor {
   long long scale_seq;
   int head_lo[COZY_MAX_PEERS];
   int head_n[COZY_MAX_PEERS];
+  int normalize;
+  const float* norm_weight;
+  float norm_offset;
+  float norm_eps;
+  int rotate;
 } CozyFp8Tensor;
 
 typedef struct CozyFp8Pack {
@@ -204,6 +220,7 @@ typedef struct CozyFp8Pack {
   int head_turn; /* the first head (of Q; K/V: the same fraction of theirs) the launch packs,
                     then the next ones round: a rank starting at its own heads writes to a
                     different peer than the other ranks at any moment */
+  CozyRope rope; /* read by tensors with `rotate` */
 } CozyFp8Pack;
 
 COZY_API int cozy_fp8_stats(const CozyFp8Stats* stats, uintptr_t stream);

@@ -24,7 +24,9 @@ def _offsets(sizes):
     return np.concatenate([[0], np.cumsum(sizes)[:-1]]).astype(int).tolist()
 
 
-def simulate_fp8(q, k, v, world, *, causal=False, on_device=False):
+def simulate_fp8(q, k, v, world, *, causal=False, on_device=False, rope=None, norm=None):
+    """W ranks' FP8 stages on one GPU; `rope` (RopeSpec on the GPU) and `norm` (ulysses.Norm,
+    Q and K) run inside the e4m3 first stage."""
     from cozy_runtime_b200 import _lib, fp8, ulysses
 
     batch, total, heads, dim = q.shape
@@ -35,7 +37,7 @@ def simulate_fp8(q, k, v, world, *, causal=False, on_device=False):
     dev = torch.device("cuda")
     steps = [
         fp8.Fp8Step(*(t[:, starts[r] : starts[r] + rows[r]].contiguous().to(dev) for t in (q, k, v)),
-                    layout, r)
+                    layout, r, rope=rope, norm_q=norm, norm_k=norm)
         for r in range(world)
     ]
     k_sum = torch.zeros(batch, hkv, dim, dtype=torch.float32, device=dev)
@@ -136,6 +138,77 @@ def test_fp8_exchange_public_call_degree1():
     law = oracle.fp8_attention_law([q], [k], [v])
     assert _cosine_per_head(got.float().cpu(), law).min().item() >= 0.999
     exact = oracle.attention_fp32(q, k, v)
+    assert _cosine_per_head(got.float().cpu(), exact).min().item() >= 0.995
+
+
+def _first_stage(x, spec, norm):
+    """The first stage's law (oracle, fp64 on the CPU) on [B, S, H, D], rounded to bf16."""
+    if spec is None:
+        return oracle.head_norm_rope(x, torch.ones(x.shape[1], 1), torch.zeros(x.shape[1], 1),
+                                     rotary=0, interleaved=True,
+                                     normalize=norm).to(torch.bfloat16)
+    cos = spec.cos.cpu().reshape(-1, spec.stride_token)
+    sin = spec.sin.cpu().reshape(-1, spec.stride_token)
+    return oracle.head_norm_rope(x, cos, sin, rotary=spec.rotary, interleaved=spec.interleaved,
+                                 normalize=norm,
+                                 stride_channel=spec.stride_channel).to(torch.bfloat16)
+
+
+def _rope_case(name, seq):
+    from cozy_runtime_b200 import rope as rope_mod
+
+    if name == "video":  # 3-D axial (C2's split), text tokens after the grid
+        return rope_mod.axial((2, 6, 10), (44, 42, 42), after=seq - 120)
+    if name == "image":  # 2-D axial (C3's split, theta 1e4), text tokens before the grid
+        return rope_mod.axial((1, 16, 16), (16, 56, 56), 10000.0, before=seq - 256)
+    return rope_mod.llama(seq, 128, 500000.0)  # 1-D split-half (C5's)
+
+
+@pytest.mark.parametrize(
+    "world,batch,seq,hq,hkv,causal,rope_name,norm",
+    [(1, 1, 632, 4, 4, False, "video", False), (4, 2, 512 + 256, 8, 8, False, "image", True),
+     (3, 1, 1000, 6, 2, True, "llama", False), (2, 1, 700, 4, 4, False, None, True)],
+)
+def test_fp8_with_rope_and_norm(world, batch, seq, hq, hkv, causal, rope_name, norm):
+    """RMSNorm / RoPE fused into the e4m3 first stage (one pass: norm, RoPE, bf16 rounding, K
+    mean, Hadamard, block scales, transpose to the owners): against the recipe's law over the
+    first stage's bf16 output (cosine ≥ 0.999) and against exact attention over it (≥ 0.995)."""
+    from cozy_runtime_b200 import attention, ulysses
+
+    q, k, v = _inputs(batch, seq, hq, hkv, seq + 5 * world)
+    spec = _rope_case(rope_name, seq) if rope_name else None
+    nm = ulysses.Norm() if norm else None
+    got = simulate_fp8(q, k, v, world, causal=causal, rope=None if spec is None else spec.to("cuda"),
+                       norm=nm)
+    attention.check_status(torch.device("cuda"))
+    qr, kr = _first_stage(q, spec, norm), _first_stage(k, spec, norm)
+    rows = [t.shape[0] for t in torch.tensor_split(torch.empty(seq), world)]
+    parts = [torch.split(t, rows, dim=1) for t in (qr, kr, v)]
+    law = oracle.fp8_attention_law(*parts, causal=causal)
+    cos_law = _cosine_per_head(got, law)
+    cos = _cosine_per_head(got, oracle.attention_fp32(qr, kr, v, causal=causal))
+    print(f"fp8+{rope_name}/{norm} W={world}: law cos {cos_law.min().item():.6f}, "
+          f"exact cos {cos.min().item():.6f}")
+    assert (got - law).abs().mean().item() <= 2.5e-3
+    assert cos_law.min().item() >= 0.999, f"vs law cosine {cos_law.min().item():.5f}"
+    assert cos.min().item() >= 0.995, f"cosine {cos.min().item():.5f}"
+
+
+def test_fp8_public_call_with_rope_degree1():
+    """`ulysses.exchange(..., fp8=True, rope=..., norm_q=..., norm_k=...)` at degree 1."""
+    from cozy_runtime_b200 import attention, ulysses
+
+    q, k, v = _inputs(1, 632, 3, 3, 78)
+    spec = _rope_case("video", 632)
+    nm = ulysses.Norm()
+    got = ulysses.exchange(q.cuda(), k.cuda(), v.cuda(), None, None, fp8=True,
+                           rope=spec.to("cuda"), norm_q=nm, norm_k=nm)
+    torch.cuda.synchronize()
+    attention.check_status(torch.device("cuda"))
+    qr, kr = _first_stage(q, spec, True), _first_stage(k, spec, True)
+    law = oracle.fp8_attention_law([qr], [kr], [v])
+    assert _cosine_per_head(got.float().cpu(), law).min().item() >= 0.999
+    exact = oracle.attention_fp32(qr, kr, v)
     assert _cosine_per_head(got.float().cpu(), exact).min().item() >= 0.995
 
 

@@ -72,10 +72,16 @@ def _cases() -> list[dict]:
             out.append({"id": f"oracle-w{world}-{hq}-{hkv}-{causal}-{rotate}-{transport}",
                         "world": world, "seed": world + hq, "seq": 2 * 6 * 10 + TEXT, "hq": hq,
                         "hkv": hkv, "causal": causal, "rotate": rotate, "transport": transport})
-    for world, hq, hkv, causal in [(2, 4, 4, False), (8, 16, 16, False), (4, 8, 2, True)]:
-        out.append({"id": f"fp8-w{world}-{hq}-{hkv}-{causal}", "world": world,
+    for world, hq, hkv, causal, transport in [(2, 4, 4, False, "peer"), (8, 16, 16, False, "peer"),
+                                              (4, 8, 2, True, "peer"), (2, 4, 4, False, "nccl"),
+                                              (4, 8, 2, True, "nccl"), (8, 16, 16, False, "nccl")]:
+        out.append({"id": f"fp8-w{world}-{hq}-{hkv}-{causal}-{transport}", "world": world,
                     "seed": world * 7 + hq, "seq": 1000, "hq": hq, "hkv": hkv, "causal": causal,
-                    "outliers": True, "fp8": True, "transport": "peer"})
+                    "outliers": True, "fp8": True, "transport": transport})
+    for world, transport in [(2, "peer"), (4, "nccl"), (8, "peer")]:  # RoPE in the e4m3 stage
+        out.append({"id": f"fp8rope-w{world}-{transport}", "world": world, "seed": 60 + world,
+                    "seq": 2 * 6 * 10 + TEXT, "hq": 8, "hkv": 8, "causal": False,
+                    "rotate": True, "fp8": True, "transport": transport})
     for name in narrow_cases():
         world = int(load(name)["world"])
         for transport in ("peer", "nccl"):
@@ -206,13 +212,21 @@ def test_exchange_against_oracle(case_id):
     _check(got, oracle.attention_fp32(q, k, v, causal=case["causal"]))
 
 
-@pytest.mark.parametrize("case_id", [c for c in CASES if c.startswith("fp8-")])
-def test_fp8_exchange_peer_against_law(case_id):
-    """The FP8 path over the NVLink transport (statistics all-reduced, e4m3 codes and scales
-    stored into the owners' buffers) against the oracle's FP8 law and exact attention."""
+@pytest.mark.parametrize("case_id", [c for c in CASES if c.startswith("fp8")])
+def test_fp8_exchange_against_law(case_id):
+    """The FP8 path between processes (statistics all-reduced; e4m3 codes and scales stored
+    into the owners' buffers over NVLink, or crossing by NCCL all-to-all), with RoPE fused into
+    the e4m3 first stage in the `fp8rope` cases, against the oracle's FP8 law and exact
+    attention over the first stage's output."""
+    from cozy_runtime_b200 import rope as rope_mod
+
     case = CASES[case_id]
     got = _result(case_id).float()
     q, k, v = inputs_of(case)
+    if case.get("rotate"):
+        spec = rope_mod.axial(GRID, (44, 42, 42), after=TEXT)
+        q, k = (oracle.head_norm_rope(t.float(), spec.cos, spec.sin, rotary=128, interleaved=True,
+                                      normalize=False).to(torch.bfloat16) for t in (q, k))
     rows = [t.shape[0] for t in torch.tensor_split(torch.empty(case["seq"]), case["world"])]
     law = oracle.fp8_attention_law(*(torch.split(t, rows, dim=1) for t in (q, k, v)),
                                    causal=case["causal"])
