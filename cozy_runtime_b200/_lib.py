@@ -123,6 +123,8 @@ class Fp8Tensor(Structure):
         ("norm_offset", c_float),
         ("norm_eps", c_float),
         ("rotate", c_int),
+        ("head_scale", c_void_p),
+        ("head_amax", c_void_p),
     ]
 
 
@@ -138,6 +140,7 @@ class Fp8Pack(Structure):
         ("row0", c_int),
         ("head_turn", c_int),
         ("rope", Rope),
+        ("per_head", c_int),
     ]
 
 
@@ -278,6 +281,7 @@ SIGNATURES = {
         c_int,
     ),
     "cozy_fp8_stats": ([POINTER(Fp8Stats), c_uint64], c_int),
+    "cozy_fp8_head_amax": ([POINTER(Fp8Pack), c_uint64], c_int),
     "cozy_fp8_pack": ([POINTER(Fp8Pack), c_uint64], c_int),
     "cozy_attention_fwd_fp8": (
         [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_longlong,

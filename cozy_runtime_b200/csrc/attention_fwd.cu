@@ -384,6 +384,10 @@ __device__ __forceinline__ void scale_chunk(uint32_t (&r)[32], const float4* ks)
 }
 
 // 32 scores -> 32 e4m3 codes of 2^(s·scale + bias) packed four to a word, summed into `acc`.
+// (The MUFU unit's f16-pair form, ex2.approx.f16x2, was measured on B200 at the same 16 results
+// per clock per SM as the fp32 form — two results an instruction at half the instruction rate —
+// and an e4m3 P path through it ran 21 % slower: 1007 against 1270 TFLOP/s at C4's per-GPU
+// shape.)
 __device__ __forceinline__ void exp_chunk_fp8(const uint32_t (&r)[32], float2 scale2, float2 bias2,
                                               float2& acc, uint32_t* pk) {
 #pragma unroll
@@ -407,48 +411,6 @@ __device__ __forceinline__ void exp_chunk_fp8(const uint32_t (&r)[32], float2 sc
     pk[i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
   }
 }
-
-// 32 scores -> 32 e4m3 codes of 2^(s·scale + bias) packed four to a word, with the exponentials
-// of two keys in one MUFU instruction (ex2.approx.f16x2): t is formed in fp32, rounded to f16
-// (for t in [-16, 8.5] an error of at most 2^-8, 0.3 % of p, against e4m3's 6 % steps), and
-// the codes are converted from the f16 pairs. The row sum adds the f16 results in pairs of
-// partial sums of 8 keys (each at most 8·2^8.5 < 2^12, so at most 2^-11 relative) and those in
-// fp32 into `acc`.
-__device__ __forceinline__ void exp_chunk_fp8_half(const uint32_t (&r)[32], float2 scale2,
-                                                   float2 bias2, float2& acc, uint32_t* pk) {
-  uint32_t part0 = 0u, part1 = 0u;  // f16x2 partial sums, +0
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    uint32_t e[2];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int k = 4 * i + 2 * h;
-      const float2 t = __ffma2_rn(make_float2(__uint_as_float(r[k]), __uint_as_float(r[k + 1])),
-                                  scale2, bias2);
-      uint32_t th;
-      asm("cvt.rn.f16x2.f32 %0, %2, %1;" : "=r"(th) : "f"(t.x), "f"(t.y));
-      asm("ex2.approx.f16x2 %0, %1;" : "=r"(e[h]) : "r"(th));
-    }
-    asm("add.rn.f16x2 %0, %0, %1;" : "+r"(part0) : "r"(e[0]));
-    asm("add.rn.f16x2 %0, %0, %1;" : "+r"(part1) : "r"(e[1]));
-    uint16_t lo, hi;
-    asm("cvt.rn.satfinite.e4m3x2.f16x2 %0, %1;" : "=h"(lo) : "r"(e[0]));
-    asm("cvt.rn.satfinite.e4m3x2.f16x2 %0, %1;" : "=h"(hi) : "r"(e[1]));
-    pk[i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
-  }
-  float2 a, b;
-  asm("{.reg .f16 l, h;\n mov.b32 {l, h}, %2;\n cvt.f32.f16 %0, l;\n cvt.f32.f16 %1, h;\n}"
-      : "=f"(a.x), "=f"(a.y) : "r"(part0));
-  asm("{.reg .f16 l, h;\n mov.b32 {l, h}, %2;\n cvt.f32.f16 %0, l;\n cvt.f32.f16 %1, h;\n}"
-      : "=f"(b.x), "=f"(b.y) : "r"(part1));
-  acc = __fadd2_rn(acc, __fadd2_rn(a, b));
-}
-
-// The FP8 kernel's exponentials: f16 pairs on the MUFU unit (1) or fp32 with the FMA-pipe
-// polynomial share (0).
-#ifndef COZY_FP8_HALF_EXP
-#define COZY_FP8_HALF_EXP 0
-#endif
 
 template <int HD, bool FP8, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -632,24 +594,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         // P as e4m3 codes of 2^(t + 8) (≤ 256·2^0.5 < 448); the row sum carries the same 2^8
         const float2 negm2 = make_float2(kPScaleLog2 - mu, kPScaleLog2 - mu);
         uint32_t pk[16];
-        if constexpr (COZY_FP8_HALF_EXP) {
-          exp_chunk_fp8_half(r0, scale_lo, negm2, acc0, pk);
-          exp_chunk_fp8_half(r1, scale_lo, negm2, acc1, pk + 8);
-        } else {
-          exp_chunk_fp8(r0, scale_lo, negm2, acc0, pk);
-          exp_chunk_fp8(r1, scale_lo, negm2, acc1, pk + 8);
-        }
+        exp_chunk_fp8(r0, scale_lo, negm2, acc0, pk);
+        exp_chunk_fp8(r1, scale_lo, negm2, acc1, pk + 8);
         tmem_st16(tS + 0, pk);
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&p_ready[2 * s]);
-        if constexpr (COZY_FP8_HALF_EXP) {
-          exp_chunk_fp8_half(r2, scale_hi, negm2, acc0, pk);
-          exp_chunk_fp8_half(r3, scale_hi, negm2, acc1, pk + 8);
-        } else {
-          exp_chunk_fp8(r2, scale_hi, negm2, acc0, pk);
-          exp_chunk_fp8(r3, scale_hi, negm2, acc1, pk + 8);
-        }
+        exp_chunk_fp8(r2, scale_hi, negm2, acc0, pk);
+        exp_chunk_fp8(r3, scale_hi, negm2, acc1, pk + 8);
         tmem_st16(tS + 16, pk);
       } else {
         const float2 negm2 = make_float2(-mu, -mu);

@@ -127,6 +127,7 @@ int attention_forward_fp8(const void* q, const void* k, const void* v, const flo
                           float scale, int* status, cudaStream_t stream);
 int fp8_stats(const CozyFp8Stats* a, cudaStream_t stream);
 int fp8_pack(const CozyFp8Pack* a, cudaStream_t stream);
+int fp8_head_amax(const CozyFp8Pack* a, cudaStream_t stream);
 }  // namespace cozy
 
 extern "C" {
@@ -140,6 +141,11 @@ int cozy_fp8_stats(const CozyFp8Stats* stats, uintptr_t stream) {
 int cozy_fp8_pack(const CozyFp8Pack* pack, uintptr_t stream) {
   if (!pack) return cudaErrorInvalidValue;
   return cozy::fp8_pack(pack, as_stream(stream));
+}
+
+int cozy_fp8_head_amax(const CozyFp8Pack* pack, uintptr_t stream) {
+  if (!pack) return cudaErrorInvalidValue;
+  return cozy::fp8_head_amax(pack, as_stream(stream));
 }
 
 int cozy_attention_fwd_fp8(const void* q, const void* k, const void* v, const float* q_scale,

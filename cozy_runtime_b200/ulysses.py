@@ -509,7 +509,7 @@ def _exchange(
     norm_q: Norm | None = None,
     norm_k: Norm | None = None,
     transport: str | None = None,
-    fp8: bool = False,
+    fp8: bool | str = False,
 ) -> Tensor:
     """Sequence shards -> whole sequences per head subset -> attention -> back.
 
@@ -522,7 +522,8 @@ def _exchange(
     CUDA group of one node. `fp8`: Q, K and V cross and multiply as e4m3 (`fp8.Fp8Step`: K less
     its global mean, Q/K Hadamard-rotated with 64-token block scales, V per-channel scales, P as
     e4m3; head_dim 128, native attention, either transport; RMSNorm/RoPE fused into the e4m3
-    first stage). `narrow` (or
+    first stage); `fp8="head"`: the reference's own FP8 row instead (`fa4_fp8`: Hadamard-rotated
+    Q and K, one e4m3 scale per (batch, head) of Q, K and V, target 440). `narrow` (or
     `narrow(total)`): Q, K less its turned global mean, V and the output cross as int8 with a
     bf16 scale per row after a Hadamard turn (`narrow.NarrowStep`, the reference's wire; head
     dims 64 and 128; any dimension that is not a power of two stays wide, as in the reference).
@@ -567,12 +568,15 @@ def _exchange(
         )
 
     if fp8:
+        if fp8 is not True and fp8 not in fp8_mod.LAWS:
+            raise ValueError(f"fp8={fp8!r}: True (the block recipe) or one of {fp8_mod.LAWS}")
         if compute is not None:
             raise NotImplementedError("the FP8 path serves the native e4m3 attention only")
         over_peer = world > 1 and (_transport(handle, transport) == "peer"
                                    and _peer_ready(handle, query.device))
         return _exchange_fp8(query, key, value, handle, layout, rank, began, causal, scale,
-                             rope=rope, norm_q=norm_q, norm_k=norm_k, over_peer=over_peer)
+                             rope=rope, norm_q=norm_q, norm_k=norm_k, over_peer=over_peer,
+                             law="head" if fp8 == "head" else "block")
     if world == 1 and rope is None and norm_q is None and norm_k is None and compute is None:
         out = torch.empty((batch, mine, heads, dim), dtype=query.dtype, device=query.device)
         first = _Clock.mark(query)
@@ -954,25 +958,20 @@ def _exchange_fp8(
     norm_q: Norm | None = None,
     norm_k: Norm | None = None,
     over_peer: bool = True,
+    law: str = "block",
 ) -> Tensor:
-    """The FP8 exchange: statistics all-reduced (K sums, V channel absmax), e4m3 codes and their
-    scales written into every owner's receive buffers (peer transport; local at degree 1) or
-    into per-destination send blocks crossing by NCCL all-to-all, the e4m3 attention, bf16 rows
-    to their owners. RMSNorm / RoPE, when given, run inside the e4m3 first stage."""
+    """The FP8 exchange: statistics all-reduced (block law: K sums and V channel absmax;
+    per-head law: Q, K, V absmax per head), e4m3 codes and their scales written into every
+    owner's receive buffers (peer transport; local at degree 1) or into per-destination send
+    blocks crossing by NCCL all-to-all, the e4m3 attention, bf16 rows to their owners. RMSNorm /
+    RoPE, when given, run inside the e4m3 first stage."""
     batch, mine, heads, dim = (int(n) for n in query.shape)
-    heads_kv = int(key.shape[2])
     device = query.device
     world, total, rows = layout.world, layout.total, layout.rows
     step = fp8_mod.Fp8Step(query, key, value, layout, rank, rope=rope, norm_q=norm_q,
-                           norm_k=norm_k)
-    k_sum = torch.zeros(batch, heads_kv, dim, dtype=torch.float32, device=device)
-    v_amax = torch.zeros(batch, heads_kv, dim, dtype=torch.float32, device=device)
-    step.stats_into(k_sum, v_amax)
-    if world > 1:
-        dist.all_reduce(k_sum, op=dist.ReduceOp.SUM, group=handle)
-        dist.all_reduce(v_amax, op=dist.ReduceOp.MAX, group=handle)
-    v_scale = fp8_mod.Fp8Step.channel_scale(v_amax)
-    v_local = step.local_v_scale(v_scale)
+                           norm_k=norm_k, law=law)
+    scales = step.scales(handle if world > 1 else None)
+    v_local = step.local_v_scale(scales.v_scale)
     sseq = step.sseq
     qn, kvn = layout.q_n[rank], layout.kv_n[rank]
     if world == 1:
@@ -982,7 +981,7 @@ def _exchange_fp8(
         v8 = torch.empty(total * batch * kvn * dim, dtype=u8, device=device)
         qs = torch.zeros(batch * qn * sseq, dtype=f32, device=device)
         ks = torch.zeros(batch * kvn * sseq, dtype=f32, device=device)
-        step.pack_to(k_sum, v_scale, [q8.data_ptr()], [k8.data_ptr()], [v8.data_ptr()],
+        step.pack_to(scales, [q8.data_ptr()], [k8.data_ptr()], [v8.data_ptr()],
                      [qs.data_ptr()], [ks.data_ptr()])
         out = torch.empty((batch, mine, heads, dim), dtype=query.dtype, device=device)
         first = _Clock.mark(query)
@@ -990,7 +989,7 @@ def _exchange_fp8(
         _CLOCK.add((began, first, _Clock.mark(query), _Clock.mark(query)), 0)
         return out
     if not over_peer:
-        return _exchange_fp8_nccl(step, k_sum, v_scale, v_local, handle, began, causal, scale)
+        return _exchange_fp8_nccl(step, scales, v_local, handle, began, causal, scale)
     sizes = {
         "q8": total * batch * max(layout.q_n) * dim,
         "k8": total * batch * max(layout.kv_n) * dim,
@@ -1008,7 +1007,7 @@ def _exchange_fp8(
         start = layout.start(rank)
         r = range(world)
         step.pack_to(
-            k_sum, v_scale,
+            scales,
             [pg.peer(p, s, "q8") + start * batch * layout.q_n[p] * dim for p in r],
             [pg.peer(p, s, "k8") + start * batch * layout.kv_n[p] * dim for p in r],
             [pg.peer(p, s, "v8") + start * batch * layout.kv_n[p] * dim for p in r],
@@ -1035,8 +1034,8 @@ def _exchange_fp8(
     return out
 
 
-def _exchange_fp8_nccl(step, k_sum: Tensor, v_scale: Tensor, v_local: Tensor, handle, began,
-                       causal: bool, scale: float | None) -> Tensor:
+def _exchange_fp8_nccl(step, scales, v_local: Tensor, handle, began, causal: bool,
+                       scale: float | None) -> Tensor:
     """The FP8 exchange over NCCL: the e4m3 first stage writes per-destination send blocks
     (codes [rows][B][n_p][128]; block scales [B][n_p][rows]), four all-to-alls move codes and
     scales, the scales are laid out per head over the whole sequence, and the bf16 output returns
@@ -1062,7 +1061,7 @@ def _exchange_fp8_nccl(step, k_sum: Tensor, v_scale: Tensor, v_local: Tensor, ha
 
     sseq = step.sseq
     # send blocks hold this rank's rows only: a head's scales are `mine` apart there
-    step.pack_to(k_sum, v_scale, at(q_send, q_sizes), at(k_send, kv_sizes), at(v_send, kv_sizes),
+    step.pack_to(scales, at(q_send, q_sizes), at(k_send, kv_sizes), at(v_send, kv_sizes),
                  at(qs_send, qs_sizes), at(ks_send, ks_sizes), scale_rows=mine)
     rows = lay.rows
     q_in = [r * batch * qn * dim for r in rows]

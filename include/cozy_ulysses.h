@@ -210,6 +210,9 @@ typedef struct CozyFp8Tensor {
   float norm_offset;
   float norm_eps;
   int rotate;
+  const float* head_scale; /* per-head mode (Q, K): one descale per (batch, head) [batch][heads]
+                              instead of the block scales; every row's per-token scale is it */
+  float* head_amax;        /* cozy_fp8_head_amax's output [batch][heads] (caller zero-fills) */
 } CozyFp8Tensor;
 
 typedef struct CozyFp8Pack {
@@ -221,10 +224,20 @@ typedef struct CozyFp8Pack {
                     then the next ones round: a rank starting at its own heads writes to a
                     different peer than the other ranks at any moment */
   CozyRope rope; /* read by tensors with `rotate` */
+  int per_head;  /* the reference's per-(batch, head) law (attention_fp8.py:134-169 after
+                    attention_upstream.py:293-317 `fa4_fp8`): the Hadamard rotation as a bf16
+                    matrix product (multiplier and result rounded to bf16), codes = x / descale
+                    correctly rounded (head_scale for Q and K; V's channel_scale holds its
+                    per-head descale broadcast over the channels), no K mean */
 } CozyFp8Pack;
 
 COZY_API int cozy_fp8_stats(const CozyFp8Stats* stats, uintptr_t stream);
 COZY_API int cozy_fp8_pack(const CozyFp8Pack* pack, uintptr_t stream);
+/* The per-head law's statistics: for every tensor with `head_amax`, the absmax over this rank's
+ * rows of each (batch, head) after the transform cozy_fp8_pack applies (norm, RoPE, rotation),
+ * atomically maxed into head_amax (the caller zero-fills it and all-reduces MAX). The reference
+ * takes the same amax after the exchange, per head (attention_fp8.py:134-160). */
+COZY_API int cozy_fp8_head_amax(const CozyFp8Pack* pack, uintptr_t stream);
 
 /* cozy_attention_fwd on e4m3 operands: q/k/v codes with element (= byte) strides, each a
  * multiple of 16; q_scale/k_scale per token [batch][heads][scale_seq] (scale_seq ≥ seq_k

@@ -25,6 +25,7 @@ from oracle.ulysses_oracle import (  # noqa: F401
     owned_heads,
     quantise_e4m3_per_head,
     quantise_fp8_blocks,
+    rotate_bf16,
     sequence_rows,
     turned,
 )

@@ -241,6 +241,7 @@ def fp8_attention_law(
     block: int = 64,
     p_scale: float = 256.0,
     hadamard: bool = True,
+    law: str = "block",
 ) -> Tensor:
     """The FP8 recipe of the video configuration over W ranks' rows, in fp32, returning the whole
     [B, S, H, D] output: K less its per-(batch, head) mean over the whole sequence (the shift of
@@ -250,7 +251,15 @@ def fp8_attention_law(
     boundaries (`quantise_fp8_blocks` per block); V as e4m3 with one scale per (batch, head, channel) over the whole sequence
     (max(absmax/448, 1e-12)); P = exp(s - rowmax) · `p_scale` as e4m3; the row sum over the
     unquantised P; O = (P codes · V codes) · V scale / row sum. Grouped K/V heads as
-    `attention_fp32`."""
+    `attention_fp32`.
+
+    `law="head"`: the reference's own FP8 row instead (`fa4_fp8`,
+    src/cozy_runtime/internal/attention_upstream.py:293-317): Q and K rotated as the bf16
+    matrix product `_hadamard` computes (`rotate_bf16`), no K mean, and Q, K and V each
+    quantised per (batch, head) by `quantise_e4m3_per_head` (attention_fp8.py:162-169); the
+    reference's kernel quantises P inside FlashAttention-4, so P follows this function's P law."""
+    if law == "head":
+        return _fp8_law_head(queries, keys, values, causal=causal, p_scale=p_scale)
     q = torch.cat(list(queries), dim=1).float()
     k = torch.cat(list(keys), dim=1).float()
     v = torch.cat(list(values), dim=1).float()
@@ -276,8 +285,34 @@ def fp8_attention_law(
     vamax = v.abs().amax(dim=1, keepdim=True)
     vscale = (vamax / E4M3_MAX).clamp(min=SCALE_FLOOR)
     vcodes = (v / vscale).clamp(-E4M3_MAX, E4M3_MAX).to(torch.float8_e4m3fn).float()
-    batch, seq, hq, dim = q.shape
-    group = hq // k.shape[2]
+    return _fp8_attend(qd, kd, vcodes, vscale, causal=causal, p_scale=p_scale)
+
+
+def rotate_bf16(x: Tensor) -> Tensor:
+    """`x` times the orthonormal Hadamard of its head dimension as the reference's `_hadamard`
+    computes it on bf16 (src/cozy_runtime/internal/attention_upstream.py:276-287): the matrix
+    rounded to bf16, products summed in fp32, the result rounded to bf16."""
+    h = hadamard_matrix(x.shape[-1]).to(torch.bfloat16).float()
+    return (x.to(torch.bfloat16).float() @ h).to(torch.bfloat16)
+
+
+def _fp8_law_head(queries, keys, values, *, causal: bool, p_scale: float) -> Tensor:
+    q = rotate_bf16(torch.cat(list(queries), dim=1))
+    k = rotate_bf16(torch.cat(list(keys), dim=1))
+    v = torch.cat(list(values), dim=1).to(torch.bfloat16)
+    (qc, qs), (kc, ks), (vc, vs) = (quantise_e4m3_per_head(t) for t in (q, k, v))
+    qd = qc.float() * qs[:, None, :, None]
+    kd = kc.float() * ks[:, None, :, None]
+    vscale = vs[:, None, :, None].expand(v.shape[0], 1, v.shape[2], v.shape[3])
+    return _fp8_attend(qd, kd, vc.float(), vscale, causal=causal, p_scale=p_scale)
+
+
+def _fp8_attend(qd: Tensor, kd: Tensor, vcodes: Tensor, vscale: Tensor, *, causal: bool,
+                p_scale: float) -> Tensor:
+    """Attention over dequantised Q and K and V codes with their scales ([B, 1, Hkv, D]): P =
+    exp(s - rowmax)·`p_scale` as e4m3, the row sum over the unquantised P."""
+    batch, seq, hq, dim = qd.shape
+    group = hq // kd.shape[2]
     out = torch.empty(batch, seq, hq, dim)
     mask = None
     if causal:

@@ -18,6 +18,8 @@ What it records, each as an `.npz` in this directory:
   `src/cozy_runtime/internal/bench/kernels.py:819` `_fused_rope`, executed with the Triton
   launch replaced by a recorder, so the recorded `want` is the reference code's output.
 * ``fp8_quantise.npz``: `src/cozy_runtime/internal/attention_fp8.py:162` `quantise_eager`.
+* ``fp8_head.npz``: the reference's FP8 row's quantisation, `attention_upstream.py:276`
+  `_hadamard` of Q and K, then `quantise_eager` of the rotated Q, K and of V.
 * ``turn_*.npz``: the int8 wire's law, `src/cozy_runtime/internal/parallel/turn.py:60`
   `law` (with and without a shift, which is `turned` of a mean as `_Shift` makes it) and `:73`
   `law_back`, on bf16 rows.
@@ -226,6 +228,24 @@ def fp8_golden() -> None:
         x=to_np(x), codes=codes.view(torch.uint8).numpy(), descale=descale.numpy(),
     )
     print("fp8_quantise:", tuple(codes.shape), tuple(descale.shape))
+
+    # The reference's own FP8 row on B200 (`fa4_fp8`): Q and K rotated by `_hadamard` (a bf16
+    # matrix product), then Q, K and V quantised per (batch, head) by `quantise` (on the CPU its
+    # eager law). Recorded: the rotated Q and K, and every code and descale.
+    from cozy_runtime.internal import attention_upstream
+
+    g = torch.Generator().manual_seed(SEED + 1)
+    q, k, v = (torch.randn(2, 200, 3, 128, generator=g) for _ in range(3))
+    k = torch.where(torch.rand(k.shape, generator=g) < 0.01, k * 8, k)
+    q, k, v = (t.to(torch.bfloat16) for t in (q, k, v))
+    rq, rk = attention_upstream._hadamard(q), attention_upstream._hadamard(k)
+    out = {"q": to_np(q), "k": to_np(k), "v": to_np(v), "rq": to_np(rq), "rk": to_np(rk)}
+    for name, t in (("q", rq), ("k", rk), ("v", v)):
+        codes, descale = attention_fp8.quantise_eager(t)
+        out[f"{name}_codes"] = codes.view(torch.uint8).numpy()
+        out[f"{name}_descale"] = descale.numpy()
+    np.savez_compressed(HERE / "fp8_head.npz", **out)
+    print("fp8_head:", tuple(q.shape))
 
 
 # (name, world, batch, seq, heads_q, heads_kv, dim, causal): bf16 inputs and compute

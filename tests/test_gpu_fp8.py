@@ -24,9 +24,11 @@ def _offsets(sizes):
     return np.concatenate([[0], np.cumsum(sizes)[:-1]]).astype(int).tolist()
 
 
-def simulate_fp8(q, k, v, world, *, causal=False, on_device=False, rope=None, norm=None):
+def simulate_fp8(q, k, v, world, *, causal=False, on_device=False, rope=None, norm=None,
+                 law="block"):
     """W ranks' FP8 stages on one GPU; `rope` (RopeSpec on the GPU) and `norm` (ulysses.Norm,
-    Q and K) run inside the e4m3 first stage."""
+    Q and K) run inside the e4m3 first stage; `law`: "block" (the FP8 configuration's recipe)
+    or "head" (the reference's per-(batch, head) row)."""
     from cozy_runtime_b200 import _lib, fp8, ulysses
 
     batch, total, heads, dim = q.shape
@@ -37,14 +39,23 @@ def simulate_fp8(q, k, v, world, *, causal=False, on_device=False, rope=None, no
     dev = torch.device("cuda")
     steps = [
         fp8.Fp8Step(*(t[:, starts[r] : starts[r] + rows[r]].contiguous().to(dev) for t in (q, k, v)),
-                    layout, r, rope=rope, norm_q=norm, norm_k=norm)
+                    layout, r, rope=rope, norm_q=norm, norm_k=norm, law=law)
         for r in range(world)
     ]
-    k_sum = torch.zeros(batch, hkv, dim, dtype=torch.float32, device=dev)
-    v_amax = torch.zeros(batch, hkv, dim, dtype=torch.float32, device=dev)
-    for st in steps:  # the all-reduce of the NVLink path, done on one GPU
-        st.stats_into(k_sum, v_amax)
-    v_scale = fp8.Fp8Step.channel_scale(v_amax)
+    # the all-reduce of the statistics, done on one GPU by accumulating every rank's
+    if law == "block":
+        k_sum = torch.zeros(batch, hkv, dim, dtype=torch.float32, device=dev)
+        v_amax = torch.zeros(batch, hkv, dim, dtype=torch.float32, device=dev)
+        for st in steps:
+            st.stats_into(k_sum, v_amax)
+        scales = fp8.Fp8Scales(v_scale=fp8.Fp8Step.channel_scale(v_amax), k_sum=k_sum)
+    else:
+        amax = [torch.zeros(batch, n, dtype=torch.float32, device=dev) for n in (heads, hkv, hkv)]
+        for st in steps:
+            st.head_amax_into(*amax)
+        qd, kd, vd = fp8.Fp8Step.head_scales(*amax)
+        scales = fp8.Fp8Scales(v_scale=vd, q_head=qd, k_head=kd)
+    v_scale = scales.v_scale
     sseq = fp8.scale_seq(total)
     recv = []
     for r in range(world):
@@ -59,7 +70,7 @@ def simulate_fp8(q, k, v, world, *, causal=False, on_device=False, rope=None, no
     for r, st in enumerate(steps):
         s0 = starts[r]
         st.pack_to(
-            k_sum, v_scale,
+            scales,
             [recv[p]["q8"].data_ptr() + s0 * batch * layout.q_n[p] * dim for p in range(world)],
             [recv[p]["k8"].data_ptr() + s0 * batch * layout.kv_n[p] * dim for p in range(world)],
             [recv[p]["v8"].data_ptr() + s0 * batch * layout.kv_n[p] * dim for p in range(world)],
@@ -210,6 +221,81 @@ def test_fp8_public_call_with_rope_degree1():
     assert _cosine_per_head(got.float().cpu(), law).min().item() >= 0.999
     exact = oracle.attention_fp32(qr, kr, v)
     assert _cosine_per_head(got.float().cpu(), exact).min().item() >= 0.995
+
+
+def test_fp8_head_law_codes_match_reference():
+    """The per-head law's first stage (`cozy_fp8_head_amax`, then `cozy_fp8_pack` with
+    `per_head`) against the reference's own quantisation of the same inputs (its FP8 row:
+    `_hadamard` of Q and K, then `quantise_eager` of Q, K and V; tests/golden/fp8_head.npz):
+    descales equal; V's codes bit for bit; Q's and K's equal except where the rotation's fp32
+    sum meets a bf16 tie in another order (at most 2e-4 of the codes, one e4m3 step); every
+    per-token scale the head's descale."""
+    from cozy_runtime_b200 import fp8, ulysses
+    from tests._golden import load, tensor
+
+    case = load("fp8_head.npz")
+    q, k, v = (tensor(case[n]).cuda() for n in ("q", "k", "v"))
+    batch, seq, heads, dim = q.shape
+    st = fp8.Fp8Step(q, k, v, ulysses.plan([seq], heads, heads), 0, law="head")
+    scales = st.scales()
+    for got, name in ((scales.q_head, "q"), (scales.k_head, "k"), (scales.v_scale[..., 0], "v")):
+        assert torch.equal(got.cpu(), torch.from_numpy(case[name + "_descale"])), name
+    assert torch.equal(scales.v_scale.cpu(), scales.v_scale[..., :1].expand_as(scales.v_scale).cpu())
+    sseq = fp8.scale_seq(seq)
+    codes = [torch.zeros(seq * batch * heads * dim, dtype=torch.uint8, device="cuda")
+             for _ in range(3)]
+    qs, ks = (torch.zeros(batch * heads * sseq, device="cuda") for _ in range(2))
+    st.pack_to(scales, *([c.data_ptr()] for c in codes), [qs.data_ptr()], [ks.data_ptr()])
+    torch.cuda.synchronize()
+    for c, name in zip(codes, ("q", "k", "v"), strict=True):
+        got = c.view(seq, batch, heads, dim).permute(1, 0, 2, 3).cpu()
+        want = torch.from_numpy(case[name + "_codes"])
+        off = got != want
+        if name == "v":
+            assert not off.any(), "V codes differ"
+            continue
+        assert off.float().mean().item() <= 2e-4, (name, off.sum().item())
+        # one e4m3 step: adjacent codes of the same sign
+        assert ((got[off].int() - want[off].int()).abs() == 1).all(), name
+    for sc, d in ((qs, scales.q_head), (ks, scales.k_head)):
+        rows = sc.view(batch, heads, sseq)[:, :, :seq]
+        assert torch.equal(rows, d[:, :, None].expand_as(rows))
+
+
+@pytest.mark.parametrize(
+    "world,batch,seq,hq,hkv,causal",
+    [(1, 1, 700, 2, 2, False), (4, 1, 1200, 8, 8, True), (3, 2, 500, 6, 3, False)],
+)
+def test_fp8_head_law_exchange(world, batch, seq, hq, hkv, causal):
+    """The reference's FP8 row through the whole path (per-head statistics all-reduced,
+    per-head e4m3 first stage, e4m3 attention, rows to their owners) against the oracle's
+    per-head law (cosine ≥ 0.999 per head) and exact attention (≥ 0.995)."""
+    from cozy_runtime_b200 import attention
+
+    q, k, v = _inputs(batch, seq, hq, hkv, seq + world + 11)
+    got = simulate_fp8(q, k, v, world, causal=causal, law="head")
+    attention.check_status(torch.device("cuda"))
+    rows = [t.shape[0] for t in torch.tensor_split(torch.empty(seq), world)]
+    law = oracle.fp8_attention_law(*[torch.split(t, rows, dim=1) for t in (q, k, v)],
+                                   causal=causal, law="head")
+    cos_law = _cosine_per_head(got, law)
+    cos = _cosine_per_head(got, oracle.attention_fp32(q, k, v, causal=causal))
+    print(f"fp8 head law W={world}: law cos {cos_law.min().item():.6f}, "
+          f"exact cos {cos.min().item():.6f}")
+    assert cos_law.min().item() >= 0.999, f"vs law cosine {cos_law.min().item():.5f}"
+    assert cos.min().item() >= 0.995, f"cosine {cos.min().item():.5f}"
+
+
+def test_fp8_head_law_public_call():
+    """`ulysses.exchange(..., fp8="head")` at degree 1 against the oracle's per-head law."""
+    from cozy_runtime_b200 import attention, ulysses
+
+    q, k, v = _inputs(1, 900, 3, 3, 79)
+    got = ulysses.exchange(q.cuda(), k.cuda(), v.cuda(), None, None, fp8="head")
+    torch.cuda.synchronize()
+    attention.check_status(torch.device("cuda"))
+    law = oracle.fp8_attention_law([q], [k], [v], law="head")
+    assert _cosine_per_head(got.float().cpu(), law).min().item() >= 0.999
 
 
 def _law_rows_gpu(q, k, v, rows, starts, block=64):

@@ -78,6 +78,10 @@ def _cases() -> list[dict]:
         out.append({"id": f"fp8-w{world}-{hq}-{hkv}-{causal}-{transport}", "world": world,
                     "seed": world * 7 + hq, "seq": 1000, "hq": hq, "hkv": hkv, "causal": causal,
                     "outliers": True, "fp8": True, "transport": transport})
+    for world, transport in [(2, "peer"), (4, "nccl")]:  # the reference's per-head FP8 row
+        out.append({"id": f"fp8head-w{world}-{transport}", "world": world, "seed": 70 + world,
+                    "seq": 1000, "hq": 8, "hkv": 8, "causal": False, "outliers": True,
+                    "fp8": "head", "transport": transport})
     for world, transport in [(2, "peer"), (4, "nccl"), (8, "peer")]:  # RoPE in the e4m3 stage
         out.append({"id": f"fp8rope-w{world}-{transport}", "world": world, "seed": 60 + world,
                     "seq": 2 * 6 * 10 + TEXT, "hq": 8, "hkv": 8, "causal": False,
@@ -229,7 +233,8 @@ def test_fp8_exchange_against_law(case_id):
                                       normalize=False).to(torch.bfloat16) for t in (q, k))
     rows = [t.shape[0] for t in torch.tensor_split(torch.empty(case["seq"]), case["world"])]
     law = oracle.fp8_attention_law(*(torch.split(t, rows, dim=1) for t in (q, k, v)),
-                                   causal=case["causal"])
+                                   causal=case["causal"],
+                                   law="head" if case["fp8"] == "head" else "block")
 
     def cos(a, b):
         a = a.permute(0, 2, 1, 3).reshape(a.shape[2], -1)

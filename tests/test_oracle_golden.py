@@ -57,6 +57,30 @@ def test_fp8_per_head_law_matches_reference():
     assert np.array_equal(descale.numpy(), case["descale"])
 
 
+def test_fp8_head_rotation_matches_reference():
+    """`rotate_bf16` against the reference's `_hadamard` on bf16 (attention_upstream.py:276):
+    equal except where the two fp32 sums, added in another order, straddle a bf16 rounding
+    tie (at most 1e-4 of the elements, one bf16 step apart)."""
+    case = load("fp8_head.npz")
+    for name in ("q", "k"):
+        got = oracle.rotate_bf16(tensor(case[name])).float()
+        want = tensor(case["r" + name]).float()
+        off = got != want
+        assert off.float().mean().item() <= 1e-4, name
+        step = want.abs()[off] * 2.0 ** -7  # one bf16 step (8 significant bits)
+        assert ((got - want).abs()[off] <= step + 1e-30).all(), name
+
+
+def test_fp8_head_quantise_matches_reference():
+    """The per-head law on the reference's rotated Q and K and on V: codes and descales equal
+    the reference's `quantise_eager` bit for bit (fixture of its FP8 row, `fa4_fp8`)."""
+    case = load("fp8_head.npz")
+    for name, src in (("q", "rq"), ("k", "rk"), ("v", "v")):
+        codes, descale = oracle.quantise_e4m3_per_head(tensor(case[src]))
+        assert np.array_equal(codes.view(torch.uint8).numpy(), case[name + "_codes"]), name
+        assert np.array_equal(descale.numpy(), case[name + "_descale"]), name
+
+
 def test_sequence_rows_is_tensor_split():
     for total in (1, 7, 250, 33272, 131071):
         for world in (1, 2, 3, 4, 7, 8):
