@@ -132,87 +132,14 @@ __device__ __forceinline__ uint32_t e4m3x4(float a, float b, float c, float d) {
 }
 
 // ------------------------------------------------------------------------ first stage
-// Work items: (64-row block of the whole sequence clipped to this rank, head, tensor, batch), the
-// block fastest. Persistent CTAs of 512 threads, two an SM (16 threads a row, 8 channels each;
-// 2 rows a thread) walk items gridDim.x apart; every thread copies its own two 16-byte pieces of an item's rows
-// into a ring of kPackStages shared-memory tiles with cp.async, kPackStages - 1 items ahead of the
-// one it transforms, so loads stay in flight through the math, the block reduction and the
-// stores. A thread reads back only the pieces it copied itself: no barrier guards the ring.
+// One CTA per work item: (64-row block of the whole sequence clipped to this rank) x head x
+// (batch, tensor); 512 threads, 16 a row (8 channels each), 2 rows a thread, both loaded before
+// any math; three CTAs an SM. (A persistent form that kept loads in flight through the math with
+// a cp.async ring measured slower on B200 — 316 against 200 us at C4's degree-8 share — since
+// the stage is bound by its instructions, the Hadamard's shuffles above all, not by HBM.)
 constexpr int kPackThreads = 512;
 constexpr int kPackPasses = 64 * 16 / kPackThreads;
-constexpr int kPackStages = 4;
-constexpr int kPackTileBytes = 64 * 256;  // 64 rows of 128 bf16
-constexpr int kPackSmem = kPackStages * kPackTileBytes;
 constexpr float kHadamardBf16 = 0.08837890625f;  // 1/sqrt(128) rounded to bf16
-
-struct PackItem {
-  int block, slot, tensor, b;
-};
-
-__device__ __forceinline__ PackItem pack_item(long long id, int blocks, int heads) {
-  PackItem it;
-  it.block = static_cast<int>(id % blocks);
-  const long long rest = id / blocks;
-  it.slot = static_cast<int>(rest % heads);
-  const int z = static_cast<int>(rest / heads);
-  it.tensor = z % 3;
-  it.b = z / 3;
-  return it;
-}
-
-// The item's head (heads from the launch's first head round: the grid's head extent is Q's
-// head count; K/V start at the same fraction of theirs), or -1 past a tensor's heads.
-__device__ __forceinline__ int item_head(const CozyFp8Pack& a, const PackItem& it) {
-  const CozyFp8Tensor& t = a.t[it.tensor];
-  if (it.slot >= t.heads) return -1;
-  const int turn = static_cast<int>(static_cast<long long>(a.head_turn) * t.heads / a.t[0].heads);
-  return (it.slot + turn) % t.heads;
-}
-
-// Rows of an item, relative to this rank's first row: [lo_row, hi_row), block0 its first row.
-__device__ __forceinline__ void item_rows(const CozyFp8Pack& a, int block, int* block0, int* lo_row,
-                                          int* hi_row) {
-  const int gblock = a.row0 / 64 + block;
-  *lo_row = max(gblock * 64, a.row0) - a.row0;
-  *hi_row = min(gblock * 64 + 64, a.row0 + a.rows) - a.row0;
-  *block0 = gblock * 64 - a.row0;
-}
-
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool in) {
-  const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem),
-               "r"(in ? 16 : 0)
-               : "memory");
-}
-
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
-// This thread's pieces of item `id` into ring tile `tile` (zero-filled outside the rank's rows).
-__device__ __forceinline__ void prefetch_item(const CozyFp8Pack& a, long long id, long long items,
-                                              int blocks, int heads, uint8_t* tile) {
-  if (id >= items) return;
-  const PackItem it = pack_item(id, blocks, heads);
-  const int head = item_head(a, it);
-  if (head < 0) return;
-  const CozyFp8Tensor& t = a.t[it.tensor];
-  int block0, lo_row, hi_row;
-  item_rows(a, it.block, &block0, &lo_row, &hi_row);
-  const int chunk = threadIdx.x & 15, row_in = threadIdx.x >> 4;
-  const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(t.src) + it.b * t.src_strides[2] +
-                             head * t.src_strides[1] + chunk * 8;
-#pragma unroll
-  for (int pass = 0; pass < kPackPasses; ++pass) {
-    const int row = pass * 32 + row_in;
-    const int r = block0 + row;
-    const bool in = r >= lo_row && r < hi_row;
-    cp_async16(tile + row * 256 + chunk * 16, in ? src + static_cast<long long>(r) * t.src_strides[0] : t.src, in);
-  }
-}
 
 // The first stage's transform of an item's rows held in `x`: RMSNorm + RoPE (rounded to bf16),
 // K less its mean (block law), the Hadamard rotation (Q and K); rows outside the rank stay 0.
@@ -265,11 +192,11 @@ __device__ __forceinline__ void transform_rows(const CozyFp8Pack& a, const CozyF
           }
 #pragma unroll
       for (int lanes = 1; lanes < 16; lanes <<= 1) {
-        const bool high = (chunk & lanes) != 0;
+        const float sign = (chunk & lanes) ? -1.f : 1.f;  // the high lane keeps other - x
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const float other = __shfl_xor_sync(0xffffffffu, x[pass][i], lanes);
-          x[pass][i] = high ? other - x[pass][i] : x[pass][i] + other;
+          x[pass][i] = fmaf(sign, x[pass][i], other);
         }
       }
       if (a.per_head) {
@@ -297,103 +224,99 @@ __device__ __forceinline__ float warp_amax(const float (&x)[kPackPasses][8]) {
 // AMAX = false: the first stage (codes to every owner of the head, per-token scales).
 // AMAX = true:  the per-head law's statistics: the absmax of every (batch, head) of every tensor
 //               with `head_amax`, after the same transform (atomic max; the caller zero-fills).
+// blockIdx: x = 64-row block of this rank, y = head, z = batch * 3 + tensor (0 Q, 1 K, 2 V).
 template <bool LAW, bool AMAX>
-__global__ void __launch_bounds__(kPackThreads, 2) fp8_pack_kernel(const CozyFp8Pack a, int blocks,
-                                                                 int heads) {
-  extern __shared__ __align__(16) uint8_t ring[];
-  __shared__ float warp_max[2][kPackThreads / 32];
-  const long long items = static_cast<long long>(blocks) * heads * 3 * a.batch;
-  const long long stride = gridDim.x;
-  const int chunk = threadIdx.x & 15, row_in = threadIdx.x >> 4, d0 = chunk * 8;
+__global__ void __launch_bounds__(kPackThreads, LAW ? 2 : 3) fp8_pack_kernel(const CozyFp8Pack a) {
+  const int tensor = blockIdx.z % 3;
+  const int b = blockIdx.z / 3;
+  const CozyFp8Tensor& t = a.t[tensor];
+  if (static_cast<int>(blockIdx.y) >= t.heads) return;
+  if (AMAX && t.head_amax == nullptr) return;
+  // heads from the launch's first head round (the grid's y extent is Q's head count; K/V
+  // start at the same fraction of theirs)
+  const int turn = static_cast<int>(static_cast<long long>(a.head_turn) * t.heads / a.t[0].heads);
+  const int head = (static_cast<int>(blockIdx.y) + turn) % t.heads;
+  const int chunk = threadIdx.x & 15;
+  const int row_in = threadIdx.x >> 4;
+  const int d0 = chunk * 8;
+  // global block of this CTA, clipped to this rank's rows [row0, row0 + rows)
+  const int gblock = a.row0 / 64 + static_cast<int>(blockIdx.x);
+  const int lo_row = max(gblock * 64, a.row0) - a.row0;
+  const int hi_row = min(gblock * 64 + 64, a.row0 + a.rows) - a.row0;
+  const int block0 = gblock * 64 - a.row0;  // may be negative: rows below lo_row are skipped
+  const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(t.src) + b * t.src_strides[2] +
+                             head * t.src_strides[1] + d0;
+  float x[kPackPasses][8];
+  {
+    uint4 raw[kPackPasses];
 #pragma unroll
-  for (int s = 0; s < kPackStages - 1; ++s) {
-    prefetch_item(a, blockIdx.x + s * stride, items, blocks, heads, ring + s * kPackTileBytes);
-    cp_async_commit();
+    for (int pass = 0; pass < kPackPasses; ++pass) {
+      const int r = block0 + pass * 32 + row_in;
+      raw[pass] = make_uint4(0u, 0u, 0u, 0u);
+      if (r >= lo_row && r < hi_row) raw[pass] = *reinterpret_cast<const uint4*>(src + r * t.src_strides[0]);
+    }
+#pragma unroll
+    for (int pass = 0; pass < kPackPasses; ++pass) unpack8(raw[pass], x[pass]);
   }
-  int k = 0;
-  int reductions = 0;  // block reductions so far: they alternate between the two warp_max sets
-  for (long long id = blockIdx.x; id < items; id += stride, ++k) {
-    prefetch_item(a, id + (kPackStages - 1) * stride, items, blocks, heads,
-                  ring + ((k + kPackStages - 1) % kPackStages) * kPackTileBytes);
-    cp_async_commit();
-    cp_async_wait<kPackStages - 1>();  // this item's pieces (this thread's own) have landed
-    const PackItem it = pack_item(id, blocks, heads);
-    const int head = item_head(a, it);
-    if (head < 0) continue;  // uniform over the CTA
-    const CozyFp8Tensor& t = a.t[it.tensor];
-    const int b = it.b;
-    int block0, lo_row, hi_row;
-    item_rows(a, it.block, &block0, &lo_row, &hi_row);
-    const uint8_t* tile = ring + (k % kPackStages) * kPackTileBytes;
-    float x[kPackPasses][8];
+  transform_rows<LAW>(a, t, b, head, block0, lo_row, hi_row, x);
+  if constexpr (AMAX) {
+    const float m = warp_amax(x);
+    // non-negative floats order like their bit patterns
+    if ((threadIdx.x & 31) == 0)
+      atomicMax(reinterpret_cast<unsigned int*>(t.head_amax) + b * t.heads + head, __float_as_uint(m));
+    return;
+  } else {
+    float inv[8];
+    float scale = 0.f;
+    bool divide = a.per_head;
+    if (t.channel_scale != nullptr) {  // per-channel (V): scale from the global channel absmax
+      const float* cs = t.channel_scale + (b * t.heads + head) * 128 + d0;
 #pragma unroll
-    for (int pass = 0; pass < kPackPasses; ++pass)
-      unpack8(*reinterpret_cast<const uint4*>(tile + (pass * 32 + row_in) * 256 + chunk * 16), x[pass]);
-    transform_rows<LAW>(a, t, b, head, block0, lo_row, hi_row, x);
-    if constexpr (AMAX) {
-      if (t.head_amax != nullptr) {
-        const float m = warp_amax(x);
-        // non-negative floats order like their bit patterns
-        if ((threadIdx.x & 31) == 0)
-          atomicMax(reinterpret_cast<unsigned int*>(t.head_amax) + b * t.heads + head, __float_as_uint(m));
-      }
-      continue;
-    } else {
-      float inv[8];
-      float scale = 0.f;
-      bool divide = a.per_head;
-      if (t.channel_scale != nullptr) {  // per-channel (V): scale from the global channel absmax
-        const float* cs = t.channel_scale + (b * t.heads + head) * 128 + d0;
+      for (int i = 0; i < 8; ++i) inv[i] = divide ? cs[i] : 1.f / cs[i];
+    } else if (t.head_scale != nullptr) {  // per (batch, head): the reference's law
+      scale = t.head_scale[b * t.heads + head];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) inv[i] = divide ? cs[i] : 1.f / cs[i];
-      } else if (t.head_scale != nullptr) {  // per (batch, head): the reference's law
-        scale = t.head_scale[b * t.heads + head];
+      for (int i = 0; i < 8; ++i) inv[i] = scale;
+      divide = true;
+    } else {  // per 64-token block: reduce the absmax over the CTA
+      __shared__ float warp_max[kPackThreads / 32];
+      const float m0 = warp_amax(x);
+      if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = m0;
+      __syncthreads();
+      float m = warp_max[0];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) inv[i] = scale;
-        divide = true;
-      } else {  // per 64-token block: reduce the absmax over the CTA
-        const float m0 = warp_amax(x);
-        // two sets: the next reduction writes the other one, and the one after it comes only
-        // after every thread passed the next reduction's barrier, i.e. finished reading this one
-        float* wm = warp_max[reductions++ & 1];
-        if ((threadIdx.x & 31) == 0) wm[threadIdx.x >> 5] = m0;
-        __syncthreads();
-        float m = wm[0];
+      for (int w = 1; w < kPackThreads / 32; ++w) m = fmaxf(m, warp_max[w]);
+      scale = fmaxf(m / kE4M3Max, kScaleFloor);
+      const float is = 1.f / scale;
 #pragma unroll
-        for (int w = 1; w < kPackThreads / 32; ++w) m = fmaxf(m, wm[w]);
-        scale = fmaxf(m / kE4M3Max, kScaleFloor);
-        const float is = 1.f / scale;
+      for (int i = 0; i < 8; ++i) inv[i] = is;
+    }
+    // codes: x·(1/scale) for the block and channel recipes; x / scale correctly rounded, as
+    // the reference's per-head law divides, where the per-head law is asked for
+    auto code = [&](int pass, int i) {
+      return divide ? __fdiv_rn(x[pass][i], inv[i]) : x[pass][i] * inv[i];
+    };
+    for (int p = 0; p < a.world; ++p) {
+      const int lo = t.head_lo[p], n = t.head_n[p];
+      if (head < lo || head >= lo + n) continue;
+      const int hh = head - lo;
+      uint8_t* dst = static_cast<uint8_t*>(t.dst[p]);
+      float* sdst = t.scale_dst[p];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) inv[i] = is;
-      }
-      // codes: x·(1/scale) for the block and channel recipes; x / scale correctly rounded, as
-      // the reference's per-head law divides, where the per-head law is asked for
-      auto code = [&](int pass, int i) {
-        return divide ? __fdiv_rn(x[pass][i], inv[i]) : x[pass][i] * inv[i];
-      };
-      for (int p = 0; p < a.world; ++p) {
-        const int lo = t.head_lo[p], n = t.head_n[p];
-        if (head < lo || head >= lo + n) continue;
-        const int hh = head - lo;
-        uint8_t* dst = static_cast<uint8_t*>(t.dst[p]);
-        float* sdst = t.scale_dst[p];
-#pragma unroll
-        for (int pass = 0; pass < kPackPasses; ++pass) {
-          const int r = block0 + pass * 32 + row_in;
-          if (r < lo_row || r >= hi_row) continue;
-          const uint2 codes = make_uint2(
-              e4m3x4(code(pass, 0), code(pass, 1), code(pass, 2), code(pass, 3)),
-              e4m3x4(code(pass, 4), code(pass, 5), code(pass, 6), code(pass, 7)));
-          // destination [rows][batch][n][128] bytes
-          *reinterpret_cast<uint2*>(dst + ((static_cast<long long>(r) * a.batch + b) * n + hh) * 128 + d0) =
-              codes;
-          if (sdst != nullptr && chunk == 0)  // per-token scales [batch][n][scale_seq] at this rank's row
-            sdst[(static_cast<long long>(b) * n + hh) * t.scale_seq + r] = scale;
-        }
+      for (int pass = 0; pass < kPackPasses; ++pass) {
+        const int r = block0 + pass * 32 + row_in;
+        if (r < lo_row || r >= hi_row) continue;
+        const uint2 codes = make_uint2(
+            e4m3x4(code(pass, 0), code(pass, 1), code(pass, 2), code(pass, 3)),
+            e4m3x4(code(pass, 4), code(pass, 5), code(pass, 6), code(pass, 7)));
+        // destination [rows][batch][n][128] bytes
+        *reinterpret_cast<uint2*>(dst + ((static_cast<long long>(r) * a.batch + b) * n + hh) * 128 + d0) =
+            codes;
+        if (sdst != nullptr && chunk == 0)  // per-token scales [batch][n][scale_seq] at this rank's row
+          sdst[(static_cast<long long>(b) * n + hh) * t.scale_seq + r] = scale;
       }
     }
   }
-  cp_async_wait<0>();
 }
 
 // The RoPE table a rotating tensor reads (the bf16 first stage's checks).
@@ -455,24 +378,15 @@ static int check_pack(const CozyFp8Pack* a, bool amax, int* heads) {
 template <bool AMAX>
 static int launch_pack(const CozyFp8Pack* a, cudaStream_t stream) {
   int heads = 0;
-  int e = check_pack(a, AMAX, &heads);
+  const int e = check_pack(a, AMAX, &heads);
   if (e != cudaSuccess) return e;
   if (a->rows == 0) return cudaSuccess;
   const int blocks = (a->row0 + a->rows + 63) / 64 - a->row0 / 64;
-  const long long items = static_cast<long long>(blocks) * heads * 3 * a->batch;
-  int device = 0, sms = 148;
-  cudaGetDevice(&device);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-  const int grid = static_cast<int>(std::min<long long>(items, 2LL * sms));
-  const bool law = first_stage_law(a->t[0]) || first_stage_law(a->t[1]) || first_stage_law(a->t[2]);
-  auto kernel = law ? fp8_pack_kernel<true, AMAX> : fp8_pack_kernel<false, AMAX>;
-  static bool opted[2][64] = {};  // per instantiation of AMAX: [law][device]
-  if (device < 0 || device >= 64 || !opted[law][device]) {
-    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPackSmem);
-    if (e != cudaSuccess) return e;
-    if (device >= 0 && device < 64) opted[law][device] = true;
-  }
-  kernel<<<grid, kPackThreads, kPackSmem, stream>>>(*a, blocks, heads);
+  dim3 grid(blocks, heads, a->batch * 3);
+  if (first_stage_law(a->t[0]) || first_stage_law(a->t[1]) || first_stage_law(a->t[2]))
+    fp8_pack_kernel<true, AMAX><<<grid, kPackThreads, 0, stream>>>(*a);
+  else
+    fp8_pack_kernel<false, AMAX><<<grid, kPackThreads, 0, stream>>>(*a);
   return cudaGetLastError();
 }
 

@@ -126,7 +126,10 @@ class Fp8Step:
         """The per-head law's descales from the global amax: max(amax / 440, 1e-12)
         (attention_fp8.py:169); V's broadcast over its 128 channels, the form the attention
         reads."""
-        q, k, v = ((a / E4M3_TARGET).clamp_(min=SCALE_FLOOR) for a in (q_amax, k_amax, v_amax))
+        # amax / 440 correctly rounded, as the reference divides on the host (a CUDA tensor
+        # divided by a scalar may be multiplied by its reciprocal instead)
+        q, k, v = ((a.double() / E4M3_TARGET).float().clamp_(min=SCALE_FLOOR)
+                   for a in (q_amax, k_amax, v_amax))
         return q.contiguous(), k.contiguous(), v[..., None].expand(*v.shape, 128).contiguous()
 
     # --------------------------------------------------------------- first stage
