@@ -241,7 +241,7 @@ def test_fp8_head_law_codes_match_reference():
     for got, name in ((scales.q_head, "q"), (scales.k_head, "k"), (scales.v_scale[..., 0], "v")):
         want = torch.from_numpy(case[name + "_descale"])
         ulps = (got.cpu().view(torch.int32) - want.view(torch.int32)).abs().max().item()
-        assert ulps == 0, f"{name} descales differ by up to {ulps} ulp
+        assert ulps == 0, f"{name} descales differ by up to {ulps} ulp"
     assert torch.equal(scales.v_scale.cpu(), scales.v_scale[..., :1].expand_as(scales.v_scale).cpu())
     sseq = fp8.scale_seq(seq)
     codes = [torch.zeros(seq * batch * heads * dim, dtype=torch.uint8, device="cuda")
