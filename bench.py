@@ -535,6 +535,9 @@ def main() -> None:
                         help="skip the parity check, attention-alone, cuDNN and long-run legs")
     parser.add_argument("--long-run-s", type=float, default=0.5,
                         help="after the timed steps, steps until this long has passed (clocks)")
+    parser.add_argument("--fp8-law", default="block", choices=["block", "head"],
+                        help="FP8 configurations: the 64-token block recipe (c4's) or the "
+                        "reference's per-(batch, head) row")
     parser.add_argument("--narrow", action="store_true",
                         help="the int8 wire (exchange(..., narrow=True)); not the headline")
     parser.add_argument("--heads", type=int, default=0,
@@ -585,10 +588,11 @@ def main() -> None:
     spec = spec.to(device) if spec is not None else None
     norm = ulysses.Norm() if cfg["norm"] else None
     fp8 = bool(cfg.get("fp8"))
+    fp8_arg = ("head" if args.fp8_law == "head" else True) if fp8 else False
 
     def step(qq, kk, vv):
         return ulysses.exchange(qq, kk, vv, group, None, rows=rows, causal=cfg["causal"],
-                                rope=spec, norm_q=norm, norm_k=norm, fp8=fp8,
+                                rope=spec, norm_q=norm, norm_k=norm, fp8=fp8_arg,
                                 narrow=args.narrow)
 
     for _ in range(args.warmup):
@@ -673,6 +677,9 @@ def main() -> None:
         from cozy_runtime_b200 import peer
 
         flag_mode = peer.layer_group_for(group, device).flag_mode()
+    links = None
+    if group is not None and ulysses.links_of(group) is not None:
+        links = ulysses.links_of(group).summary()  # the formation's per-pair probe
     crossing = None
     if transport == "peer" and group is not None:
         # the latest call's crossing on each rank: its copy-engine copies to the other ranks and
@@ -806,11 +813,13 @@ def main() -> None:
                 "parallelism": f"ulysses{world}",
                 "rows_per_rank": rows,
                 "wire": "int8 (narrow)" if args.narrow else ("e4m3" if fp8 else "bf16"),
+                **({"fp8_law": args.fp8_law} if fp8 else {}),
                 "l2": "inputs larger than L2 (no flush)",
             },
             "transport": transport,
             "flag_mode": flag_mode,
             "crossing": crossing,
+            "links": links,
             "layer": {
                 "attention_span_ms": round(span_max, 4),
                 "attention_alone_ms": None if alone_ms is None else round(alone_ms, 4),

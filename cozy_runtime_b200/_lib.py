@@ -302,6 +302,8 @@ SIGNATURES = {
     "cozy_group_flag_mode": ([c_void_p], c_int),
     "cozy_group_flag": ([c_void_p, c_int, c_int, POINTER(c_longlong)], c_int),
     "cozy_group_crossing": ([c_void_p, POINTER(c_float), POINTER(ctypes.c_ulonglong)], c_int),
+    "cozy_group_probe": ([c_void_p, c_int, c_int, POINTER(c_float), POINTER(ctypes.c_ulonglong)],
+                         c_int),
     "cozy_ulysses_layer_fwd": ([c_void_p, POINTER(LayerCall), c_uint64], c_int),
     "cozy_ulysses_layer_begin": ([c_void_p, POINTER(LayerCall), c_uint64], c_int),
     "cozy_ulysses_layer_attend": ([c_void_p, POINTER(LayerCall), c_uint64], c_int),

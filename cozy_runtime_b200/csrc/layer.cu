@@ -407,6 +407,33 @@ int cozy_group_crossing(CozyGroup* g, float* ms, unsigned long long* bytes) {
   return cudaSuccess;
 }
 
+int cozy_group_probe(CozyGroup* g, int dst, int reps, float* ms, unsigned long long* bytes) {
+  if (g == nullptr || ms == nullptr || bytes == nullptr || reps < 1) return cudaErrorInvalidValue;
+  std::lock_guard<std::mutex> guard(g->lock);
+  if (!g->opened || dst < 0 || dst >= g->world || dst == g->rank) return cudaErrorInvalidValue;
+  void* to = g->peer[dst][0][0];
+  const size_t n = std::min(g->caps.stage, g->caps.q);
+  if (to == nullptr || g->stage == nullptr || n == 0) return cudaErrorInvalidValue;
+  cudaEvent_t start, end;
+  cudaError_t e = cudaEventCreate(&start);
+  if (e != cudaSuccess) return e;
+  if ((e = cudaEventCreate(&end)) != cudaSuccess) {
+    cudaEventDestroy(start);
+    return e;
+  }
+  // the same copy engines and stream the crossing uses, `reps` times back to back
+  e = cudaEventRecord(start, g->side);
+  for (int i = 0; i < reps && e == cudaSuccess; ++i)
+    e = cudaMemcpyAsync(to, g->stage, n, cudaMemcpyDeviceToDevice, g->side);
+  if (e == cudaSuccess) e = cudaEventRecord(end, g->side);
+  if (e == cudaSuccess) e = cudaEventSynchronize(end);
+  if (e == cudaSuccess) e = cudaEventElapsedTime(ms, start, end);
+  cudaEventDestroy(start);
+  cudaEventDestroy(end);
+  *bytes = static_cast<unsigned long long>(n) * reps;
+  return e;
+}
+
 int cozy_group_flag_mode(const CozyGroup* g) {
   if (g == nullptr) return -1;
   return g->write_value ? 1 : 2;

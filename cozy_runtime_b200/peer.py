@@ -286,6 +286,14 @@ class LayerGroup:
             return None
         return ms.value, nbytes.value
 
+    def probe(self, dst: int, reps: int = 32) -> tuple[float, int]:
+        """(ms, bytes) of `reps` copies from this rank's staging buffer into `dst`'s receive
+        buffer over the crossing's copy engines (`cozy_group_probe`; no call in flight)."""
+        ms, nbytes = ctypes.c_float(0), ctypes.c_ulonglong(0)
+        _lib.check("cozy_group_probe", _lib.load().cozy_group_probe(
+            self.ptr, dst, reps, ctypes.byref(ms), ctypes.byref(nbytes)))
+        return ms.value, nbytes.value
+
     def run(self, phase: str, call: _lib.LayerCall, stream: int) -> None:
         entry = f"cozy_ulysses_layer_{phase}"
         _lib.check(entry, getattr(_lib.load(), entry)(self.ptr, ctypes.byref(call), stream))

@@ -43,6 +43,7 @@ from torch import Tensor
 
 from cozy_runtime_b200 import _lib, attention, peer
 from cozy_runtime_b200 import fp8 as fp8_mod
+from cozy_runtime_b200 import links as links_mod
 from cozy_runtime_b200 import narrow as narrow_mod
 from cozy_runtime_b200 import rope as rope_mod
 from cozy_runtime_b200.rope import RopeSpec
@@ -657,7 +658,21 @@ def _form_check(handle, device: torch.device) -> bool:
         ok = False
     agreed = torch.tensor([1 if ok else 0], dtype=torch.int32, device=device)
     dist.all_reduce(agreed, op=dist.ReduceOp.MIN, group=handle)
-    return bool(agreed.item())
+    if not agreed.item():
+        return False
+    # the bytes are right; now the links: every ordered pair measured over the layer's own copy
+    # engines (the reference's per-pair probe, links.py:394-519), the route from the pairs
+    found = links_mod.measure(peer.layer_group_for(handle, device), handle, device)
+    _LINKS[handle] = found
+    return found.exchange == "peer"
+
+
+_LINKS: weakref.WeakKeyDictionary = weakref.WeakKeyDictionary()
+
+
+def links_of(handle):
+    """The measured links of a group whose NVLink layer formed (`links.Links`), else None."""
+    return _LINKS.get(handle) if handle is not None else None
 
 
 def transport_of(handle, device: torch.device | None = None) -> str:

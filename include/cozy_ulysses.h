@@ -428,6 +428,14 @@ COZY_API int cozy_group_flag(const CozyGroup* group, int kind, int src, long lon
  * write on the side stream, and the bytes its copies moved to the other ranks (for NVLink
  * bandwidth: bytes / ms). cudaErrorNotReady while that call's copies are still under way. */
 COZY_API int cozy_group_crossing(CozyGroup* group, float* ms, unsigned long long* bytes);
+/* The link probe of one ordered pair (this rank -> `dst`): `reps` back-to-back copies of this
+ * rank's staging buffer into dst's receive buffer (set 0), on the copy engines and side stream
+ * the crossing uses; returns their time and bytes. It overwrites dst's receive set 0: call it
+ * only while no layer call is in flight on any rank of the group (between barriers). Replaces
+ * the reference's per-pair copy measurement (src/cozy_runtime/internal/parallel/links.py:
+ * 394-519), which it takes inside the group's own processes and buffers. */
+COZY_API int cozy_group_probe(CozyGroup* group, int dst, int reps, float* ms,
+                              unsigned long long* bytes);
 
 /* The layer: cozy_ulysses_layer_fwd = begin (first stage, copies and flags to every rank),
  * attend (the attention, waiting per source inside the kernel, output rows stored into their

@@ -314,3 +314,86 @@ def test_failure_after_crossing_ends_the_wait_of_peers():
         outcomes = [open(os.path.join(tmp, f"{r}.txt")).read().split() for r in range(2)]
     assert outcomes[1][0] == "ValueError"
     assert outcomes[0][0] == "RuntimeError" and float(outcomes[0][1]) < 60
+
+
+# ------------------------------------------------------------------------------ link probe
+def test_links_route_from_pairs():
+    """The route follows from the measured pairs alone (the reference's `Links.exchange`):
+    every ordered pair direct -> the NVLink layer; one slow pair -> NCCL, and `why` names it."""
+    from cozy_runtime_b200 import links
+
+    fast = [[0, 750, 760], [740, 0, 755], [770, 745, 0]]
+    found = links.decide(fast, [18, 18, 18])
+    assert found.exchange == "peer" and found.all_direct and len(found.pairs) == 6
+    assert found.summary()["min_gbs"] == 740.0
+    slow = [row[:] for row in fast]
+    slow[2][0] = 48.0  # a PCIe-class pair
+    found = links.decide(slow, [18, 18, 0])
+    assert found.exchange == "nccl" and not found.all_direct
+    assert "2->0" in found.why()
+    unmapped = links.decide(fast, peers=[[True, True, True], [True, True, False], [True] * 3])
+    assert unmapped.exchange == "nccl" and not unmapped.all_peers
+
+
+def test_links_nvml_count_with_a_fake_nvml():
+    """NVML's active link count (read-only queries), against a stand-in NVML; -1 without one."""
+    from cozy_runtime_b200 import links
+
+    class FakeNvml:
+        NVML_FEATURE_ENABLED = 1
+        NVML_NVLINK_MAX_LINKS = 18
+
+        def nvmlInit(self):
+            pass
+
+        def nvmlDeviceGetHandleByIndex(self, index):
+            return index
+
+        def nvmlDeviceGetNvLinkState(self, handle, link):
+            if link >= 18:
+                raise RuntimeError("no such link")
+            return 1 if link < 18 - handle else 0
+
+    assert links.nvlink_links(0, FakeNvml()) == 18
+    assert links.nvlink_links(3, FakeNvml()) == 15
+
+    class Broken:
+        def nvmlInit(self):
+            raise RuntimeError("driver not loaded")
+
+    assert links.nvlink_links(0, Broken()) == -1
+
+
+def _links_rank(rank, world, port, out):
+    import torch.distributed as dist
+
+    from cozy_runtime_b200 import links
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world)
+
+    class FakeLayer:  # the layer group's probe: rank 1 -> 0 is a slow pair
+        def probe(self, dst, reps):
+            gbs = 40.0 if (rank, dst) == (1, 0) else 700.0
+            nbytes = 1 << 26
+            return nbytes / (gbs * 1e9) * 1e3, nbytes
+
+    found = links.measure(FakeLayer(), dist.group.WORLD, torch.device("cpu"))
+    with open(os.path.join(out, f"{rank}.txt"), "w") as fh:
+        fh.write(f"{found.exchange}|{found.why()}")
+    dist.destroy_process_group()
+
+
+def test_links_measure_over_gloo_ranks(tmp_path):
+    """`links.measure` over two CPU ranks with a stand-in probe: both ranks gather the same rate
+    matrix and take the same route (NCCL: the 1->0 pair is slow)."""
+    import socket
+
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    mp.spawn(_links_rank, args=(2, port, str(tmp_path)), nprocs=2, join=True)
+    got = [open(tmp_path / f"{r}.txt").read() for r in range(2)]
+    assert got[0] == got[1] and got[0].startswith("nccl|") and "1->0" in got[0]
