@@ -406,11 +406,12 @@ def first_law_fp32(x, spec, norm: bool, token0: int):
     return out
 
 
-def parity_check(q, k, v, out, rows, rank, group, cfg, spec, device) -> dict:
+def parity_check(q, k, v, out, rows, rank, group, cfg, spec, device, fp8=False) -> dict:
     """One step's output on every rank against fp32 attention computed on that rank's GPU: three
     query heads, up to 512 of this rank's rows (its first and last 256), the keys and values of
     the whole sequence gathered from every rank. The path's bf16 bar: max-abs ≤ 2e-2, mean-abs
-    ≤ 2e-3 (max over ranks)."""
+    ≤ 2e-3 (max over ranks); FP8: cosine similarity ≥ 0.995 per head (min over heads and
+    ranks)."""
     import torch
     import torch.distributed as dist
 
@@ -435,7 +436,7 @@ def parity_check(q, k, v, out, rows, rank, group, cfg, spec, device) -> dict:
     sel = torch.arange(mine, device=device)
     if mine > 512:
         sel = torch.cat([sel[:256], sel[-256:]])
-    worst, total, count = 0.0, 0.0, 0
+    worst, total, count, cos = 0.0, 0.0, 0, 1.0
     for h in pick:
         qx = first_law_fp32(q[:, :, [h]], spec, cfg["norm"], start)[:, sel]
         kvh = kv_pick.index(h // grouping)
@@ -445,17 +446,72 @@ def parity_check(q, k, v, out, rows, rank, group, cfg, spec, device) -> dict:
                 cols = torch.arange(kx.shape[1], device=device)
                 sc = sc.masked_fill(cols[None, :] > (start + sel)[:, None], float("-inf"))
             want = torch.softmax(sc, dim=-1) @ vx[b, :, kvh]
-            err = (out[b, sel, h].float() - want).abs()
+            got = out[b, sel, h].float()
+            err = (got - want).abs()
             worst = max(worst, err.max().item())
             total += err.sum().item()
             count += err.numel()
-    stats = torch.tensor([worst, total / max(count, 1)], dtype=torch.float64, device=device)
+            cos = min(cos, torch.nn.functional.cosine_similarity(
+                got.reshape(1, -1), want.reshape(1, -1)).item())
+    stats = torch.tensor([worst, total / max(count, 1), -cos], dtype=torch.float64, device=device)
     if group is not None:
         dist.all_reduce(stats, op=dist.ReduceOp.MAX, group=group)
-    worst, mean = stats.tolist()
+    worst, mean, neg_cos = stats.tolist()
+    ok = -neg_cos >= 0.995 if fp8 else worst <= 2e-2 and mean <= 2e-3
     return {"max_abs": round(worst, 5), "mean_abs": round(mean, 6),
-            "ok": bool(worst <= 2e-2 and mean <= 2e-3),
+            "min_head_cosine": round(-neg_cos, 6), "ok": bool(ok),
+            "bar": "cosine >= 0.995 per head" if fp8 else "max-abs <= 2e-2, mean-abs <= 2e-3",
             "checked": f"heads {pick}, up to 512 rows a rank, vs fp32 torch on the GPU"}
+
+
+def fp8_first_stage(q, k, v, layout, rank, law, spec, norm, steps, device) -> dict:
+    """The FP8 first stage's kernels alone at this rank's shape (statistics, then the e4m3 pack
+    into every owner's block, all on this GPU), CUDA events; algorithmic bytes ÷ time."""
+    import torch
+
+    from cozy_runtime_b200 import fp8 as fp8_mod
+
+    st = fp8_mod.Fp8Step(q, k, v, layout, rank, rope=spec, norm_q=norm, norm_k=norm, law=law)
+    scales = st.scales()  # this rank's statistics: timing only
+    b, mine, hq, d = (int(n) for n in q.shape)
+    hkv = int(k.shape[2])
+    world = layout.world
+    u8 = torch.uint8
+    codes = [[torch.empty(max(1, mine * b * n[p] * d), dtype=u8, device=device) for p in range(world)]
+             for n in (layout.q_n, layout.kv_n, layout.kv_n)]
+    sc = [[torch.empty(max(1, b * n[p] * mine), device=device) for p in range(world)]
+          for n in (layout.q_n, layout.kv_n)]
+    block = law == "block"
+    acc = [torch.zeros(b, hkv, d, device=device) for _ in range(2)] if block else [
+        torch.zeros(b, n, device=device) for n in (hq, hkv, hkv)]
+
+    def stats():
+        if block:
+            st.stats_into(*acc)
+        else:
+            st.head_amax_into(*acc)
+
+    def pack():
+        st.pack_to(scales, *([t.data_ptr() for t in c] for c in codes),
+                   *([t.data_ptr() for t in c] for c in sc), scale_rows=mine)
+
+    elems = mine * b * d
+    read_stats = (2 * hkv if block else hq + 2 * hkv) * elems * 2
+    moved_pack = (hq + 2 * hkv) * elems * 3 + (hq + hkv) * mine * b * 4
+    out = {"law": law, "rows": mine, "heads": hq}
+    for name, fn, nbytes in (("stats", stats, read_stats), ("pack", pack, moved_pack)):
+        for _ in range(3):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        out[f"{name}_us"] = round(ms * 1e3, 1)
+        out[f"{name}_gbs"] = round(nbytes / (ms * 1e-3) / 1e9, 1)
+    return out
 
 
 def attention_alone(cfg, layout, rank, steps, device) -> float:
@@ -628,6 +684,11 @@ def main() -> None:
 
     # ---- outside the timed region: the output checked, the attention alone, cuDNN, clocks
     extras: dict = {}
+    if not args.no_extras and fp8:
+        extras["parity"] = parity_check(q, k, v, out, rows, rank, group, cfg, spec, device,
+                                        fp8=True)
+        extras["first_stage"] = fp8_first_stage(q, k, v, layout, rank, args.fp8_law, spec,
+                                                norm, max(3, args.steps // 2), device)
     if not args.no_extras and not fp8 and not args.narrow:
         extras["parity"] = parity_check(q, k, v, out, rows, rank, group, cfg, spec, device)
         alone = torch.tensor([attention_alone(cfg, layout, rank, max(3, args.steps // 4),
@@ -831,6 +892,7 @@ def main() -> None:
                 "after_attention_ms": round(after_max, 4),
             },
             "parity": extras.get("parity"),
+            "first_stage": extras.get("first_stage"),
             "clocks": sampler.summary(),
             "long_run": long_run,
             "e2e": None if e2e_ms is None else {
