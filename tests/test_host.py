@@ -397,3 +397,39 @@ def test_links_measure_over_gloo_ranks(tmp_path):
     mp.spawn(_links_rank, args=(2, port, str(tmp_path)), nprocs=2, join=True)
     got = [open(tmp_path / f"{r}.txt").read() for r in range(2)]
     assert got[0] == got[1] and got[0].startswith("nccl|") and "1->0" in got[0]
+
+
+# ------------------------------------------------------------------------ bench reference arm
+def _bench(*args, env=None):
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    return subprocess.run([sys.executable, os.path.join(root, "bench.py"), *args], cwd=root,
+                          env={**os.environ, **(env or {})}, capture_output=True, text=True,
+                          timeout=300)
+
+
+def test_bench_reference_arm_line():
+    """`bench.py --impl reference` prints one JSON line with the contract's keys: the reference
+    arm's value, its cpu_baseline (kind, cores, sample) and an e2e with no device copies."""
+    import json
+
+    run = _bench("--impl", "reference", "--steps", "1", "--warmup", "0")
+    assert run.returncode == 0, run.stderr[-2000:]
+    line = json.loads(run.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and line["value"] > 0 and line["n_gpus"] == 1
+    base = line["cpu_baseline"]
+    assert base["kind"] in ("port", "reference") and base["cores"] >= 1 and base["sample"]
+    assert base["value"] == line["value"]
+    assert line["e2e"] == {"value": line["value"], "unit": line["unit"],
+                           "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+
+
+def test_bench_reference_arm_other_ranks_exit_quietly():
+    """Under torchrun the reference arm runs on rank 0 alone; other ranks exit 0 and print
+    nothing."""
+    run = _bench("--impl", "reference", "--gpus", "2", "--steps", "1", "--warmup", "0",
+                 env={"RANK": "1", "LOCAL_RANK": "1", "WORLD_SIZE": "2"})
+    assert run.returncode == 0, run.stderr[-2000:]
+    assert run.stdout.strip() == ""
