@@ -50,6 +50,7 @@ constexpr int kQKV = 0;  // flag kinds: a call's Q/K/V blocks have landed
 constexpr int kOut = 1;  //             its output rows have landed
 constexpr long long kDefaultWaitNs = 10000000000LL;
 constexpr int kBuffers = 4;  // per set: q, k, v receive buffers and the landing buffer
+constexpr size_t kProbeBytes = 8u << 20;  // the link probe's copy size (see needed())
 
 // Who owns what in one layer (ulysses.py:647 padding: ceil(H / W) query heads a rank; key/value
 // heads as the owned query heads read them).
@@ -103,10 +104,15 @@ Caps needed(const CozyLayerShape& s, const Plan& p, int sms) {
     sum_kv += p.kv_n[r];
   }
   Caps c;
-  c.q = static_cast<size_t>(p.total) * b * most_q * d * el;
+  // The Q receive buffers and the staging buffer never shrink below kProbeBytes: the link probe
+  // (cozy_group_probe) copies between them, and copies much smaller than this measure the
+  // copy's fixed cost, not the link (67 KB copies read 18 GB/s over an NVLink pair that moves
+  // 700 GB/s).
+  c.q = std::max(static_cast<size_t>(p.total) * b * most_q * d * el, kProbeBytes);
   c.kv = static_cast<size_t>(p.total) * b * most_kv * d * el;
   c.land = b * most_rows * s.heads_q * d * el;
-  c.stage = static_cast<size_t>(most_rows) * b * (sum_q + 2 * sum_kv) * d * el;
+  c.stage = std::max(static_cast<size_t>(most_rows) * b * (sum_q + 2 * sum_kv) * d * el,
+                     kProbeBytes);
   c.workspace = cozy::attention_workspace_bytes(s.batch, p.total, p.total, most_q, s.head_dim,
                                                 s.causal, sms);
   return c;

@@ -24,8 +24,8 @@ from dataclasses import dataclass
 #: A pair copying below this (GB/s) is not NVLink class: PCIe 5.0 x16 moves about 50 GB/s a
 #: direction, one NVLink 5 link 50 GB/s, a B200's eighteen 900 GB/s.
 DIRECT_GBS = 100.0
-#: Copies of the group's staging buffer per measured pair.
-REPS = 32
+#: Copies per measured pair (each of the layer's 8 MiB probe size: 64 MiB, ~0.1 ms on NVLink).
+REPS = 8
 
 
 @dataclass(frozen=True)

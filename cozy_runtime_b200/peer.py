@@ -286,7 +286,7 @@ class LayerGroup:
             return None
         return ms.value, nbytes.value
 
-    def probe(self, dst: int, reps: int = 32) -> tuple[float, int]:
+    def probe(self, dst: int, reps: int = 8) -> tuple[float, int]:
         """(ms, bytes) of `reps` copies from this rank's staging buffer into `dst`'s receive
         buffer over the crossing's copy engines (`cozy_group_probe`; no call in flight)."""
         ms, nbytes = ctypes.c_float(0), ctypes.c_ulonglong(0)

@@ -429,7 +429,8 @@ COZY_API int cozy_group_flag(const CozyGroup* group, int kind, int src, long lon
  * bandwidth: bytes / ms). cudaErrorNotReady while that call's copies are still under way. */
 COZY_API int cozy_group_crossing(CozyGroup* group, float* ms, unsigned long long* bytes);
 /* The link probe of one ordered pair (this rank -> `dst`): `reps` back-to-back copies of this
- * rank's staging buffer into dst's receive buffer (set 0), on the copy engines and side stream
+ * rank's staging buffer (at least 8 MiB, whatever the layer shape: smaller copies measure the
+ * copy's fixed cost) into dst's receive buffer (set 0), on the copy engines and side stream
  * the crossing uses; returns their time and bytes. It overwrites dst's receive set 0: call it
  * only while no layer call is in flight on any rank of the group (between barriers). Replaces
  * the reference's per-pair copy measurement (src/cozy_runtime/internal/parallel/links.py:
