@@ -742,7 +742,8 @@ def main() -> None:
     if group is not None and ulysses.links_of(group) is not None:
         links = ulysses.links_of(group).summary()  # the formation's per-pair probe
     crossing = None
-    if transport == "peer" and group is not None:
+    # the crossing of the bf16 layer (the FP8 and int8 wires store into the peers in-kernel)
+    if transport == "peer" and group is not None and not fp8 and not args.narrow:
         # the latest call's crossing on each rank: its copy-engine copies to the other ranks and
         # their flag writes, timed on the side stream (bytes / time = the NVLink rate reached)
         torch.cuda.synchronize()
