@@ -10,22 +10,18 @@
 
 namespace cozy {
 
-// Row ranges an arrival can name: up to 4 pieces of each of COZY_MAX_PEERS sources.
-constexpr int kMaxArrivalRanges = 4 * COZY_MAX_PEERS;
-
 // Rows that are still crossing from other GPUs when the attention starts: rows
-// [src_start[s], src_start[s + 1]) of the (whole-sequence) operands are range s (a piece of one
-// source's rows) and are resident once flags[s] (this GPU's memory, written by that source)
-// reaches `seq`. Ranges [self_lo, self_hi) (this GPU's own rows) are resident at launch. The
-// kernel waits per range, at most `limit_ns`, then reports a peer timeout in the status word
-// and returns.
+// [src_start[s], src_start[s + 1]) of the (whole-sequence) operands come from source s and are
+// resident once flags[s] (this GPU's memory, written by source s) reaches `seq`. Row block
+// `self` is resident at launch. The kernel waits per source, at most `limit_ns`, then reports a
+// peer timeout in the status word and returns.
 struct Arrival {
   const long long* flags;
   long long seq;
   long long limit_ns;
   int n_src;
-  int self_lo, self_hi;
-  int src_start[kMaxArrivalRanges + 1];
+  int self;
+  int src_start[COZY_MAX_PEERS + 1];
 };
 
 // cozy_attention_fwd with an optional arrival (nullptr: every row resident) and the split's

@@ -93,17 +93,15 @@ struct AttentionParams {
   // last block first, which for causal calls is the heaviest); each tile's key blocks run from
   // kv_turn downwards, cyclically (kv_turn < 0: upwards from block 0).
   int q_turn, kv_turn, q_seg;
-  // Rows still crossing from other GPUs: rows [src_start[s], src_start[s + 1]) are range s (a
-  // piece of one source's rows), resident once arrive[s] (a flag in this GPU's memory the source
-  // writes) reaches arrive_seq; the producer waits for a range's flag before its first load of
-  // that range's rows (bounded by arrive_limit_ns, then kStatusPeerTimeout). arrive == nullptr:
-  // all rows are resident. The ranges in arrive_resident (this GPU's own rows) are resident
-  // from the start.
+  // Rows still crossing from other GPUs: rows [src_start[s], src_start[s + 1]) come from source
+  // s, resident once arrive[s] (a flag in this GPU's memory the source writes) reaches
+  // arrive_seq; the producer waits for a source's flag before its first load of that source's
+  // rows (bounded by arrive_limit_ns, then kStatusPeerTimeout). arrive == nullptr: all rows are
+  // resident. Source arrive_self is resident from the start.
   const long long* arrive;
   long long arrive_seq, arrive_limit_ns;
-  unsigned long long arrive_resident;
-  int n_src;
-  int src_start[kMaxArrivalRanges + 1];
+  int n_src, arrive_self;
+  int src_start[COZY_MAX_PEERS + 1];
 };
 
 // Tile index t -> (query block, head, batch). The query blocks are taken in walk order (from
@@ -800,23 +798,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     // Rows [r0, r1) resident: wait for each source not seen yet (warp-uniform; lane 0 polls),
     // then order the flag reads before the tensor copies that read the rows (async proxy).
-    const unsigned long long every =
-        p.n_src >= 64 ? ~0ull : ((1ull << p.n_src) - 1ull);
-    unsigned long long seen = p.arrive != nullptr ? p.arrive_resident : every;
+    uint32_t seen = p.arrive != nullptr ? (1u << p.arrive_self) : 0xffffffffu;
     auto resident = [&](int r0, int r1) -> bool {
-      if (seen == every) return true;
-      unsigned long long need = 0;
+      uint32_t need = 0;
       for (int src = 0; src < p.n_src; ++src)
-        if (p.src_start[src] < r1 && p.src_start[src + 1] > r0) need |= 1ull << src;
+        if (p.src_start[src] < r1 && p.src_start[src + 1] > r0) need |= 1u << src;
       need &= ~seen;
       if (need == 0) return true;
       while (need != 0) {
-        const int src = __ffsll(static_cast<long long>(need)) - 1;
+        const int src = __ffs(need) - 1;
         bool arrived = true;
         if (lane == 0)
           arrived = wait_flag(p.arrive + src, p.arrive_seq, p.arrive_limit_ns, abort, p.status);
         if (!__shfl_sync(0xffffffffu, arrived, 0)) return false;
-        seen |= 1ull << src;
+        seen |= 1u << src;
         need &= need - 1;
       }
       asm volatile("fence.proxy.async.global;" ::: "memory");
@@ -1315,13 +1310,11 @@ static int attention_launch(const void* q, const void* k, const void* v, void* o
   p.arrive_seq = 0;
   p.arrive_limit_ns = 0;
   p.n_src = 0;
-  p.arrive_resident = 0;
+  p.arrive_self = 0;
   if (arrival != nullptr) {
-    if (arrival->flags == nullptr || arrival->n_src < 1 ||
-        arrival->n_src > kMaxArrivalRanges || arrival->self_lo < 0 ||
-        arrival->self_hi <= arrival->self_lo || arrival->self_hi > arrival->n_src ||
-        arrival->limit_ns <= 0 || reinterpret_cast<uintptr_t>(arrival->flags) % 8 != 0 ||
-        seq_q != seq_k)
+    if (arrival->flags == nullptr || arrival->n_src < 1 || arrival->n_src > COZY_MAX_PEERS ||
+        arrival->self < 0 || arrival->self >= arrival->n_src || arrival->limit_ns <= 0 ||
+        reinterpret_cast<uintptr_t>(arrival->flags) % 8 != 0 || seq_q != seq_k)
       return cudaErrorInvalidValue;
     if (arrival->src_start[0] != 0 || arrival->src_start[arrival->n_src] != seq_k)
       return cudaErrorInvalidValue;
@@ -1331,13 +1324,12 @@ static int attention_launch(const void* q, const void* k, const void* v, void* o
     p.arrive_seq = arrival->seq;
     p.arrive_limit_ns = arrival->limit_ns;
     p.n_src = arrival->n_src;
-    for (int r = arrival->self_lo; r < arrival->self_hi; ++r) p.arrive_resident |= 1ull << r;
+    p.arrive_self = arrival->self;
     for (int r = 0; r <= arrival->n_src; ++r) p.src_start[r] = arrival->src_start[r];
     // This GPU's own rows are resident first: every tile's keys start there and walk down
     // through the sources in the order they arrive (each source sends to the ranks after it in
     // turn, so source self - 1 lands first); non-causal query blocks start there too.
-    const int lo = arrival->src_start[arrival->self_lo];
-    const int hi = arrival->src_start[arrival->self_hi];
+    const int lo = arrival->src_start[arrival->self], hi = arrival->src_start[arrival->self + 1];
     if (hi > lo) {
       p.kv_turn = (hi - 1) / kBlockN;
       if (!causal) {

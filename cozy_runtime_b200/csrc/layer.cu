@@ -8,14 +8,12 @@
 //      transpose into per-destination head blocks; r's own block goes straight into r's receive
 //      buffer, the others into a staging buffer;
 //   2. on the side stream, destination by destination (r+1, r+2, ...), the copy engines move each
-//      block into the destination's receive buffer at r's row offset in four pieces of rows,
-//      the last rows first, and after each piece a stream memory write (a system-scope fence,
-//      then the store) sets that piece's arrival flag in the destination's memory;
-//   3. the attention starts at once on r's own rows: its producer warp waits for a piece's flag
-//      before its first load of that piece's rows, and its key and query walks start at r's
-//      own rows and go down through the sources in the order they arrive (a source's rows from
-//      its last down, the order its pieces cross); its epilogue stores every output row into
-//      its owner's landing buffer;
+//      block into the destination's receive buffer at r's row offset, and a stream memory write
+//      (a system-scope fence, then the store) sets r's arrival flag in the destination's memory;
+//   3. the attention starts at once on r's own rows: its producer warp waits for a source's flag
+//      before its first load of that source's rows, and its key and query walks start at r's
+//      own rows and go down through the sources in the order they arrive; its epilogue stores
+//      every output row into its owner's landing buffer;
 //   4. r publishes "my output rows have landed" to every rank, waits (bounded) until every rank
 //      has, and copies its landing buffer into `out`.
 // Buffers are double-buffered by call parity: r writes call n into a peer only after every rank
@@ -48,12 +46,8 @@ int peer_wait(const long long* flags, int count, long long seq, long long limit_
 
 namespace {
 
-// Flags, in this GPU's memory: [world][kPieces] "piece c of source r's Q/K/V rows has landed",
-// then [world] "source r's output rows for this GPU have landed". Each source's rows cross in
-// kPieces pieces, each with its own flag, so the attention takes a source's first rows while
-// its later ones are still crossing.
-constexpr int kPieces = 4;
-constexpr int kOut = 1;  // cozy_group_flag's kinds: 0 a call's Q/K/V rows, 1 its output rows
+constexpr int kQKV = 0;  // flag kinds: a call's Q/K/V blocks have landed
+constexpr int kOut = 1;  //             its output rows have landed
 constexpr long long kDefaultWaitNs = 10000000000LL;
 constexpr int kBuffers = 4;  // per set: q, k, v receive buffers and the landing buffer
 constexpr size_t kProbeBytes = 8u << 20;  // the link probe's copy size (see needed())
@@ -177,7 +171,7 @@ struct CozyGroup {
   int rank = 0, world = 1, device = 0, sms = 0;
   bool local = false;  // every rank in this process on one GPU (peer pointers, no IPC)
   bool opened = false;
-  long long* flags = nullptr;  // [world][kPieces] Q/K/V pieces, then [world] outputs
+  long long* flags = nullptr;  // [2 kinds][world], this GPU's memory
   void* mine[2][kBuffers] = {};
   void* stage = nullptr;
   void* workspace = nullptr;
@@ -255,9 +249,8 @@ int cozy_group_create(int rank, int world, CozyGroup** group) {
   if (e == cudaSuccess)
     e = cudaDeviceGetAttribute(&g->sms, cudaDevAttrMultiProcessorCount, g->device);
   g->write_value = e == cudaSuccess && stream_mem_ops(g->device) && write_value64() != nullptr;
-  const size_t flag_bytes = static_cast<size_t>(world) * (kPieces + 1) * 8;
-  if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&g->flags), flag_bytes);
-  if (e == cudaSuccess) e = cudaMemset(g->flags, 0, flag_bytes);
+  if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&g->flags), 2 * world * 8);
+  if (e == cudaSuccess) e = cudaMemset(g->flags, 0, 2 * world * 8);
   if (e == cudaSuccess && !g->write_value)
     e = cudaHostAlloc(reinterpret_cast<void**>(&g->ring), kRing * sizeof(long long),
                       cudaHostAllocDefault);
@@ -403,16 +396,8 @@ int cozy_group_flag(const CozyGroup* g, int kind, int src, long long* value) {
   if (g == nullptr || value == nullptr || kind < 0 || kind > 1 || src < 0 || src >= g->world ||
       g->flags == nullptr)
     return cudaErrorInvalidValue;
-  if (kind == kOut)
-    return cudaMemcpy(value, g->flags + g->world * kPieces + src, sizeof(long long),
-                      cudaMemcpyDeviceToHost);
-  // Q/K/V: the call all of whose pieces have landed
-  long long pieces[kPieces];
-  const cudaError_t e = cudaMemcpy(pieces, g->flags + src * kPieces, sizeof(pieces),
-                                   cudaMemcpyDeviceToHost);
-  if (e != cudaSuccess) return e;
-  *value = *std::min_element(pieces, pieces + kPieces);
-  return cudaSuccess;
+  return cudaMemcpy(value, g->flags + kind * g->world + src, sizeof(long long),
+                    cudaMemcpyDeviceToHost);
 }
 
 int cozy_group_crossing(CozyGroup* g, float* ms, unsigned long long* bytes) {
@@ -522,36 +507,29 @@ int cozy_ulysses_layer_begin(CozyGroup* g, const CozyLayerCall* c, uintptr_t str
   g->cross_bytes = 0;
   for (int step = 1; step < world; ++step) {
     const int p = (me + step) % world;
-    // pieces from the last rows down: the owner's key walk meets this rank's rows from the top
-    for (int c = kPieces - 1; c >= 0; --c) {
-      const size_t r0 = mine * c / kPieces, r1 = mine * (c + 1) / kPieces;
-      for (int i = 0; i < 3 && r1 > r0; ++i) {
-        const int n = i == 0 ? plan.q_n[p] : plan.kv_n[p];
-        const size_t row_bytes = b * n * d * el;
-        const size_t bytes = (r1 - r0) * row_bytes;
-        if (bytes == 0) continue;
-        g->cross_bytes += bytes;
-        uint8_t* dst = static_cast<uint8_t*>(g->peer[p][set][i]) + row_offset(plan, s, me, n) +
-                       r0 * row_bytes;
-        if ((e = cudaMemcpyAsync(dst, static_cast<uint8_t*>(g->stage) + block_off[i][p] +
-                                          r0 * row_bytes,
-                                 bytes, cudaMemcpyDeviceToDevice, g->side)) != cudaSuccess)
-          return e;
-      }
-      long long* flag = g->peer_flags[p] + me * kPieces + c;
-      if (g->write_value) {
-        const CUresult r = write_value64()(reinterpret_cast<CUstream>(g->side),
-                                           reinterpret_cast<CUdeviceptr>(flag),
-                                           static_cast<cuuint64_t>(seq), 0);
-        if (r != CUDA_SUCCESS) return cudaErrorLaunchFailure;
-      } else {
-        // the flag word crosses as one more copy, behind the blocks on the same stream
-        long long* word = g->ring + (seq % kRing);
-        *word = seq;
-        if ((e = cudaMemcpyAsync(flag, word, sizeof(long long), cudaMemcpyHostToDevice, g->side)) !=
-            cudaSuccess)
-          return e;
-      }
+    for (int i = 0; i < 3; ++i) {
+      const int n = i == 0 ? plan.q_n[p] : plan.kv_n[p];
+      const size_t bytes = mine * b * n * d * el;
+      if (bytes == 0) continue;
+      g->cross_bytes += bytes;
+      uint8_t* dst = static_cast<uint8_t*>(g->peer[p][set][i]) + row_offset(plan, s, me, n);
+      if ((e = cudaMemcpyAsync(dst, static_cast<uint8_t*>(g->stage) + block_off[i][p], bytes,
+                               cudaMemcpyDeviceToDevice, g->side)) != cudaSuccess)
+        return e;
+    }
+    long long* flag = g->peer_flags[p] + kQKV * world + me;
+    if (g->write_value) {
+      const CUresult r = write_value64()(reinterpret_cast<CUstream>(g->side),
+                                         reinterpret_cast<CUdeviceptr>(flag),
+                                         static_cast<cuuint64_t>(seq), 0);
+      if (r != CUDA_SUCCESS) return cudaErrorLaunchFailure;
+    } else {
+      // the flag word crosses as one more copy, behind the blocks on the same stream
+      long long* word = g->ring + (seq % kRing);
+      *word = seq;
+      if ((e = cudaMemcpyAsync(flag, word, sizeof(long long), cudaMemcpyHostToDevice, g->side)) !=
+          cudaSuccess)
+        return e;
     }
   }
   if ((e = cudaEventRecord(g->cross_end, g->side)) != cudaSuccess) return e;
@@ -587,18 +565,12 @@ int cozy_ulysses_layer_attend(CozyGroup* g, const CozyLayerCall* c, uintptr_t st
     }
     cozy::Arrival arrival;
     memset(&arrival, 0, sizeof(arrival));
-    arrival.flags = g->flags;
+    arrival.flags = g->flags + kQKV * world;
     arrival.seq = seq;
     arrival.limit_ns = c->wait_limit_ns > 0 ? c->wait_limit_ns : kDefaultWaitNs;
-    arrival.n_src = world * kPieces;
-    arrival.self_lo = me * kPieces;
-    arrival.self_hi = (me + 1) * kPieces;
-    // the pieces' rows, as each source cuts them (its rows r0..r1 of piece c, above)
-    for (int p = 0; p < world; ++p)
-      for (int k = 0; k < kPieces; ++k)
-        arrival.src_start[p * kPieces + k] =
-            plan.start[p] + static_cast<int>(static_cast<long long>(s.rows[p]) * k / kPieces);
-    arrival.src_start[world * kPieces] = plan.start[world];
+    arrival.n_src = world;
+    arrival.self = me;
+    for (int p = 0; p <= world; ++p) arrival.src_start[p] = plan.start[p];
     const float scale = c->scale > 0.f ? c->scale : 1.f / sqrtf(static_cast<float>(d));
     e = cozy::attention_forward_ex(g->mine[set][0], g->mine[set][1], g->mine[set][2], nullptr,
                                    s.batch, plan.total, plan.total, qn, kvn, s.head_dim, qs, ks,
@@ -611,7 +583,7 @@ int cozy_ulysses_layer_attend(CozyGroup* g, const CozyLayerCall* c, uintptr_t st
   CozyPeerSlots slots;
   memset(&slots, 0, sizeof(slots));
   slots.count = world;
-  for (int p = 0; p < world; ++p) slots.slot[p] = g->peer_flags[p] + world * kPieces + me;
+  for (int p = 0; p < world; ++p) slots.slot[p] = g->peer_flags[p] + kOut * world + me;
   return cozy::peer_signal(&slots, seq, c->status, stream);
 }
 
@@ -625,7 +597,7 @@ int cozy_ulysses_layer_end(CozyGroup* g, const CozyLayerCall* c, uintptr_t strea
   const long long seq = g->seq;
   const int set = static_cast<int>(seq & 1);
   const long long limit = c->wait_limit_ns > 0 ? c->wait_limit_ns : kDefaultWaitNs;
-  if ((e = cozy::peer_wait(g->flags + g->world * kPieces, g->world, seq, limit, c->status,
+  if ((e = cozy::peer_wait(g->flags + kOut * g->world, g->world, seq, limit, c->status,
                            stream)) != cudaSuccess)
     return e;
   const size_t bytes =
