@@ -433,3 +433,32 @@ def test_bench_reference_arm_other_ranks_exit_quietly():
                  env={"RANK": "1", "LOCAL_RANK": "1", "WORLD_SIZE": "2"})
     assert run.returncode == 0, run.stderr[-2000:]
     assert run.stdout.strip() == ""
+
+
+# ------------------------------------------------------------------- context-parallel types
+def test_group_mesh_serves_the_backend_its_group():
+    """A parallel config built from `CpComms` and `GroupMesh` (the reference's cp.py:32-77)
+    hands `attention_ulysses.group` its process group; the ring axis refuses."""
+    from cozy_runtime_b200 import attention_ulysses, cp
+
+    sentinel = object()
+    mesh = cp.GroupMesh(cp.CpComms(pg=sentinel, rank=1, device="cpu"), size=4, local_rank=1)
+    assert mesh.size() == 4 and mesh.get_local_rank() == 1
+    assert mesh["ulysses"].get_group() is sentinel and mesh[("ulysses",)].get_group() is sentinel
+    with pytest.raises(cp.ContextParallelUnavailable):
+        mesh["ring"].get_group()
+    with pytest.raises(KeyError):
+        mesh["tensor"]
+
+    class ContextParallelConfig:
+        ring_degree = 1
+        _ulysses_mesh = mesh
+
+    class ParallelConfig:
+        context_parallel_config = ContextParallelConfig()
+
+    attention_ulysses.serve(None)
+    assert attention_ulysses.group(ParallelConfig()) is sentinel
+    ContextParallelConfig.ring_degree = 2
+    with pytest.raises(ValueError):
+        attention_ulysses.group(ParallelConfig())
