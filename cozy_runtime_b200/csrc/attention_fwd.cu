@@ -662,9 +662,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       dst = p.out + static_cast<long long>(b) * p.out_b +
             static_cast<long long>(q_row) * p.out_s + static_cast<long long>(head) * p.out_h;
     }
-    // 32 fp32 columns of the row's O (against its row sum's reference) -> bf16 output
-    auto emit = [&](int c, const uint32_t (&o)[32], float inv) {
-      uint32_t packed[16];
+    // 32 fp32 columns of the row's O (against its row sum's reference) -> 16 bf16 pairs
+    auto pack_chunk = [&](int c, const uint32_t (&o)[32], float inv, uint32_t (&packed)[16]) {
       if constexpr (FP8) {  // V's per-channel scales
         const float* vs = p.v_scale +
                           (static_cast<long long>(b) * p.heads_kv + kv_head) * HD + c * 32;
@@ -678,6 +677,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           packed[i] = pack_bf16x2(__uint_as_float(o[2 * i]) * inv,
                                   __uint_as_float(o[2 * i + 1]) * inv);
       }
+    };
+    // ... straight to the row's destination, 16 bytes a store
+    auto emit = [&](int c, const uint32_t (&o)[32], float inv) {
+      uint32_t packed[16];
+      pack_chunk(c, o, inv, packed);
       if (valid) {
         uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
 #pragma unroll
@@ -766,6 +770,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (ok) {
       // rows that saw no key (bottom-right causal with seq_q > seq_k) are written as zeros
       const float inv = (l > 0.f && m != -INFINITY) ? 1.f / l : 0.f;
+      // With a scatter most rows go to other GPUs' memory. A warp's 32 rows are staged in its
+      // quarter of this tile's Q buffer (free: every MMA that read it completed before o_final,
+      // and a bf16 Q tile is exactly the 128 rows × HD bf16 of the output tile)
+      // and leave as whole rows, CPR lanes a row, so each store instruction writes whole 32-byte
+      // sectors of RPI rows instead of one 16-byte piece of 32 rows.
+      constexpr int CPR = HD / 8;  // 16-byte chunks a row
+      constexpr int RPI = 32 / CPR;  // rows a store instruction
+      // (bf16 only: the FP8 kernel's e4m3 Q tile is half the bytes of a bf16 output tile)
+      const bool staged = !FP8 && p.scatter && n_kv > 0;
+      uint8_t* stage = reinterpret_cast<uint8_t*>(
+                           (reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                           ~static_cast<uintptr_t>(1023)) +
+                       L::kQOffset + e_s * L::kTileBytes + quarter * (32 * HD * 2);
 #pragma unroll
       for (int c = 0; c < HD / 32; ++c) {
         uint32_t o[32];
@@ -777,7 +794,34 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] = 0u;
         }
-        emit(c, o, inv);
+        if (staged) {
+          uint32_t packed[16];
+          pack_chunk(c, o, inv, packed);
+          // chunk j of row r sits at chunk j ^ (r mod CPR): the row's writers and the
+          // cooperative readers below both spread over the banks
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int j = c * 4 + i;
+            *reinterpret_cast<uint4*>(stage + e_lane * (HD * 2) + ((j ^ (e_lane % CPR)) * 16)) =
+                make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+          }
+        } else {
+          emit(c, o, inv);
+        }
+      }
+      if (staged) {
+        __syncwarp();
+        const int sub = e_lane / CPR, ch = e_lane % CPR;
+        const unsigned long long my_dst = reinterpret_cast<unsigned long long>(dst);
+#pragma unroll 4
+        for (int r0 = 0; r0 < 32; r0 += RPI) {
+          const int r = r0 + sub;
+          const unsigned long long row_dst = __shfl_sync(0xffffffffu, my_dst, r);
+          const bool row_valid = __shfl_sync(0xffffffffu, valid, r);
+          const uint4 v =
+              *reinterpret_cast<const uint4*>(stage + r * (HD * 2) + ((ch ^ (r % CPR)) * 16));
+          if (row_valid) reinterpret_cast<uint4*>(row_dst)[ch] = v;
+        }
       }
     }
     }
