@@ -75,7 +75,10 @@ def raise_if_failed(device: torch.device) -> None:
     """Raise if an earlier call on `device` reported a timed-out wait, as far as the watch has
     seen without synchronizing (the reference raises after any failure of an exchange,
     src/cozy_runtime/internal/parallel/ulysses.py:754-758). The word is cleared, so the error is
-    raised once."""
+    raised once. While a stream is being captured into a CUDA graph nothing is checked (an
+    event query is not allowed then); the watch resumes with the next eager call."""
+    if torch.cuda.is_current_stream_capturing():
+        return
     index = device.index if device.index is not None else torch.cuda.current_device()
     watch = _WATCHES.get(index)
     word = watch.failed() if watch is not None else 0
