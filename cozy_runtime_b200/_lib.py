@@ -210,6 +210,7 @@ class LayerCall(Structure):
         ("norm_eps", c_float * 2),
         ("wait_limit_ns", c_longlong),
         ("status", c_void_p),
+        ("gate", c_int),
     ]
 
 

@@ -461,6 +461,21 @@ int cozy_group_flag_mode(const CozyGroup* g) {
   return g->write_value ? 1 : 2;
 }
 
+// Sets `flag` (this GPU's or a peer's) to `seq` behind `stream`'s earlier work: a stream memory
+// write (a system-scope fence, then the store), or the copy of a pinned host word where the
+// device lacks 64-bit stream writes.
+static int write_flag(CozyGroup* g, long long* flag, long long seq, cudaStream_t stream) {
+  if (g->write_value) {
+    const CUresult r = write_value64()(reinterpret_cast<CUstream>(stream),
+                                       reinterpret_cast<CUdeviceptr>(flag),
+                                       static_cast<cuuint64_t>(seq), 0);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorLaunchFailure;
+  }
+  long long* word = g->ring + (seq % kRing);
+  *word = seq;
+  return cudaMemcpyAsync(flag, word, sizeof(long long), cudaMemcpyHostToDevice, stream);
+}
+
 int cozy_ulysses_layer_begin(CozyGroup* g, const CozyLayerCall* c, uintptr_t stream_handle) {
   Plan plan;
   int e = check_call(g, c, &plan);
@@ -517,6 +532,9 @@ int cozy_ulysses_layer_begin(CozyGroup* g, const CozyLayerCall* c, uintptr_t str
           cudaSuccess)
     return e;
   if ((e = cudaEventRecord(g->packed, stream)) != cudaSuccess) return e;
+  if (c->gate && world > 1 && (e = write_flag(g, g->flags + kQKV * world + me, seq, stream)) !=
+                                  cudaSuccess)
+    return e;
   // 2. the crossing: copy engines, destination by destination, each followed by its flag
   const int used = std::min(world - 1, kLanes);
   for (int l = 0; l < std::max(used, 1); ++l)
@@ -536,20 +554,8 @@ int cozy_ulysses_layer_begin(CozyGroup* g, const CozyLayerCall* c, uintptr_t str
                                cudaMemcpyDeviceToDevice, lane)) != cudaSuccess)
         return e;
     }
-    long long* flag = g->peer_flags[p] + kQKV * world + me;
-    if (g->write_value) {
-      const CUresult r = write_value64()(reinterpret_cast<CUstream>(lane),
-                                         reinterpret_cast<CUdeviceptr>(flag),
-                                         static_cast<cuuint64_t>(seq), 0);
-      if (r != CUDA_SUCCESS) return cudaErrorLaunchFailure;
-    } else {
-      // the flag word crosses as one more copy, behind the blocks on the same stream
-      long long* word = g->ring + (seq % kRing);
-      *word = seq;
-      if ((e = cudaMemcpyAsync(flag, word, sizeof(long long), cudaMemcpyHostToDevice, lane)) !=
-          cudaSuccess)
-        return e;
-    }
+    if ((e = write_flag(g, g->peer_flags[p] + kQKV * world + me, seq, lane)) != cudaSuccess)
+      return e;
   }
   // lane 0 joins the others: `sent` and the crossing's end cover every lane
   for (int l = 1; l < used; ++l) {
@@ -571,6 +577,13 @@ int cozy_ulysses_layer_attend(CozyGroup* g, const CozyLayerCall* c, uintptr_t st
   const long long seq = g->seq;
   const int set = static_cast<int>(seq & 1);
   const int qn = plan.q_n[me], kvn = plan.kv_n[me];
+  const bool gate = c->gate && world > 1;
+  if (gate) {  // every source's rows (this rank's own flag set after its pack) before the attention
+    const long long limit = c->wait_limit_ns > 0 ? c->wait_limit_ns : kDefaultWaitNs;
+    if ((e = cozy::peer_wait(g->flags + kQKV * world, world, seq, limit, c->status, stream)) !=
+        cudaSuccess)
+      return e;
+  }
   if (qn > 0) {
     const long long b = s.batch, d = s.head_dim;
     const long long qs[3] = {b * qn * d, d, qn * d};
@@ -599,7 +612,7 @@ int cozy_ulysses_layer_attend(CozyGroup* g, const CozyLayerCall* c, uintptr_t st
     e = cozy::attention_forward_ex(g->mine[set][0], g->mine[set][1], g->mine[set][2], nullptr,
                                    s.batch, plan.total, plan.total, qn, kvn, s.head_dim, qs, ks,
                                    ks, nullptr, &map, &sc, s.causal, scale, c->status,
-                                   world > 1 ? &arrival : nullptr, g->workspace,
+                                   world > 1 && !gate ? &arrival : nullptr, g->workspace,
                                    g->caps.workspace, stream);
     if (e != cudaSuccess) return e;
   }

@@ -731,7 +731,18 @@ def _layer_call(
         call.norm_eps[i] = float(norm.eps)
     call.wait_limit_ns = int(wait_limit_ns)
     call.status = status
+    call.gate = int(layer_gate(len(rows)))
     return call, keep
+
+
+def layer_gate(world: int) -> bool:
+    """Whether the NVLink layer holds the attention until every source's rows have landed
+    (`CozyLayerCall.gate`) instead of letting it start at once and wait per source inside the
+    kernel. `COZY_LAYER_GATE` = 1 / 0 forces either."""
+    forced = os.environ.get("COZY_LAYER_GATE", "")
+    if forced in ("0", "1"):
+        return forced == "1"
+    return False
 
 
 def _exchange_peer(

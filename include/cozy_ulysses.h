@@ -406,6 +406,10 @@ typedef struct CozyLayerCall {
   float norm_eps[2];          /* Q, K */
   long long wait_limit_ns; /* the longest a wait on another rank may take (0: 10 s) */
   int* status;             /* device status word (0 = fine) */
+  int gate;                /* 0: the attention starts at once and waits per source inside the
+                              kernel; 1: a wait kernel holds it until every source's rows have
+                              landed (every rank then starts its attention at nearly the same
+                              moment) */
 } CozyLayerCall;
 
 COZY_API int cozy_group_create(int rank, int world, CozyGroup** group);

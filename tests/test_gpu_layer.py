@@ -108,6 +108,29 @@ def test_layer_matches_oracle(world, batch, seq, hq, hkv, dim, causal):
     _close(groups)
 
 
+@pytest.mark.parametrize("world,seq,hq,hkv,causal", [(3, 1100, 5, 5, False),
+                                                     (8, 4159 * 2, 24, 24, False),
+                                                     (4, 1500, 8, 2, True)])
+def test_layer_gate_matches_oracle(monkeypatch, world, seq, hq, hkv, causal):
+    """The gated layer (`CozyLayerCall.gate`: a wait kernel holds the attention until every
+    source's rows have landed, then it runs with every row resident) against the oracle."""
+    from cozy_runtime_b200 import attention
+
+    monkeypatch.setenv("COZY_LAYER_GATE", "1")
+    g = torch.Generator().manual_seed(seq + 3 * world)
+    q = torch.randn(1, seq, hq, 128, generator=g).to(torch.bfloat16)
+    k = torch.randn(1, seq, hkv, 128, generator=g).to(torch.bfloat16)
+    v = torch.randn(1, seq, hkv, 128, generator=g).to(torch.bfloat16)
+    got, groups = simulate_layer(q, k, v, world, causal=causal)
+    attention.check_status(torch.device("cuda"))
+    heads = list(range(0, hq, max(1, hq // 4)))
+    group = hq // hkv
+    want = oracle.attention_fp32(q[:, :, heads], k[:, :, [h // group for h in heads]],
+                                 v[:, :, [h // group for h in heads]], causal=causal)
+    _check(got[:, :, heads], want)
+    _close(groups)
+
+
 def test_layer_twice_uses_both_buffer_sets():
     """Two calls in a row on the same groups (call parity picks the other set of receive and
     landing buffers) give identical outputs."""
