@@ -881,6 +881,7 @@ def main() -> None:
             "transport": transport,
             "flag_mode": flag_mode,
             "layer_gate": ulysses.layer_gate(world) if transport == "peer" else None,
+            "layer_cross": ulysses.layer_cross(world) if transport == "peer" else None,
             "crossing": crossing,
             "links": links,
             "layer": {

@@ -211,6 +211,7 @@ class LayerCall(Structure):
         ("wait_limit_ns", c_longlong),
         ("status", c_void_p),
         ("gate", c_int),
+        ("cross", c_int),
     ]
 
 

@@ -488,9 +488,13 @@ int cozy_ulysses_layer_begin(CozyGroup* g, const CozyLayerCall* c, uintptr_t str
   const int set = static_cast<int>(seq & 1);
   const size_t el = 2, d = static_cast<size_t>(s.head_dim), b = static_cast<size_t>(s.batch);
   const size_t mine = static_cast<size_t>(s.rows[me]);
+  const bool sm_cross = c->cross && world > 1;
   // the staging buffer is free once the previous call's copies have left
   if ((e = cudaStreamWaitEvent(stream, g->sent, 0)) != cudaSuccess) return e;
-  // 1. first stage: own block into own receive buffer, the others into staging
+  if (sm_cross && (e = cudaEventRecord(g->cross_start, stream)) != cudaSuccess) return e;
+  // 1. first stage: own block into own receive buffer, the others into staging (copy-engine
+  //    crossing) or straight into their owners' receive buffers (SM crossing; destinations
+  //    listed from this rank on, so the ranks write to different peers at any moment)
   CozyPackTensor t[3];
   memset(t, 0, sizeof(t));
   const void* src[3] = {c->q, c->k, c->v};
@@ -508,6 +512,16 @@ int cozy_ulysses_layer_begin(CozyGroup* g, const CozyLayerCall* c, uintptr_t str
     t[i].norm_offset = i < 2 ? c->norm_offset[i] : 0.f;
     t[i].norm_eps = i < 2 ? c->norm_eps[i] : 0.f;
     for (int p = 0; p < world; ++p) {
+      if (sm_cross) {
+        const int q = (me + p) % world;
+        const int n = i == 0 ? plan.q_n[q] : plan.kv_n[q];
+        t[i].head_lo[p] = i == 0 ? plan.q_lo[q] : plan.kv_lo[q];
+        t[i].head_n[p] = n;
+        t[i].dst[p] = n == 0 ? nullptr
+                             : static_cast<uint8_t*>(g->peer[q][set][i]) +
+                                   row_offset(plan, s, me, n);
+        continue;
+      }
       const int n = i == 0 ? plan.q_n[p] : plan.kv_n[p];
       t[i].head_lo[p] = i == 0 ? plan.q_lo[p] : plan.kv_lo[p];
       t[i].head_n[p] = n;
@@ -528,9 +542,25 @@ int cozy_ulysses_layer_begin(CozyGroup* g, const CozyLayerCall* c, uintptr_t str
   }
   if (mine > 0 &&
       (e = cozy::ulysses_pack_to(t, 3, world, s.rows[me], s.batch, s.head_dim,
-                                 c->rope != nullptr ? &rope : nullptr, false, stream)) !=
+                                 c->rope != nullptr ? &rope : nullptr, sm_cross, stream)) !=
           cudaSuccess)
     return e;
+  if (sm_cross) {
+    // 2. the flags: every block stored (the pack's bulk stores complete before it ends), one
+    //    kernel fences at system scope and sets this rank's flag in every rank's memory
+    //    (its own too, which the gate waits on)
+    CozyPeerSlots slots;
+    memset(&slots, 0, sizeof(slots));
+    slots.count = world;
+    for (int p = 0; p < world; ++p) slots.slot[p] = g->peer_flags[p] + kQKV * world + me;
+    if ((e = cozy::peer_signal(&slots, seq, c->status, stream)) != cudaSuccess) return e;
+    g->cross_bytes = 0;
+    for (int p = 0; p < world; ++p)
+      if (p != me)
+        g->cross_bytes += mine * b * (plan.q_n[p] + 2 * plan.kv_n[p]) * d * el;
+    if ((e = cudaEventRecord(g->cross_end, stream)) != cudaSuccess) return e;
+    return cudaEventRecord(g->sent, stream);
+  }
   if ((e = cudaEventRecord(g->packed, stream)) != cudaSuccess) return e;
   if (c->gate && world > 1 && (e = write_flag(g, g->flags + kQKV * world + me, seq, stream)) !=
                                   cudaSuccess)

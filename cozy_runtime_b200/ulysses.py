@@ -732,7 +732,18 @@ def _layer_call(
     call.wait_limit_ns = int(wait_limit_ns)
     call.status = status
     call.gate = int(layer_gate(len(rows)))
+    call.cross = int(layer_cross(len(rows)) == "sm")
     return call, keep
+
+
+def layer_cross(world: int) -> str:
+    """How the NVLink layer's blocks cross (`CozyLayerCall.cross`): "ce" (copy engines from a
+    staging buffer, beside the attention) or "sm" (the first stage stores straight into the
+    owners' buffers). `COZY_LAYER_CROSS` forces either."""
+    forced = os.environ.get("COZY_LAYER_CROSS", "")
+    if forced in ("ce", "sm"):
+        return forced
+    return "ce"
 
 
 def layer_gate(world: int) -> bool:

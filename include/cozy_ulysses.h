@@ -410,6 +410,10 @@ typedef struct CozyLayerCall {
                               kernel; 1: a wait kernel holds it until every source's rows have
                               landed (every rank then starts its attention at nearly the same
                               moment) */
+  int cross;               /* 0: the first stage packs the other ranks' blocks into a staging
+                              buffer and copy engines move them, beside the attention; 1: the
+                              first stage stores them straight into their owners' receive
+                              buffers over NVLink (SM stores), and one kernel sets the flags */
 } CozyLayerCall;
 
 COZY_API int cozy_group_create(int rank, int world, CozyGroup** group);

@@ -111,13 +111,40 @@ def test_layer_matches_oracle(world, batch, seq, hq, hkv, dim, causal):
 @pytest.mark.parametrize("world,seq,hq,hkv,causal", [(3, 1100, 5, 5, False),
                                                      (8, 4159 * 2, 24, 24, False),
                                                      (4, 1500, 8, 2, True)])
-def test_layer_gate_matches_oracle(monkeypatch, world, seq, hq, hkv, causal):
+@pytest.mark.parametrize("cross", ["ce", "sm"])
+def test_layer_gate_matches_oracle(monkeypatch, world, seq, hq, hkv, causal, cross):
     """The gated layer (`CozyLayerCall.gate`: a wait kernel holds the attention until every
     source's rows have landed, then it runs with every row resident) against the oracle."""
     from cozy_runtime_b200 import attention
 
     monkeypatch.setenv("COZY_LAYER_GATE", "1")
+    monkeypatch.setenv("COZY_LAYER_CROSS", cross)
     g = torch.Generator().manual_seed(seq + 3 * world)
+    q = torch.randn(1, seq, hq, 128, generator=g).to(torch.bfloat16)
+    k = torch.randn(1, seq, hkv, 128, generator=g).to(torch.bfloat16)
+    v = torch.randn(1, seq, hkv, 128, generator=g).to(torch.bfloat16)
+    got, groups = simulate_layer(q, k, v, world, causal=causal)
+    attention.check_status(torch.device("cuda"))
+    heads = list(range(0, hq, max(1, hq // 4)))
+    group = hq // hkv
+    want = oracle.attention_fp32(q[:, :, heads], k[:, :, [h // group for h in heads]],
+                                 v[:, :, [h // group for h in heads]], causal=causal)
+    _check(got[:, :, heads], want)
+    _close(groups)
+
+
+@pytest.mark.parametrize("world,seq,hq,hkv,causal", [(3, 1100, 5, 5, False),
+                                                     (8, 4159 * 2, 24, 24, False),
+                                                     (7, 2000, 32, 8, True)])
+def test_layer_sm_crossing_matches_oracle(monkeypatch, world, seq, hq, hkv, causal):
+    """The SM crossing (`CozyLayerCall.cross`: the first stage stores every block straight
+    into its owner's receive buffer, one kernel sets the flags) with the attention's in-kernel
+    waits, against the oracle."""
+    from cozy_runtime_b200 import attention
+
+    monkeypatch.setenv("COZY_LAYER_CROSS", "sm")
+    monkeypatch.setenv("COZY_LAYER_GATE", "0")
+    g = torch.Generator().manual_seed(seq + 5 * world)
     q = torch.randn(1, seq, hq, 128, generator=g).to(torch.bfloat16)
     k = torch.randn(1, seq, hkv, 128, generator=g).to(torch.bfloat16)
     v = torch.randn(1, seq, hkv, 128, generator=g).to(torch.bfloat16)
