@@ -743,7 +743,12 @@ def layer_cross(world: int) -> str:
     forced = os.environ.get("COZY_LAYER_CROSS", "")
     if forced in ("ce", "sm"):
         return forced
-    return "ce"
+    # Measured at C2 on one B200 node: degree 8, SM stores cross 67 MB a rank at 518 GB/s
+    # (1.709 ms layer) against 234 GB/s on the copy engines (1.846 ms; seven streams at once
+    # were no faster than one); degree 2, the copy engines' crossing (444 GB/s) hides under the
+    # attention's own-rows work and the layer matched the SM-store design (6.02-6.09 against
+    # 5.91-6.06 ms).
+    return "sm" if world >= 4 else "ce"
 
 
 def layer_gate(world: int) -> bool:
