@@ -16,6 +16,11 @@
 //      every output row into its owner's landing buffer;
 //   4. r publishes "my output rows have landed" to every rank, waits (bounded) until every rank
 //      has, and copies its landing buffer into `out`.
+// With `cross` set (SM crossing, the Python side's choice from degree 4), steps 1-2 become one:
+// the first stage stores every block straight into its owner's receive buffer (bulk stores from
+// shared memory) and one kernel fences at system scope and sets the flags. With `gate` set, a
+// wait kernel holds the attention until every source has landed, and it runs with every row
+// resident.
 // Buffers are double-buffered by call parity: r writes call n into a peer only after every rank
 // finished call n - 1 (step 4 of call n - 1), so every read of the set of call n - 2 is done. No
 // SM is needed for the crossing itself, so the copies and the attention overlap.

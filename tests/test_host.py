@@ -462,3 +462,17 @@ def test_group_mesh_serves_the_backend_its_group():
     ContextParallelConfig.ring_degree = 2
     with pytest.raises(ValueError):
         attention_ulysses.group(ParallelConfig())
+
+
+def test_layer_crossing_policy(monkeypatch):
+    """The NVLink layer crosses by SM stores from degree 4 and by copy engines below (the
+    measured choice), unless `COZY_LAYER_CROSS` forces one; the gate is off unless forced."""
+    from cozy_runtime_b200 import ulysses
+
+    monkeypatch.delenv("COZY_LAYER_CROSS", raising=False)
+    monkeypatch.delenv("COZY_LAYER_GATE", raising=False)
+    assert [ulysses.layer_cross(w) for w in (2, 3, 4, 7, 8)] == ["ce", "ce", "sm", "sm", "sm"]
+    assert not ulysses.layer_gate(8)
+    monkeypatch.setenv("COZY_LAYER_CROSS", "ce")
+    monkeypatch.setenv("COZY_LAYER_GATE", "1")
+    assert ulysses.layer_cross(8) == "ce" and ulysses.layer_gate(2)
