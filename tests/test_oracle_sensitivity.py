@@ -72,3 +72,23 @@ def test_exchange_golden_rejects_top_left_causal():
     scores = scores.masked_fill(~top_left, float("-inf"))
     wrong = torch.einsum("bhqk,bkhd->bqhd", scores.softmax(-1), vv.float())
     assert (wrong - want[:, half:]).abs().max() > 1e-2
+
+
+def test_fp8_head_golden_rejects_an_unrotated_quantiser():
+    """The reference's FP8 row rotates Q and K by the Hadamard before the per-head scale is
+    taken: quantising the unrotated keys gives other codes and descales."""
+    case = load("fp8_head.npz")
+    codes, descale = oracle.quantise_e4m3_per_head(tensor(case["k"]))
+    assert not np.array_equal(codes.view(torch.uint8).numpy(), case["k_codes"])
+    assert not np.array_equal(descale.numpy(), case["k_descale"])
+
+
+def test_fp8_head_golden_rejects_an_fp32_rotation():
+    """The reference's rotation is a bf16 matrix product (result rounded to bf16): an fp32
+    rotation with the exact 1/sqrt(128) moves many of the rotated values off the fixture."""
+    case = load("fp8_head.npz")
+    x = tensor(case["q"]).float()
+    exact = x @ oracle.hadamard_matrix(x.shape[-1])
+    want = tensor(case["rq"]).float()
+    assert (exact != want).float().mean().item() > 0.5
+    assert (oracle.rotate_bf16(tensor(case["q"])).float() != want).float().mean().item() < 1e-4
