@@ -835,13 +835,17 @@ def main() -> None:
         kernel_ms = alone_ms if alone_ms else span_max
         ach = my_flops / (kernel_ms * 1e-3) / 1e12 if kernel_ms else 0.0
         # my kernels a step: first stage + attention, then per transport the land (NCCL) or
-        # a signal and a wait kernel (peer: the crossing is copy engines and stream writes); FP8
-        # adds the statistics kernel
+        # the output flags' signal and wait kernels (peer: a copy-engine crossing is copies and
+        # stream writes; an SM crossing adds the arrival flags' signal kernel, the gate a wait
+        # kernel); FP8: statistics, e4m3 first stage and attention, over NVLink with the
+        # arrival and output flags' signal and wait kernels
         kernels = 1 + (1 if (cfg["rope"] or cfg["norm"] or world > 1) else 0)
         if world > 1:
             kernels += {"peer": 2, "nccl": 1}.get(transport, 0)
+            if transport == "peer" and not fp8 and not args.narrow:
+                kernels += int(ulysses.layer_cross(world) == "sm") + int(ulysses.layer_gate(world))
         if fp8:
-            kernels += 1 + (2 if world > 1 else 0)
+            kernels = 3 + (4 if world > 1 and transport == "peer" else 0)
         if args.narrow:  # key sums, shift, pack, 3 widens, attention, return pack, land widen
             kernels = 9 + (2 if cfg["rope"] or cfg["norm"] else 0) + (
                 4 if world > 1 and transport == "peer" else 0)
