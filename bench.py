@@ -845,7 +845,7 @@ def main() -> None:
             if transport == "peer" and not fp8 and not args.narrow:
                 kernels += int(ulysses.layer_cross(world) == "sm") + int(ulysses.layer_gate(world))
         if fp8:
-            kernels = 3 + (4 if world > 1 and transport == "peer" else 0)
+            kernels = 3 + ({"peer": 4, "nccl": 1}.get(transport, 0) if world > 1 else 0)
         if args.narrow:  # key sums, shift, pack, 3 widens, attention, return pack, land widen
             kernels = 9 + (2 if cfg["rope"] or cfg["norm"] else 0) + (
                 4 if world > 1 and transport == "peer" else 0)
